@@ -1,0 +1,176 @@
+/*
+ * polylora_b200 — C ABI of the B200 (sm_100a) batched multi-adapter LoRA path.
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA
+ * stream handle (cudaStream_t passed as void*), returns a PLORA_* status and
+ * never throws across the boundary.  No entry point allocates device memory:
+ * callers pass outputs and, where one is needed, a workspace sized by
+ * plora_workspace_size().  Work is enqueued on `stream`; nothing synchronises
+ * the host except plora_device_status().
+ *
+ * Layout conventions (all tensors contiguous, row-major):
+ *   x        (num_rows, max_seq, in_features)      activation rows
+ *   lora_a   (num_slots, in_features, max_rank)    per-slot LoRA A, rank-minor
+ *   lora_b   (num_slots, max_rank, out_features)   per-slot LoRA B
+ *   tmp      (num_rows, max_seq, max_rank)         shrink output / expand input
+ *   y        (num_rows, max_seq, out_features)     base output, updated in place
+ *   weight_indices (num_rows,) int64  slot of each row; slot 0 is "__base__"
+ *   seq_lens       (num_rows,) int32  valid tokens of each row (right padded)
+ *   lora_ranks     (num_slots,) int32 rank of each slot (0 = no-op)
+ *   scalings       (num_slots,) fp32  alpha / rank of each slot
+ * Token t = row * max_seq + m is active when m < min(seq_lens[row], max_seq)
+ * and lora_ranks[weight_indices[row]] > 0.
+ */
+#ifndef POLYLORA_B200_H_
+#define POLYLORA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define PLORA_DTYPE_F32 0
+#define PLORA_DTYPE_F16 1
+#define PLORA_DTYPE_BF16 2
+
+/* status codes */
+#define PLORA_OK 0
+#define PLORA_ERR_INVALID_ARGUMENT 1 /* shapes, pointers or sizes rejected on the host */
+#define PLORA_ERR_UNSUPPORTED 2      /* valid request this build does not handle     */
+#define PLORA_ERR_CUDA 3             /* a CUDA runtime call failed                   */
+#define PLORA_ERR_WORKSPACE 4        /* workspace missing or too small               */
+#define PLORA_ERR_DEVICE 5           /* a kernel raised the device status word       */
+
+/* device status bits (plora_device_status) */
+#define PLORA_DEV_WAIT_TIMEOUT 1 /* a bounded pipeline wait expired; kernel returned early */
+#define PLORA_DEV_SLOT_RANGE 2   /* a weight index outside [0, num_slots) was skipped      */
+#define PLORA_DEV_RANK_RANGE 4   /* a rank outside [0, max_rank] was clamped               */
+
+/* Library version string. */
+const char* plora_version(void);
+
+/* Human-readable text for a PLORA_* status code. */
+const char* plora_status_string(int status);
+
+/* Detail of the last failing call on this host thread ("" if none). */
+const char* plora_last_error(void);
+
+/* Reads (and with clear != 0, resets) the device status word of the current
+ * device.  Synchronises the device.  No counterpart in the reference: the
+ * reference's Triton kernels have no device-side error reporting. */
+int plora_device_status(int32_t* status_out, int32_t clear);
+
+/* Workspace bytes needed by plora_build_segments, plora_sgmv_a_fwd and
+ * plora_sgmv_b_fwd for a batch of num_rows x max_seq tokens over num_slots
+ * slots (segment scratch plus, for the *_fwd calls, the table itself).
+ * The workspace must be 256-byte aligned. */
+size_t plora_workspace_size(int64_t num_rows, int64_t max_seq, int32_t num_slots);
+
+/* ---------------------------------------------------------------------------
+ * Segment table: rows grouped by slot, built on the device.
+ * Replaces the host-synchronising schedule of the reference
+ * (src/polylora/sgmv.py:29-61 _build_flat_schedule and the n_eff gather at
+ * sgmv.py:304-309): the result stays on the device and needs no .item().
+ *   slot_start  (num_slots + 1,) int32: exclusive prefix of active tokens per
+ *               slot; slot_start[num_slots] is the active-token total.
+ *   token_index (num_rows * max_seq,) int32: active token ids (row*max_seq+m)
+ *               ordered by (slot, row, m); entries past the total are unused.
+ * A token is active when its slot's rank in `lora_ranks` is > 0.
+ * ------------------------------------------------------------------------- */
+int plora_build_segments(const int64_t* weight_indices, const int32_t* seq_lens,
+                         const int32_t* lora_ranks, int64_t num_rows, int64_t max_seq,
+                         int32_t num_slots, int32_t* slot_start, int32_t* token_index,
+                         void* workspace, size_t workspace_size, void* stream);
+
+/* Reference-compatible flat tile schedule: src/polylora/sgmv.py:29-61
+ * (_build_flat_schedule).  cum_tiles (num_rows+1,) and num_n_tiles (num_rows,)
+ * int32 are written on the device; the tile total is cum_tiles[num_rows]. */
+int plora_flat_schedule(const int32_t* seq_lens, const int32_t* n_eff, int64_t num_rows,
+                        int32_t block_m, int32_t block_n, int32_t* cum_tiles,
+                        int32_t* num_n_tiles, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * SGMV shrink (LoRA A, down-projection): src/polylora/sgmv.py:141-175
+ * sgmv_lora_a_fwd(x, weights, seq_lens, weight_indices, lora_ranks, stack_num)
+ *   tmp[t, n] = sum_k x[t, k] * lora_a[slot(t), k, n]  for n < min(rank*stack_num, max_rank)
+ *   tmp[t, n] = 0 for the remaining n of an active token; inactive tokens are
+ *   not written (the reference leaves them uninitialised).
+ * Builds the segment table in `workspace`, then runs the shrink kernel.
+ * ------------------------------------------------------------------------- */
+int plora_sgmv_a_fwd(const void* x, const void* lora_a, void* tmp, const int32_t* seq_lens,
+                     const int64_t* weight_indices, const int32_t* lora_ranks, int64_t num_rows,
+                     int64_t max_seq, int64_t in_features, int64_t max_rank, int32_t num_slots,
+                     int32_t stack_num, int32_t dtype, void* workspace, size_t workspace_size,
+                     void* stream);
+
+/* ---------------------------------------------------------------------------
+ * SGMV expand (LoRA B, up-projection) with fused scaling and add-back:
+ * src/polylora/sgmv.py:278-328
+ * sgmv_lora_b_fwd(x, weights, seq_lens, weight_indices, lora_ranks, scalings, base_output)
+ *   y[t, :] += scalings[slot] * sum_{k < min(rank, max_rank)} tmp[t, k] * lora_b[slot, k, :]
+ * in place on y (the reference's base_output; callers pass zeros where the
+ * reference would allocate them).  Rows of rank-0 slots and padding tokens are
+ * left bit-identical.
+ * ------------------------------------------------------------------------- */
+int plora_sgmv_b_fwd(const void* tmp, const void* lora_b, void* y, const int32_t* seq_lens,
+                     const int64_t* weight_indices, const int32_t* lora_ranks,
+                     const float* scalings, int64_t num_rows, int64_t max_seq, int64_t max_rank,
+                     int64_t out_features, int32_t num_slots, int32_t dtype, void* workspace,
+                     size_t workspace_size, void* stream);
+
+/* Shrink over a prebuilt segment table (plora_build_segments).  Same math as
+ * plora_sgmv_a_fwd; `lora_ranks` may hold ranks of a different module than
+ * the table was built with: tokens whose slot rank is 0 here are skipped. */
+int plora_sgmv_shrink(const void* x, const void* lora_a, void* tmp, const int32_t* lora_ranks,
+                      const int32_t* slot_start, const int32_t* token_index, int64_t num_tokens,
+                      int64_t in_features, int64_t max_rank, int32_t num_slots, int32_t stack_num,
+                      int32_t dtype, void* stream);
+
+/* Expand over a prebuilt segment table.  Same math as plora_sgmv_b_fwd. */
+int plora_sgmv_expand(const void* tmp, const void* lora_b, void* y, const int32_t* lora_ranks,
+                      const float* scalings, const int32_t* slot_start, const int32_t* token_index,
+                      int64_t num_tokens, int64_t max_rank, int64_t out_features,
+                      int32_t num_slots, int32_t dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * GPU slot refill: src/polylora/cache.py:97-150 (_allocate_or_evict zeroing +
+ * _load_adapter_into_slot copies).  One pinned host->device copy of a packed
+ * adapter image into `staging`, then one kernel that writes every module's
+ * slot (A and B zero-padded to max_rank, rank, scale; absent modules become
+ * rank 0 / scale 0).  Enqueued on `stream` (callers use a side stream and
+ * order it against compute with events).
+ *   modules      device array of plora_slot_module (see below)
+ *   host_image   pinned packed adapter image (layout below), image_bytes long
+ *   staging      device buffer of at least image_bytes
+ * Image layout: num_modules records of plora_slot_record, then the data
+ * blocks they point at (byte offsets from the image start):
+ *   A block (in_features x rank) row-major, B block (rank x out_features).
+ * ------------------------------------------------------------------------- */
+typedef struct plora_slot_module {
+  void* lora_a;     /* (num_slots, in_features, max_rank) */
+  void* lora_b;     /* (num_slots, max_rank, out_features) */
+  int32_t* ranks;   /* (num_slots,) */
+  float* scales;    /* (num_slots,) */
+  int64_t in_features;
+  int64_t out_features;
+} plora_slot_module;
+
+typedef struct plora_slot_record {
+  int64_t a_offset; /* byte offset of the A block in the image */
+  int64_t b_offset; /* byte offset of the B block in the image */
+  int32_t rank;     /* 0 = module absent from this adapter */
+  float scale;      /* alpha / rank */
+} plora_slot_record;
+
+int plora_slot_fill(const plora_slot_module* modules, int32_t num_modules, int32_t slot,
+                    int32_t num_slots, int64_t max_rank, int32_t dtype, const void* host_image,
+                    size_t image_bytes, void* staging, size_t staging_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POLYLORA_B200_H_ */

@@ -1,0 +1,186 @@
+"""ctypes binding of libpolylora_b200.so (declared in include/polylora_b200.h).
+
+The library is the only compute path of this package: when it is missing or
+fails to load, every kernel wrapper raises :class:`NativeLibraryError`; there
+is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+from . import build as _build
+
+DTYPE_F32 = 0
+DTYPE_F16 = 1
+DTYPE_BF16 = 2
+
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_UNSUPPORTED = 2
+ERR_CUDA = 3
+ERR_WORKSPACE = 4
+ERR_DEVICE = 5
+
+DEV_WAIT_TIMEOUT = 1
+DEV_SLOT_RANGE = 2
+DEV_RANK_RANGE = 4
+
+_c_void_p = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_i64 = ctypes.c_int64
+_size = ctypes.c_size_t
+
+
+class NativeLibraryError(RuntimeError):
+    """The CUDA library could not be loaded (no silent fallback exists)."""
+
+
+class PloraError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, func: str, status: int, detail: str) -> None:
+        super().__init__(f"{func} failed with status {status}: {detail}")
+        self.func = func
+        self.status = status
+        self.detail = detail
+
+
+class SlotModule(ctypes.Structure):
+    """plora_slot_module."""
+
+    _fields_ = [
+        ("lora_a", _c_void_p),
+        ("lora_b", _c_void_p),
+        ("ranks", _c_void_p),
+        ("scales", _c_void_p),
+        ("in_features", _i64),
+        ("out_features", _i64),
+    ]
+
+
+class SlotRecord(ctypes.Structure):
+    """plora_slot_record."""
+
+    _fields_ = [
+        ("a_offset", _i64),
+        ("b_offset", _i64),
+        ("rank", _i32),
+        ("scale", ctypes.c_float),
+    ]
+
+
+# name -> (restype, argtypes)
+_SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "plora_version": (ctypes.c_char_p, []),
+    "plora_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "plora_last_error": (ctypes.c_char_p, []),
+    "plora_device_status": (ctypes.c_int, [ctypes.POINTER(_i32), _i32]),
+    "plora_workspace_size": (_size, [_i64, _i64, _i32]),
+    "plora_build_segments": (
+        ctypes.c_int,
+        [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i32, _c_void_p, _c_void_p, _c_void_p, _size, _c_void_p],
+    ),
+    "plora_flat_schedule": (
+        ctypes.c_int,
+        [_c_void_p, _c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p, _c_void_p],
+    ),
+    "plora_sgmv_a_fwd": (
+        ctypes.c_int,
+        [
+            _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+            _i64, _i64, _i64, _i64, _i32, _i32, _i32, _c_void_p, _size, _c_void_p,
+        ],
+    ),
+    "plora_sgmv_b_fwd": (
+        ctypes.c_int,
+        [
+            _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+            _i64, _i64, _i64, _i64, _i32, _i32, _c_void_p, _size, _c_void_p,
+        ],
+    ),
+    "plora_sgmv_shrink": (
+        ctypes.c_int,
+        [
+            _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+            _i64, _i64, _i64, _i32, _i32, _i32, _c_void_p,
+        ],
+    ),
+    "plora_sgmv_expand": (
+        ctypes.c_int,
+        [
+            _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+            _i64, _i64, _i64, _i32, _i32, _c_void_p,
+        ],
+    ),
+    "plora_slot_fill": (
+        ctypes.c_int,
+        [_c_void_p, _i32, _i32, _i32, _i64, _i32, _c_void_p, _size, _c_void_p, _size, _c_void_p],
+    ),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def library_path() -> Path:
+    return _build.LIB_PATH
+
+
+def load(build_if_missing: bool = True) -> ctypes.CDLL:
+    """Loads (building first if absent and nvcc exists) the C-ABI library."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = library_path()
+        if not path.exists() and build_if_missing:
+            try:
+                _build.build()
+            except Exception as exc:  # pragma: no cover - depends on toolchain
+                raise NativeLibraryError(f"cannot build {path.name}: {exc}") from exc
+        if not path.exists():
+            raise NativeLibraryError(f"{path} is missing; run python -m polylora_b200.build")
+        try:
+            lib = ctypes.CDLL(str(path))
+        except OSError as exc:
+            raise NativeLibraryError(f"cannot load {path}: {exc}") from exc
+        for name, (restype, argtypes) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    return (load().plora_last_error() or b"").decode()
+
+
+def check(func: str, status: int) -> None:
+    if status != OK:
+        raise PloraError(func, status, last_error())
+
+
+def call(func: str, *args: object) -> None:
+    """Calls a status-returning entry point and raises on failure."""
+    check(func, getattr(load(), func)(*args))
+
+
+def device_status(clear: bool = True) -> int:
+    """Synchronises the current device and returns its status word."""
+    out = _i32(0)
+    load().plora_device_status(ctypes.byref(out), 1 if clear else 0)
+    return int(out.value)
+
+
+def workspace_size(num_rows: int, max_seq: int, num_slots: int) -> int:
+    return int(load().plora_workspace_size(num_rows, max_seq, num_slots))
+
+
+def version() -> str:
+    return load().plora_version().decode()

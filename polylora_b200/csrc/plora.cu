@@ -1,0 +1,473 @@
+// C ABI of libpolylora_b200.so: argument checks, TMA tensor maps, launch
+// configuration and dispatch between the tensor-core (bf16/fp16) and CUDA-core
+// kernels.  One translation unit so the device status word is shared.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "segments.cuh"
+#include "sgmv_simt.cuh"
+#include "sgmv_tc.cuh"
+
+using namespace plora;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(PLORA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define PLORA_CUDA(call, what)             \
+  do {                                     \
+    cudaError_t _e = (call);               \
+    if (_e != cudaSuccess) return cuda_fail(_e, what); \
+  } while (0)
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  int sm_count = 0;
+  bool attrs_set = false;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  PLORA_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(PLORA_ERR_UNSUPPORTED, "device ordinal %d", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.attrs_set) {
+    PLORA_CUDA(cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev),
+               "cudaDeviceGetAttribute");
+    int major = 0, minor = 0;
+    PLORA_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev), "cc");
+    PLORA_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev), "cc");
+    if (major != 10 || minor != 0)
+      return fail(PLORA_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", dev,
+                  major, minor);
+#define SET_SMEM(kern, bytes) \
+  PLORA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), #kern)
+    SET_SMEM((sgmv_shrink_tc_kernel<16, true>), ShrinkCfg<16>::kSmemBytes);
+    SET_SMEM((sgmv_shrink_tc_kernel<32, true>), ShrinkCfg<32>::kSmemBytes);
+    SET_SMEM((sgmv_shrink_tc_kernel<64, true>), ShrinkCfg<64>::kSmemBytes);
+    SET_SMEM((sgmv_shrink_tc_kernel<16, false>), ShrinkCfg<16>::kSmemBytes);
+    SET_SMEM((sgmv_shrink_tc_kernel<32, false>), ShrinkCfg<32>::kSmemBytes);
+    SET_SMEM((sgmv_shrink_tc_kernel<64, false>), ShrinkCfg<64>::kSmemBytes);
+    SET_SMEM((sgmv_expand_tc_kernel<16, true>), ExpandCfg<16>::kSmemBytes);
+    SET_SMEM((sgmv_expand_tc_kernel<32, true>), ExpandCfg<32>::kSmemBytes);
+    SET_SMEM((sgmv_expand_tc_kernel<64, true>), ExpandCfg<64>::kSmemBytes);
+    SET_SMEM((sgmv_expand_tc_kernel<16, false>), ExpandCfg<16>::kSmemBytes);
+    SET_SMEM((sgmv_expand_tc_kernel<32, false>), ExpandCfg<32>::kSmemBytes);
+    SET_SMEM((sgmv_expand_tc_kernel<64, false>), ExpandCfg<64>::kSmemBytes);
+#undef SET_SMEM
+    d.attrs_set = true;
+  }
+  *out = &d;
+  return PLORA_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 3-D tiled map over a contiguous (d2, d1, d0) 16-bit tensor.
+int make_map_3d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, uint64_t d1,
+                uint64_t d2, uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
+  const cuuint32_t box[3] = {b0, b1, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt = dtype == PLORA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return PLORA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+size_t elem_size(int dtype) { return dtype == PLORA_DTYPE_F32 ? 4 : 2; }
+
+bool valid_dtype(int dtype) {
+  return dtype == PLORA_DTYPE_F32 || dtype == PLORA_DTYPE_F16 || dtype == PLORA_DTYPE_BF16;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return PLORA_OK;
+}
+
+// Workspace of the *_fwd entry points: segment scratch, slot_start, token_index.
+struct FwdWorkspace {
+  SegWorkspace seg;
+  int32_t* slot_start;
+  int32_t* token_index;
+};
+
+size_t fwd_workspace_bytes(int64_t num_rows, int64_t max_seq, int32_t num_slots) {
+  return seg_workspace_bytes(num_rows, num_slots) + align256((size_t)(num_slots + 1) * 4) +
+         align256((size_t)(num_rows * max_seq) * 4);
+}
+
+int build_segments(const int64_t* wi, const int32_t* seq_lens, const int32_t* ranks,
+                   int64_t num_rows, int64_t max_seq, int32_t num_slots, int32_t* slot_start,
+                   int32_t* token_index, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  if (num_slots < 1 || num_slots > kSegMaxSlots)
+    return fail(PLORA_ERR_UNSUPPORTED, "num_slots %d outside [1, %d]", num_slots, kSegMaxSlots);
+  if (num_rows < 0 || max_seq < 0)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "negative num_rows/max_seq");
+  if (num_rows * max_seq > (int64_t)INT32_MAX)
+    return fail(PLORA_ERR_UNSUPPORTED, "num_rows*max_seq exceeds int32 token ids");
+  if (!slot_start) return fail(PLORA_ERR_INVALID_ARGUMENT, "slot_start is null");
+  if (num_rows == 0 || max_seq == 0) {
+    PLORA_CUDA(cudaMemsetAsync(slot_start, 0, (size_t)(num_slots + 1) * 4, stream), "memset");
+    return PLORA_OK;
+  }
+  if (!wi || !seq_lens || !ranks || !token_index)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "null segment input");
+  const size_t need = seg_workspace_bytes(num_rows, num_slots);
+  if (!ws || ws_bytes < need)
+    return fail(PLORA_ERR_WORKSPACE, "segment workspace %zu < %zu bytes", ws_bytes, need);
+  SegWorkspace w = seg_workspace_carve(ws, num_rows, num_slots);
+  const int64_t blocks = (num_rows + kSegRowsPerBlock - 1) / kSegRowsPerBlock;
+  if (blocks > INT32_MAX) return fail(PLORA_ERR_UNSUPPORTED, "too many rows");
+  seg_count_kernel<<<(unsigned)blocks, kSegRowsPerBlock, (size_t)num_slots * 4, stream>>>(
+      wi, seq_lens, ranks, num_rows, max_seq, num_slots, w);
+  int st = check_launch("seg_count_kernel");
+  if (st) return st;
+  seg_scan_kernel<<<1, 1024, 0, stream>>>((int32_t)blocks, num_slots, w, slot_start);
+  if ((st = check_launch("seg_scan_kernel"))) return st;
+  seg_place_kernel<<<(unsigned)((num_rows + 7) / 8), 256, 0, stream>>>(
+      num_rows, max_seq, seq_lens, num_slots, w, token_index);
+  return check_launch("seg_place_kernel");
+}
+
+// Tensor-core path eligibility (16-bit types, rank tile 16/32/64, 16-byte rows).
+bool tc_rank_ok(int64_t R) { return R == 16 || R == 32 || R == 64; }
+
+int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, SegTable seg,
+                int64_t K, int64_t R, int32_t stack_num, int32_t dtype, cudaStream_t stream) {
+  DeviceInfo* di = nullptr;
+  int st = device_info(&di);
+  if (st) return st;
+  ShrinkArgs args;
+  args.x = static_cast<const uint8_t*>(x);
+  args.a = static_cast<const uint8_t*>(a);
+  args.tmp = static_cast<uint8_t*>(tmp);
+  args.ranks = ranks;
+  args.seg = seg;
+  args.K = (int32_t)K;
+  args.R = (int32_t)R;
+  args.stack_num = stack_num;
+  const bool tc = dtype != PLORA_DTYPE_F32 && tc_rank_ok(R) && K % 8 == 0 && aligned16(x) &&
+                  aligned16(a) && aligned16(tmp);
+  if (tc) {
+    CUtensorMap map;
+    const CUtensorMapSwizzle swz = R == 16   ? CU_TENSOR_MAP_SWIZZLE_32B
+                                   : R == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                             : CU_TENSOR_MAP_SWIZZLE_128B;
+    if ((st = make_map_3d(&map, a, dtype, (uint64_t)R, (uint64_t)K, (uint64_t)seg.num_slots,
+                          (uint32_t)R, kShrinkKC, swz)))
+      return st;
+    const dim3 grid(di->sm_count), block(kShrinkThreads);
+    const bool bf = dtype == PLORA_DTYPE_BF16;
+#define LAUNCH_SHRINK(RPV)                                                               \
+  if (bf)                                                                                \
+    sgmv_shrink_tc_kernel<RPV, true><<<grid, block, ShrinkCfg<RPV>::kSmemBytes, stream>>>( \
+        map, args);                                                                      \
+  else                                                                                   \
+    sgmv_shrink_tc_kernel<RPV, false><<<grid, block, ShrinkCfg<RPV>::kSmemBytes, stream>>>( \
+        map, args);
+    if (R == 16) {
+      LAUNCH_SHRINK(16)
+    } else if (R == 32) {
+      LAUNCH_SHRINK(32)
+    } else {
+      LAUNCH_SHRINK(64)
+    }
+#undef LAUNCH_SHRINK
+    return check_launch("sgmv_shrink_tc_kernel");
+  }
+  if (R > kSimtMaxRank) return fail(PLORA_ERR_UNSUPPORTED, "max_rank %lld > %d", (long long)R, kSimtMaxRank);
+  const dim3 grid(di->sm_count * 8), block(kSimtThreads);
+  if (dtype == PLORA_DTYPE_F32)
+    sgmv_shrink_simt_kernel<float><<<grid, block, 0, stream>>>(args, seg.num_slots);
+  else if (dtype == PLORA_DTYPE_BF16)
+    sgmv_shrink_simt_kernel<__nv_bfloat16><<<grid, block, 0, stream>>>(args, seg.num_slots);
+  else
+    sgmv_shrink_simt_kernel<__half><<<grid, block, 0, stream>>>(args, seg.num_slots);
+  return check_launch("sgmv_shrink_simt_kernel");
+}
+
+int expand_impl(const void* tmp, const void* b, void* y, const int32_t* ranks, const float* scales,
+                SegTable seg, int64_t R, int64_t N, int32_t dtype, cudaStream_t stream) {
+  DeviceInfo* di = nullptr;
+  int st = device_info(&di);
+  if (st) return st;
+  ExpandArgs args;
+  args.tmp = static_cast<const uint8_t*>(tmp);
+  args.b = static_cast<const uint8_t*>(b);
+  args.y = static_cast<uint8_t*>(y);
+  args.ranks = ranks;
+  args.scales = scales;
+  args.seg = seg;
+  args.R = (int32_t)R;
+  args.N = (int32_t)N;
+  const bool tc = dtype != PLORA_DTYPE_F32 && tc_rank_ok(R) && N % 8 == 0 && aligned16(tmp) &&
+                  aligned16(b) && aligned16(y);
+  if (tc) {
+    CUtensorMap map;
+    if ((st = make_map_3d(&map, b, dtype, (uint64_t)N, (uint64_t)R, (uint64_t)seg.num_slots, 64,
+                          (uint32_t)R, CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+    const dim3 grid(di->sm_count), block(kExpandThreads);
+    const bool bf = dtype == PLORA_DTYPE_BF16;
+#define LAUNCH_EXPAND(RPV)                                                               \
+  if (bf)                                                                                \
+    sgmv_expand_tc_kernel<RPV, true><<<grid, block, ExpandCfg<RPV>::kSmemBytes, stream>>>( \
+        map, args);                                                                      \
+  else                                                                                   \
+    sgmv_expand_tc_kernel<RPV, false><<<grid, block, ExpandCfg<RPV>::kSmemBytes, stream>>>( \
+        map, args);
+    if (R == 16) {
+      LAUNCH_EXPAND(16)
+    } else if (R == 32) {
+      LAUNCH_EXPAND(32)
+    } else {
+      LAUNCH_EXPAND(64)
+    }
+#undef LAUNCH_EXPAND
+    return check_launch("sgmv_expand_tc_kernel");
+  }
+  if (R > kSimtMaxRank) return fail(PLORA_ERR_UNSUPPORTED, "max_rank %lld > %d", (long long)R, kSimtMaxRank);
+  const dim3 grid(di->sm_count * 8), block(kSimtThreads);
+  if (dtype == PLORA_DTYPE_F32)
+    sgmv_expand_simt_kernel<float><<<grid, block, 0, stream>>>(args, seg.num_slots);
+  else if (dtype == PLORA_DTYPE_BF16)
+    sgmv_expand_simt_kernel<__nv_bfloat16><<<grid, block, 0, stream>>>(args, seg.num_slots);
+  else
+    sgmv_expand_simt_kernel<__half><<<grid, block, 0, stream>>>(args, seg.num_slots);
+  return check_launch("sgmv_expand_simt_kernel");
+}
+
+int check_common(int32_t dtype, int32_t num_slots, int64_t max_rank) {
+  if (!valid_dtype(dtype)) return fail(PLORA_ERR_INVALID_ARGUMENT, "unknown dtype %d", dtype);
+  if (num_slots < 1 || num_slots > kSegMaxSlots)
+    return fail(PLORA_ERR_UNSUPPORTED, "num_slots %d outside [1, %d]", num_slots, kSegMaxSlots);
+  if (max_rank < 1) return fail(PLORA_ERR_INVALID_ARGUMENT, "max_rank must be >= 1");
+  return PLORA_OK;
+}
+
+FwdWorkspace carve_fwd(void* ws, int64_t num_rows, int64_t max_seq, int32_t num_slots) {
+  FwdWorkspace f;
+  char* p = static_cast<char*>(ws);
+  f.seg = seg_workspace_carve(p, num_rows, num_slots);
+  p += seg_workspace_bytes(num_rows, num_slots);
+  f.slot_start = reinterpret_cast<int32_t*>(p);
+  p += align256((size_t)(num_slots + 1) * 4);
+  f.token_index = reinterpret_cast<int32_t*>(p);
+  return f;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* plora_version(void) { return "polylora_b200 0.1.0 (sm_100a)"; }
+
+const char* plora_status_string(int status) {
+  switch (status) {
+    case PLORA_OK: return "ok";
+    case PLORA_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case PLORA_ERR_UNSUPPORTED: return "unsupported";
+    case PLORA_ERR_CUDA: return "CUDA error";
+    case PLORA_ERR_WORKSPACE: return "workspace too small";
+    case PLORA_ERR_DEVICE: return "device status raised";
+    default: return "unknown status";
+  }
+}
+
+const char* plora_last_error(void) { return g_last_error.c_str(); }
+
+int plora_device_status(int32_t* status_out, int32_t clear) {
+  int v = 0;
+  PLORA_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  PLORA_CUDA(cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)), "read device status");
+  if (clear) {
+    const int zero = 0;
+    PLORA_CUDA(cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)), "clear device status");
+  }
+  if (status_out) *status_out = v;
+  return v ? fail(PLORA_ERR_DEVICE, "device status 0x%x", v) : PLORA_OK;
+}
+
+size_t plora_workspace_size(int64_t num_rows, int64_t max_seq, int32_t num_slots) {
+  if (num_rows < 0 || max_seq < 0 || num_slots < 1) return 0;
+  return fwd_workspace_bytes(num_rows, max_seq, num_slots);
+}
+
+int plora_build_segments(const int64_t* weight_indices, const int32_t* seq_lens,
+                         const int32_t* lora_ranks, int64_t num_rows, int64_t max_seq,
+                         int32_t num_slots, int32_t* slot_start, int32_t* token_index,
+                         void* workspace, size_t workspace_size, void* stream) {
+  g_last_error.clear();
+  return build_segments(weight_indices, seq_lens, lora_ranks, num_rows, max_seq, num_slots,
+                        slot_start, token_index, workspace, workspace_size,
+                        static_cast<cudaStream_t>(stream));
+}
+
+int plora_flat_schedule(const int32_t* seq_lens, const int32_t* n_eff, int64_t num_rows,
+                        int32_t block_m, int32_t block_n, int32_t* cum_tiles,
+                        int32_t* num_n_tiles, void* stream) {
+  g_last_error.clear();
+  if (num_rows < 0 || block_m < 1 || block_n < 1 || !cum_tiles)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "flat schedule arguments");
+  if (num_rows > 0 && (!seq_lens || !n_eff || !num_n_tiles))
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "null flat schedule input");
+  flat_schedule_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
+      seq_lens, n_eff, num_rows, block_m, block_n, cum_tiles, num_n_tiles);
+  return check_launch("flat_schedule_kernel");
+}
+
+int plora_sgmv_shrink(const void* x, const void* lora_a, void* tmp, const int32_t* lora_ranks,
+                      const int32_t* slot_start, const int32_t* token_index, int64_t num_tokens,
+                      int64_t in_features, int64_t max_rank, int32_t num_slots, int32_t stack_num,
+                      int32_t dtype, void* stream) {
+  g_last_error.clear();
+  int st = check_common(dtype, num_slots, max_rank);
+  if (st) return st;
+  if (in_features < 1 || in_features > INT32_MAX || stack_num < 1)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "in_features/stack_num");
+  if (num_tokens == 0) return PLORA_OK;
+  if (!x || !lora_a || !tmp || !lora_ranks || !slot_start || !token_index)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "null pointer");
+  SegTable seg{slot_start, token_index, num_slots};
+  return shrink_impl(x, lora_a, tmp, lora_ranks, seg, in_features, max_rank, stack_num, dtype,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int plora_sgmv_expand(const void* tmp, const void* lora_b, void* y, const int32_t* lora_ranks,
+                      const float* scalings, const int32_t* slot_start, const int32_t* token_index,
+                      int64_t num_tokens, int64_t max_rank, int64_t out_features,
+                      int32_t num_slots, int32_t dtype, void* stream) {
+  g_last_error.clear();
+  int st = check_common(dtype, num_slots, max_rank);
+  if (st) return st;
+  if (out_features < 1 || out_features > INT32_MAX)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "out_features");
+  if (num_tokens == 0) return PLORA_OK;
+  if (!tmp || !lora_b || !y || !lora_ranks || !scalings || !slot_start || !token_index)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "null pointer");
+  SegTable seg{slot_start, token_index, num_slots};
+  return expand_impl(tmp, lora_b, y, lora_ranks, scalings, seg, max_rank, out_features, dtype,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int plora_sgmv_a_fwd(const void* x, const void* lora_a, void* tmp, const int32_t* seq_lens,
+                     const int64_t* weight_indices, const int32_t* lora_ranks, int64_t num_rows,
+                     int64_t max_seq, int64_t in_features, int64_t max_rank, int32_t num_slots,
+                     int32_t stack_num, int32_t dtype, void* workspace, size_t workspace_size,
+                     void* stream) {
+  g_last_error.clear();
+  int st = check_common(dtype, num_slots, max_rank);
+  if (st) return st;
+  if (num_rows == 0 || max_seq == 0) return PLORA_OK;  // sgmv.py:159-160
+  const size_t need = fwd_workspace_bytes(num_rows, max_seq, num_slots);
+  if (!workspace || workspace_size < need)
+    return fail(PLORA_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_size, need);
+  FwdWorkspace w = carve_fwd(workspace, num_rows, max_seq, num_slots);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((st = build_segments(weight_indices, seq_lens, lora_ranks, num_rows, max_seq, num_slots,
+                           w.slot_start, w.token_index, workspace, workspace_size, s)))
+    return st;
+  return plora_sgmv_shrink(x, lora_a, tmp, lora_ranks, w.slot_start, w.token_index,
+                           num_rows * max_seq, in_features, max_rank, num_slots, stack_num, dtype,
+                           stream);
+}
+
+int plora_sgmv_b_fwd(const void* tmp, const void* lora_b, void* y, const int32_t* seq_lens,
+                     const int64_t* weight_indices, const int32_t* lora_ranks,
+                     const float* scalings, int64_t num_rows, int64_t max_seq, int64_t max_rank,
+                     int64_t out_features, int32_t num_slots, int32_t dtype, void* workspace,
+                     size_t workspace_size, void* stream) {
+  g_last_error.clear();
+  int st = check_common(dtype, num_slots, max_rank);
+  if (st) return st;
+  if (num_rows == 0 || max_seq == 0) return PLORA_OK;  // sgmv.py:314-315
+  const size_t need = fwd_workspace_bytes(num_rows, max_seq, num_slots);
+  if (!workspace || workspace_size < need)
+    return fail(PLORA_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_size, need);
+  FwdWorkspace w = carve_fwd(workspace, num_rows, max_seq, num_slots);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((st = build_segments(weight_indices, seq_lens, lora_ranks, num_rows, max_seq, num_slots,
+                           w.slot_start, w.token_index, workspace, workspace_size, s)))
+    return st;
+  return plora_sgmv_expand(tmp, lora_b, y, lora_ranks, scalings, w.slot_start, w.token_index,
+                           num_rows * max_seq, max_rank, out_features, num_slots, dtype, stream);
+}
+
+int plora_slot_fill(const plora_slot_module* modules, int32_t num_modules, int32_t slot,
+                    int32_t num_slots, int64_t max_rank, int32_t dtype, const void* host_image,
+                    size_t image_bytes, void* staging, size_t staging_bytes, void* stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return fail(PLORA_ERR_INVALID_ARGUMENT, "unknown dtype %d", dtype);
+  if (num_modules < 0 || slot < 0 || slot >= num_slots || max_rank < 1)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "slot %d of %d, %d modules", slot, num_slots,
+                num_modules);
+  if (num_modules == 0) return PLORA_OK;
+  if (!modules || !host_image || !staging)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "null pointer");
+  if (image_bytes < (size_t)num_modules * sizeof(plora_slot_record))
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "image smaller than its records");
+  if (staging_bytes < image_bytes)
+    return fail(PLORA_ERR_WORKSPACE, "staging %zu < image %zu bytes", staging_bytes, image_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  PLORA_CUDA(cudaMemcpyAsync(staging, host_image, image_bytes, cudaMemcpyHostToDevice, s),
+             "slot image copy");
+  const dim3 grid(64, (unsigned)num_modules), block(256);
+  const uint8_t* img = static_cast<const uint8_t*>(staging);
+  if (elem_size(dtype) == 4)
+    slot_fill_kernel<float><<<grid, block, 0, s>>>(modules, num_modules, slot, max_rank, img);
+  else if (dtype == PLORA_DTYPE_BF16)
+    slot_fill_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(modules, num_modules, slot, max_rank, img);
+  else
+    slot_fill_kernel<__half><<<grid, block, 0, s>>>(modules, num_modules, slot, max_rank, img);
+  return check_launch("slot_fill_kernel");
+}
+
+}  // extern "C"

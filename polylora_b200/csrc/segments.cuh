@@ -1,0 +1,233 @@
+// Device-side segment construction: groups the active tokens of a batch by
+// slot with a stable (slot, row, position) order, and the reference-compatible
+// flat tile schedule.  Integer work only; results are bit-exact and
+// deterministic (no atomics decide an order).
+//
+// Replaces the host-synchronising schedule construction of the reference,
+// src/polylora/sgmv.py:29-61 (_build_flat_schedule) and sgmv.py:304-309, and
+// the per-row slot lookups of layers.py:124-130.
+#pragma once
+
+#include "common.cuh"
+
+namespace plora {
+
+constexpr int kSegRowsPerBlock = 256;  // rows counted per block (8 warps)
+constexpr int kSegMaxSlots = 4096;     // slot-count limit of the segment kernels
+
+// Workspace layout (bytes, each part 256-aligned):
+//   partial[num_blocks][num_slots] int32   per-block per-slot token counts,
+//                                          rewritten in place to global bases
+//   row_off[num_rows]              int32   token offset of a row within its block+slot
+//   row_info[num_rows]             int32   slot (>= 0) or -1 when inactive
+__host__ __device__ inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+struct SegWorkspace {
+  int32_t* partial;
+  int32_t* row_off;
+  int32_t* row_info;
+};
+
+__host__ inline size_t seg_workspace_bytes(int64_t num_rows, int32_t num_slots) {
+  const int64_t blocks = (num_rows + kSegRowsPerBlock - 1) / kSegRowsPerBlock;
+  return align256((size_t)blocks * (size_t)num_slots * 4) + 2 * align256((size_t)num_rows * 4);
+}
+
+__host__ inline SegWorkspace seg_workspace_carve(void* ws, int64_t num_rows, int32_t num_slots) {
+  const int64_t blocks = (num_rows + kSegRowsPerBlock - 1) / kSegRowsPerBlock;
+  char* p = static_cast<char*>(ws);
+  SegWorkspace w;
+  w.partial = reinterpret_cast<int32_t*>(p);
+  p += align256((size_t)blocks * (size_t)num_slots * 4);
+  w.row_off = reinterpret_cast<int32_t*>(p);
+  p += align256((size_t)num_rows * 4);
+  w.row_info = reinterpret_cast<int32_t*>(p);
+  return w;
+}
+
+// Pass 1: per block of 256 rows, the token count of every slot and, for each
+// active row, the offset of its tokens among the block's rows of that slot in
+// row order.  Warps take turns (8 steps); inside a warp the same-slot prefix
+// comes from __match_any_sync groups and a shuffle scan.
+__global__ void __launch_bounds__(kSegRowsPerBlock) seg_count_kernel(
+    const int64_t* __restrict__ weight_indices, const int32_t* __restrict__ seq_lens,
+    const int32_t* __restrict__ lora_ranks, int64_t num_rows, int64_t max_seq, int32_t num_slots,
+    SegWorkspace ws) {
+  extern __shared__ int32_t cnt[];  // [num_slots]
+  for (int s = threadIdx.x; s < num_slots; s += blockDim.x) cnt[s] = 0;
+
+  const int64_t row = (int64_t)blockIdx.x * kSegRowsPerBlock + threadIdx.x;
+  int key = -1;
+  int len = 0;
+  if (row < num_rows) {
+    const int64_t slot = weight_indices[row];
+    if (slot < 0 || slot >= num_slots) {
+      raise_status(PLORA_DEV_SLOT_RANGE);
+    } else {
+      const int32_t rank = lora_ranks[slot];
+      int64_t l = seq_lens[row];
+      l = l < 0 ? 0 : (l > max_seq ? max_seq : l);
+      if (rank > 0 && l > 0) {
+        key = (int)slot;
+        len = (int)l;
+      }
+    }
+  }
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const unsigned peers = __match_any_sync(0xffffffffu, key);
+  // Exclusive prefix of len over lower lanes of the same group.
+  int prefix = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int lj = __shfl_sync(0xffffffffu, len, j);
+    if (j < lane && ((peers >> j) & 1u)) prefix += lj;
+  }
+  const bool group_last = (31 - __clz(peers)) == lane;
+
+  for (int w = 0; w < kSegRowsPerBlock / 32; ++w) {
+    if (warp == w && key >= 0) {
+      const int base = cnt[key];
+      if (row < num_rows) ws.row_off[row] = base + prefix;
+      __syncwarp(peers);
+      if (group_last) cnt[key] = base + prefix + len;
+    }
+    __syncthreads();
+  }
+  if (row < num_rows) ws.row_info[row] = key;
+  int32_t* out = ws.partial + (int64_t)blockIdx.x * num_slots;
+  for (int s = threadIdx.x; s < num_slots; s += blockDim.x) out[s] = cnt[s];
+}
+
+// Pass 2 (one block): slot_start = exclusive scan over slots of the totals,
+// and partial[b][s] rewritten to the global first position of block b's
+// tokens of slot s.
+__global__ void __launch_bounds__(1024) seg_scan_kernel(int32_t num_blocks, int32_t num_slots,
+                                                         SegWorkspace ws,
+                                                         int32_t* __restrict__ slot_start) {
+  __shared__ int32_t warp_sums[32];
+  __shared__ int32_t carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  for (int s0 = 0; s0 < num_slots; s0 += blockDim.x) {
+    const int s = s0 + threadIdx.x;
+    int total = 0;
+    if (s < num_slots) {
+      for (int b = 0; b < num_blocks; ++b) total += ws.partial[(int64_t)b * num_slots + s];
+    }
+    // block-wide exclusive scan of total
+    int incl = total;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += v;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int ws_v = (lane < (int)(blockDim.x >> 5)) ? warp_sums[lane] : 0;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, ws_v, d);
+        if (lane >= d) ws_v += v;
+      }
+      warp_sums[lane] = ws_v;  // inclusive over warps
+    }
+    __syncthreads();
+    const int excl = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + incl - total;
+    if (s < num_slots) {
+      slot_start[s] = excl;
+      int run = excl;
+      for (int b = 0; b < num_blocks; ++b) {
+        int32_t* cell = ws.partial + (int64_t)b * num_slots + s;
+        const int c = *cell;
+        *cell = run;
+        run += c;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = excl + total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) slot_start[num_slots] = carry;
+}
+
+// Pass 3: one warp per row writes the row's token ids at its final position.
+__global__ void __launch_bounds__(256) seg_place_kernel(int64_t num_rows, int64_t max_seq,
+                                                         const int32_t* __restrict__ seq_lens,
+                                                         int32_t num_slots, SegWorkspace ws,
+                                                         int32_t* __restrict__ token_index) {
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= num_rows) return;
+  const int key = ws.row_info[row];
+  if (key < 0) return;
+  int64_t l = seq_lens[row];
+  l = l < 0 ? 0 : (l > max_seq ? max_seq : l);
+  const int64_t blk = row / kSegRowsPerBlock;
+  const int64_t dst = (int64_t)ws.partial[blk * num_slots + key] + ws.row_off[row];
+  const int64_t tok0 = row * max_seq;
+  for (int64_t m = lane; m < l; m += 32) token_index[dst + m] = (int32_t)(tok0 + m);
+}
+
+// Flat tile schedule of the reference (sgmv.py:29-61), one block with carry:
+//   num_n_tiles[b] = cdiv(n_eff[b], block_n)
+//   tiles[b]       = (seq_len == 0 || n_eff == 0) ? 0 : cdiv(seq_len, block_m) * num_n_tiles[b]
+//   cum_tiles      = [0, cumsum(tiles)]
+__global__ void __launch_bounds__(1024) flat_schedule_kernel(const int32_t* __restrict__ seq_lens,
+                                                              const int32_t* __restrict__ n_eff,
+                                                              int64_t num_rows, int32_t block_m,
+                                                              int32_t block_n,
+                                                              int32_t* __restrict__ cum_tiles,
+                                                              int32_t* __restrict__ num_n_tiles) {
+  __shared__ int32_t warp_sums[32];
+  __shared__ int32_t carry;
+  if (threadIdx.x == 0) {
+    carry = 0;
+    cum_tiles[0] = 0;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  for (int64_t b0 = 0; b0 < num_rows; b0 += blockDim.x) {
+    const int64_t b = b0 + threadIdx.x;
+    int32_t tiles = 0;
+    if (b < num_rows) {
+      const int32_t sl = seq_lens[b];
+      const int32_t ne = n_eff[b];
+      const int32_t nm = (sl + block_m - 1) / block_m;
+      const int32_t nn = (ne + block_n - 1) / block_n;
+      num_n_tiles[b] = nn;
+      tiles = (sl == 0 || ne == 0) ? 0 : nm * nn;
+    }
+    int32_t incl = tiles;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int32_t v = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += v;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int32_t v = (lane < (int)(blockDim.x >> 5)) ? warp_sums[lane] : 0;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int32_t u = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v += u;
+      }
+      warp_sums[lane] = v;
+    }
+    __syncthreads();
+    const int32_t incl_all = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + incl;
+    if (b < num_rows) cum_tiles[b + 1] = incl_all;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = incl_all;
+    __syncthreads();
+  }
+}
+
+}  // namespace plora

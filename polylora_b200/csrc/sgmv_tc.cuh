@@ -1,0 +1,576 @@
+// SGMV shrink and expand on the 5th-generation tensor cores (tcgen05 + TMEM),
+// bf16/fp16 operands with fp32 accumulation.
+//
+// Both kernels walk the device segment table (slot_start / token_index):
+// active tokens are grouped by slot, so one slot's LoRA weights are staged
+// in shared memory once per tile of up to 128 tokens, the tokens themselves
+// are gathered with 16-byte cp.async (rows are not contiguous in the batch),
+// and a single elected thread issues tcgen05.mma into a TMEM accumulator.
+// The per-slot weight tiles come in by TMA (cp.async.bulk.tensor into this
+// CTA's own shared memory).  Work is split evenly over a persistent grid: shrink by
+// tokens, expand by tokens x 128-column output tiles.
+//
+// Reference semantics: src/polylora/sgmv.py:63-138 (_sgmv_lora_a_kernel) and
+// sgmv.py:178-275 (_sgmv_lora_b_kernel).
+#pragma once
+
+#include "common.cuh"
+
+namespace plora {
+
+constexpr int kTileM = 128;        // tokens per MMA tile (TMEM lanes)
+constexpr int kShrinkKC = 64;      // K elements per shrink stage (one 128-byte row)
+constexpr int kShrinkStages = 6;
+constexpr int kExpandNT = 128;     // output columns per expand unit
+constexpr int kExpandStages = 4;
+constexpr int kShrinkThreads = 320;  // 4 gather warps, TMA, MMA, 4 epilogue warps
+constexpr int kExpandThreads = 384;  // TMA, tmp gather, MMA, idle, 8 epilogue warps
+
+struct SegTable {
+  const int32_t* slot_start;   // (num_slots + 1)
+  const int32_t* token_index;  // (>= slot_start[num_slots])
+  int32_t num_slots;
+};
+
+struct ShrinkArgs {
+  const uint8_t* x;   // (tokens, K)
+  const uint8_t* a;   // (NS, K, R)   (SIMT path; the TC path reads it by TMA)
+  uint8_t* tmp;       // (tokens, R)
+  const int32_t* ranks;
+  SegTable seg;
+  int32_t K, R, stack_num;
+};
+
+struct ExpandArgs {
+  const uint8_t* tmp;  // (tokens, R)
+  const uint8_t* b;    // (NS, R, N)  (SIMT path)
+  uint8_t* y;          // (tokens, N)
+  const int32_t* ranks;
+  const float* scales;
+  SegTable seg;
+  int32_t R, N;
+};
+
+// Items of the shrink: maximal runs of <= 128 tokens of one slot inside the
+// CTA's contiguous share [p, end) of the slot-ordered token list.
+struct ShrinkItems {
+  int64_t p, end;
+  int slot;
+  __device__ void init(const SegTable& t, int64_t b, int64_t e) {
+    p = b;
+    end = e;
+    slot = (b < e) ? slot_of_position(t.slot_start, t.num_slots, b) : 0;
+  }
+  __device__ bool next(const SegTable& t, int& s, int64_t& start, int& cnt) {
+    if (p >= end) return false;
+    while ((int64_t)__ldg(t.slot_start + slot + 1) <= p) ++slot;
+    const int64_t lim = min(end, (int64_t)__ldg(t.slot_start + slot + 1));
+    cnt = (int)min(lim - p, (int64_t)kTileM);
+    s = slot;
+    start = p;
+    p += cnt;
+    return true;
+  }
+};
+
+// Units of the expand: the work space is (token, 128-column tile) pairs laid
+// out slot-major, then 128-token item, then column tile, then token.  A CTA
+// takes a contiguous share; a unit is one (item, column tile) with the token
+// sub-range [t0, t1) of the item that falls inside the share.
+struct ExpandUnit {
+  int slot;
+  int64_t item_start;  // first position of the item in token_index
+  int cnt;             // tokens in the item
+  int tile;            // output column tile
+  int t0, t1;          // token sub-range of this unit
+};
+
+struct ExpandUnits {
+  int64_t w, wend;
+  int ntiles;
+  __device__ void init(int64_t b, int64_t e, int nt) {
+    w = b;
+    wend = e;
+    ntiles = nt;
+  }
+  __device__ bool next(const SegTable& t, ExpandUnit& u) {
+    if (w >= wend) return false;
+    // largest slot s with slot_start[s] * ntiles <= w
+    int lo = 0, hi = t.num_slots - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if ((int64_t)__ldg(t.slot_start + mid) * ntiles <= w)
+        lo = mid;
+      else
+        hi = mid - 1;
+    }
+    const int s = lo;
+    const int64_t s0 = __ldg(t.slot_start + s);
+    const int64_t cnt_s = (int64_t)__ldg(t.slot_start + s + 1) - s0;
+    const int64_t local = w - s0 * ntiles;
+    const int64_t item = local / ((int64_t)kTileM * ntiles);
+    const int cnt = (int)min((int64_t)kTileM, cnt_s - item * kTileM);
+    const int64_t within = local - item * kTileM * ntiles;
+    u.slot = s;
+    u.item_start = s0 + item * kTileM;
+    u.cnt = cnt;
+    u.tile = (int)(within / cnt);
+    u.t0 = (int)(within % cnt);
+    const int64_t take = min((int64_t)(cnt - u.t0), wend - w);
+    u.t1 = u.t0 + (int)take;
+    w += take;
+    return true;
+  }
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~(uintptr_t)1023);
+}
+
+// Time-bounded wait that ignores the abort flag (used to drain own work).
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      raise_status(PLORA_DEV_WAIT_TIMEOUT);
+      return;
+    }
+  }
+}
+
+// ============================================================== shrink
+template <int RP>
+struct ShrinkCfg {
+  static constexpr int kXBytes = kTileM * kShrinkKC * 2;  // 16 KB, K-major SW128
+  static constexpr int kABytes = kShrinkKC * RP * 2;      // MN-major, swizzle = RP*2 bytes
+  static constexpr int kStageBytes = kXBytes + ((kABytes + 1023) & ~1023);
+  static constexpr int kTmemCols = (2 * RP < 32) ? 32 : 2 * RP;
+  static constexpr uint32_t kALayout = RP == 16 ? kSwizzle32 : (RP == 32 ? kSwizzle64 : kSwizzle128);
+  static constexpr uint32_t kAAtom = 8 * RP * 2;  // 8 K-rows of one swizzle atom
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kSmemBytes = 1024 + kShrinkStages * kStageBytes + kBarrierBytes;
+};
+
+template <int RP, bool BF16>
+__global__ void __launch_bounds__(kShrinkThreads, 1)
+    sgmv_shrink_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const ShrinkArgs args) {
+  using Cfg = ShrinkCfg<RP>;
+  using E = Elem<BF16>;
+  constexpr int S = kShrinkStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t total = __ldg(args.seg.slot_start + args.seg.num_slots);
+  const int64_t begin = total * blockIdx.x / gridDim.x;
+  const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
+  if (begin >= end) return;  // uniform across the CTA
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 128 + 1);  // 128 gather threads (noinc) + TMA arrive
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int nkc = (args.K + kShrinkKC - 1) / kShrinkKC;
+
+  ShrinkItems items;
+  items.init(args.seg, begin, end);
+  int s, cnt;
+  int64_t start;
+
+  if (warp < 4) {
+    // ---------------- token gather: x rows -> K-major SW128 stage tiles
+    const int t = threadIdx.x;  // 0..127
+    const int c = t & 7;        // 16-byte chunk within the 128-byte row
+    const int r0 = t >> 3;      // rows r0 + 16 j
+    uint32_t ctr = 0;
+    bool ok = true;
+    while (ok && items.next(args.seg, s, start, cnt)) {
+      if (__ldg(args.ranks + s) <= 0) continue;
+      const uint8_t* rowp[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int r = r0 + 16 * j;
+        rowp[j] = (r < cnt)
+                      ? args.x + (int64_t)__ldg(args.seg.token_index + start + r) * args.K * 2
+                      : nullptr;
+      }
+      for (int kc = 0; kc < nkc; ++kc, ++ctr) {
+        const int st = ctr % S;
+        if (!mbar_wait(&empty[st], ((ctr / S) & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int k0 = kc * kShrinkKC + c * 8;
+        const int kleft = args.K - k0;
+        const uint32_t bytes = kleft >= 8 ? 16u : (kleft > 0 ? (uint32_t)kleft * 2u : 0u);
+        const uint32_t xs = smem_u32(smem + st * Cfg::kStageBytes);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (rowp[j] != nullptr) {
+            const int r = r0 + 16 * j;
+            const uint32_t dst = xs + r * 128 + ((c ^ (r & 7)) << 4);
+            cp_async_16(dst, bytes ? rowp[j] + (int64_t)k0 * 2 : rowp[j], bytes);
+          }
+        }
+        cp_async_arrive_noinc(&full[st]);
+      }
+    }
+    cp_async_wait_all();
+  } else if (warp == 4) {
+    // ---------------- TMA: LoRA A chunk (64 x RP) of the item's slot
+    if (lane == 0) {
+      prefetch_tmap(&tmap_a);
+      uint32_t ctr = 0;
+      bool ok = true;
+      while (ok && items.next(args.seg, s, start, cnt)) {
+        if (__ldg(args.ranks + s) <= 0) continue;
+        for (int kc = 0; kc < nkc; ++kc, ++ctr) {
+          const int st = ctr % S;
+          if (!mbar_wait(&empty[st], ((ctr / S) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[st], Cfg::kABytes);
+          tma_load_3d(smem_u32(smem + st * Cfg::kStageBytes + Cfg::kXBytes), &tmap_a, &full[st], 0,
+                      kc * kShrinkKC, s);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issue (one thread)
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(BF16, false, true, kTileM, RP);
+      uint32_t ctr = 0, item_ctr = 0;
+      bool issued = false, ok = true;
+      while (ok && items.next(args.seg, s, start, cnt)) {
+        if (__ldg(args.ranks + s) <= 0) continue;
+        const int ab = item_ctr & 1;
+        if (!mbar_wait(&acc_empty[ab], ((item_ctr >> 1) & 1) ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + ab * RP;
+        for (int kc = 0; kc < nkc; ++kc, ++ctr) {
+          const int st = ctr % S;
+          if (!mbar_wait(&full[st], (ctr / S) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_smem();
+          tc_fence_after();
+          const uint32_t xs = smem_u32(smem + st * Cfg::kStageBytes);
+          const uint32_t as = xs + Cfg::kXBytes;
+#pragma unroll
+          for (int kk = 0; kk < kShrinkKC / 16; ++kk) {
+            const uint64_t adesc = smem_desc(xs + kk * 32, 16, 1024, kSwizzle128);
+            const uint64_t bdesc =
+                smem_desc(as + kk * 2 * Cfg::kAAtom, Cfg::kAAtom, Cfg::kAAtom, Cfg::kALayout);
+            umma_f16(d_tmem, adesc, bdesc, idesc, (kc | kk) != 0);
+          }
+          umma_commit(&empty[st]);
+          issued = true;
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[ab]);
+        ++item_ctr;
+      }
+      if (issued) {
+        umma_commit(drain);
+        mbar_drain(drain, 0);
+      }
+    }
+  } else {
+    // ---------------- epilogue: TMEM -> registers -> tmp rows
+    const int q = warp & 3;  // TMEM lane quarter of this warp
+    uint32_t item_ctr = 0;
+    while (items.next(args.seg, s, start, cnt)) {
+      const int rank = __ldg(args.ranks + s);
+      if (rank <= 0) continue;
+      const int ab = item_ctr & 1;
+      if (!mbar_wait_warp(&acc_full[ab], (item_ctr >> 1) & 1, abort_flag)) break;
+      tc_fence_after();
+      uint32_t v[RP / 16][16];
+#pragma unroll
+      for (int g = 0; g < RP / 16; ++g)
+        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + ab * RP + g * 16, v[g]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+      const int r = q * 32 + lane;
+      if (r < cnt) {
+        const int n_eff = min(rank * args.stack_num, args.R);
+        const int64_t tok = __ldg(args.seg.token_index + start + r);
+        uint4* dst = reinterpret_cast<uint4*>(args.tmp + tok * args.R * 2);
+#pragma unroll
+        for (int ch = 0; ch < RP / 8; ++ch) {
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int j0 = ch * 8 + 2 * i;
+            const float f0 = (j0 < n_eff) ? __uint_as_float(v[j0 >> 4][j0 & 15]) : 0.f;
+            const float f1 = (j0 + 1 < n_eff) ? __uint_as_float(v[(j0 + 1) >> 4][(j0 + 1) & 15]) : 0.f;
+            w[i] = (uint32_t)E::from_f(f0) | ((uint32_t)E::from_f(f1) << 16);
+          }
+          dst[ch] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      ++item_ctr;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ============================================================== expand
+template <int RP>
+struct ExpandCfg {
+  static constexpr int kBoxBytes = RP * 128;  // RP rows x 64 columns, MN-major SW128
+  static constexpr int kBStageBytes = 2 * kBoxBytes;
+  static constexpr int kBStageStride = (kBStageBytes + 1023) & ~1023;
+  static constexpr int kTmpBytes = kTileM * RP * 2;  // K-major, no swizzle
+  static constexpr int kTmemCols = 2 * kExpandNT;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kSmemBytes =
+      1024 + kExpandStages * kBStageStride + 2 * kTmpBytes + kBarrierBytes;
+};
+
+template <int RP, bool BF16>
+__global__ void __launch_bounds__(kExpandThreads, 1)
+    sgmv_expand_tc_kernel(const __grid_constant__ CUtensorMap tmap_b, const ExpandArgs args) {
+  using Cfg = ExpandCfg<RP>;
+  using E = Elem<BF16>;
+  constexpr int S = kExpandStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* bst_base = smem;
+  uint8_t* tmp_base = smem + S * Cfg::kBStageStride;
+  uint64_t* bfull = reinterpret_cast<uint64_t*>(tmp_base + 2 * Cfg::kTmpBytes);
+  uint64_t* bempty = bfull + S;
+  uint64_t* tfull = bempty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* afull = tempty + 2;
+  uint64_t* aempty = afull + 2;
+  uint64_t* drain = aempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int ntiles = (args.N + kExpandNT - 1) / kExpandNT;
+  const int64_t total = (int64_t)__ldg(args.seg.slot_start + args.seg.num_slots) * ntiles;
+  const int64_t begin = total * blockIdx.x / gridDim.x;
+  const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
+  if (begin >= end) return;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&bfull[i], 1);
+      mbar_init(&bempty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 32);
+      mbar_init(&tempty[i], 1);
+      mbar_init(&afull[i], 1);
+      mbar_init(&aempty[i], 8);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  ExpandUnits units;
+  units.init(begin, end, ntiles);
+  ExpandUnit u;
+
+  if (warp == 0) {
+    // ---------------- TMA: LoRA B tile (RP x 128) of the unit's slot
+    if (lane == 0) {
+      prefetch_tmap(&tmap_b);
+      uint32_t ctr = 0;
+      while (units.next(args.seg, u)) {
+        if (__ldg(args.ranks + u.slot) <= 0) continue;
+        const int st = ctr % S;
+        if (!mbar_wait(&bempty[st], ((ctr / S) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&bfull[st], Cfg::kBStageBytes);
+        const uint32_t dst = smem_u32(bst_base + st * Cfg::kBStageStride);
+        tma_load_3d(dst, &tmap_b, &bfull[st], u.tile * kExpandNT, 0, u.slot);
+        tma_load_3d(dst + Cfg::kBoxBytes, &tmap_b, &bfull[st], u.tile * kExpandNT + 64, 0, u.slot);
+        ++ctr;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- tmp gather: item rows -> K-major (no swizzle) tile
+    uint32_t item_ctr = 0;
+    int64_t prev = -1;
+    while (units.next(args.seg, u)) {
+      const int rank = __ldg(args.ranks + u.slot);
+      if (rank <= 0 || u.item_start == prev) continue;
+      prev = u.item_start;
+      const int tb = item_ctr & 1;
+      if (!mbar_wait(&tempty[tb], ((item_ctr >> 1) & 1) ^ 1, abort_flag)) break;
+      const int kr = min(rank, args.R);
+      const uint32_t tbuf = smem_u32(tmp_base + tb * Cfg::kTmpBytes);
+#pragma unroll
+      for (int rr = 0; rr < kTileM / 32; ++rr) {
+        const int r = lane + 32 * rr;
+        if (r < u.cnt) {
+          const uint8_t* src =
+              args.tmp + (int64_t)__ldg(args.seg.token_index + u.item_start + r) * args.R * 2;
+#pragma unroll
+          for (int c = 0; c < RP / 8; ++c) {
+            const int kleft = kr - c * 8;
+            const uint32_t bytes = kleft >= 8 ? 16u : (kleft > 0 ? (uint32_t)kleft * 2u : 0u);
+            const uint32_t dst = tbuf + (r >> 3) * (RP * 16) + c * 128 + (r & 7) * 16;
+            cp_async_16(dst, bytes ? src + c * 16 : src, bytes);
+          }
+        }
+      }
+      cp_async_arrive_noinc(&tfull[tb]);
+      ++item_ctr;
+    }
+    cp_async_wait_all();
+  } else if (warp == 2) {
+    // ---------------- MMA issue (one thread)
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(BF16, false, true, kTileM, kExpandNT);
+      uint32_t bctr = 0, unit_ctr = 0, item_ctr = 0;
+      int64_t prev = -1;
+      int tb = 0;
+      bool issued = false, ok = true;
+      while (ok && units.next(args.seg, u)) {
+        if (__ldg(args.ranks + u.slot) <= 0) continue;
+        if (u.item_start != prev) {
+          if (prev >= 0) umma_commit(&tempty[tb]);  // previous tile free once its MMAs finish
+          prev = u.item_start;
+          tb = item_ctr & 1;
+          if (!mbar_wait(&tfull[tb], (item_ctr >> 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_smem();
+          ++item_ctr;
+        }
+        const int st = bctr % S;
+        if (!mbar_wait(&bfull[st], (bctr / S) & 1, abort_flag)) break;
+        const int ab = unit_ctr & 1;
+        if (!mbar_wait(&aempty[ab], ((unit_ctr >> 1) & 1) ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t tsm = smem_u32(tmp_base + tb * Cfg::kTmpBytes);
+        const uint32_t bsm = smem_u32(bst_base + st * Cfg::kBStageStride);
+#pragma unroll
+        for (int ks = 0; ks < RP / 16; ++ks) {
+          const uint64_t adesc = smem_desc(tsm + ks * 256, 128, RP * 16, kSwizzleNone);
+          const uint64_t bdesc = smem_desc(bsm + ks * 2048, Cfg::kBoxBytes, 1024, kSwizzle128);
+          umma_f16(tmem_base + ab * kExpandNT, adesc, bdesc, idesc, ks != 0);
+        }
+        umma_commit(&bempty[st]);
+        umma_commit(&afull[ab]);
+        issued = true;
+        ++bctr;
+        ++unit_ctr;
+      }
+      if (issued) {
+        umma_commit(drain);
+        mbar_drain(drain, 0);
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- epilogue: y[token, cols] += scale * D  (in place)
+    const int q = warp & 3;         // TMEM lane quarter
+    const int h = (warp - 4) >> 2;  // column half of the 128-column tile
+    const int r = q * 32 + lane;
+    uint32_t unit_ctr = 0;
+    while (units.next(args.seg, u)) {
+      if (__ldg(args.ranks + u.slot) <= 0) continue;
+      const float scale = __ldg(args.scales + u.slot);
+      const int n_base = u.tile * kExpandNT + h * 64;
+      const int ncols = min(64, args.N - n_base);  // multiple of 8 (N % 8 == 0)
+      const bool active = (r >= u.t0) && (r < u.t1) && ncols > 0;
+      uint4 yv[8];
+      uint4* yrow = nullptr;
+      if (active) {
+        const int64_t tok = __ldg(args.seg.token_index + u.item_start + r);
+        yrow = reinterpret_cast<uint4*>(args.y + (tok * args.N + n_base) * 2);
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          if (c * 8 < ncols) yv[c] = yrow[c];
+      }
+      const int ab = unit_ctr & 1;
+      if (!mbar_wait_warp(&afull[ab], (unit_ctr >> 1) & 1, abort_flag)) break;
+      tc_fence_after();
+      uint32_t acc[4][16];
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + ab * kExpandNT + h * 64 + g * 16,
+                  acc[g]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&aempty[ab]);
+      if (active) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          if (c * 8 < ncols) {
+            uint32_t in[4] = {yv[c].x, yv[c].y, yv[c].z, yv[c].w};
+            uint32_t out[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int j = c * 8 + 2 * i;
+              const float a0 = __uint_as_float(acc[j >> 4][j & 15]);
+              const float a1 = __uint_as_float(acc[(j + 1) >> 4][(j + 1) & 15]);
+              const float y0 = E::to_f((uint16_t)(in[i] & 0xFFFFu)) + scale * a0;
+              const float y1 = E::to_f((uint16_t)(in[i] >> 16)) + scale * a1;
+              out[i] = (uint32_t)E::from_f(y0) | ((uint32_t)E::from_f(y1) << 16);
+            }
+            yrow[c] = make_uint4(out[0], out[1], out[2], out[3]);
+          }
+        }
+      }
+      ++unit_ctr;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace plora

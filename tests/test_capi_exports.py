@@ -1,0 +1,76 @@
+"""The C-ABI library loads on a machine without a GPU and exports every entry
+point declared in include/polylora_b200.h.  Only argument checks that return
+before any CUDA call are exercised here."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "polylora_b200.h"
+
+
+def declared_functions() -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(plora_\w+)\s*\(", text)))
+
+
+def test_header_declares_expected_entry_points():
+    names = declared_functions()
+    for required in ("plora_sgmv_a_fwd", "plora_sgmv_b_fwd", "plora_sgmv_shrink", "plora_sgmv_expand",
+                     "plora_build_segments", "plora_flat_schedule", "plora_slot_fill",
+                     "plora_workspace_size", "plora_device_status"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol(native):
+    lib = native.load()
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+    # the ctypes binding covers the whole header
+    assert set(declared_functions()) <= set(native._SIGNATURES)
+
+
+def test_version_and_status_strings(native):
+    assert "sm_100a" in native.version()
+    lib = native.load()
+    assert lib.plora_status_string(native.OK) == b"ok"
+    assert lib.plora_status_string(native.ERR_WORKSPACE) == b"workspace too small"
+
+
+def test_struct_layouts_match_header(native):
+    assert ctypes.sizeof(native.SlotModule) == 48
+    assert ctypes.sizeof(native.SlotRecord) == 24
+
+
+@pytest.mark.parametrize("dtype", [3, -1])
+def test_bad_dtype_rejected_before_cuda(native, dtype):
+    lib = native.load()
+    st = lib.plora_sgmv_shrink(None, None, None, None, None, None, 16, 64, 16, 5, 1, dtype, None)
+    assert st == native.ERR_INVALID_ARGUMENT
+    assert "dtype" in native.last_error()
+
+
+def test_workspace_size_and_null_checks(native):
+    lib = native.load()
+    assert native.workspace_size(16384, 1, 65) >= (16384 + 66) * 4
+    assert native.workspace_size(-1, 1, 65) == 0
+    # too many slots is refused up front
+    st = lib.plora_sgmv_expand(None, None, None, None, None, None, None, 8, 16, 64, 5000, 2, None)
+    assert st == native.ERR_UNSUPPORTED
+    # missing workspace
+    st = lib.plora_sgmv_a_fwd(None, None, None, None, None, None, 4, 2, 64, 16, 5, 1, 2, None, 0, None)
+    assert st == native.ERR_WORKSPACE
+
+
+def test_product_path_has_no_cpu_fallback():
+    import torch
+
+    from polylora_b200.sgmv import sgmv_lora_a_fwd
+
+    x = torch.zeros(2, 3, 8)
+    w = torch.zeros(3, 8, 4)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        sgmv_lora_a_fwd(x, w, torch.ones(2, dtype=torch.int32), torch.zeros(2, dtype=torch.int64),
+                        torch.zeros(3, dtype=torch.int32))
