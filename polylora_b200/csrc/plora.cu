@@ -118,6 +118,24 @@ int make_map_3d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, uint
   return PLORA_OK;
 }
 
+// 2-D tiled map over a contiguous (d1, d0) 16-bit tensor.
+int make_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, uint64_t d1,
+                uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {d0, d1};
+  const cuuint64_t strides[1] = {d0 * 2};
+  const cuuint32_t box[2] = {b0, b1};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt = dtype == PLORA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled(2d) failed (%d)", (int)r);
+  return PLORA_OK;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 size_t elem_size(int dtype) { return dtype == PLORA_DTYPE_F32 ? 4 : 2; }
@@ -170,10 +188,11 @@ int build_segments(const int64_t* wi, const int32_t* seq_lens, const int32_t* ra
       wi, seq_lens, ranks, num_rows, max_seq, num_slots, w);
   int st = check_launch("seg_count_kernel");
   if (st) return st;
-  seg_scan_kernel<<<1, 1024, 0, stream>>>((int32_t)blocks, num_slots, w, slot_start);
+  seg_scan_kernel<<<1, 1024, (size_t)num_slots * 4, stream>>>((int32_t)blocks, num_slots, w,
+                                                               slot_start);
   if ((st = check_launch("seg_scan_kernel"))) return st;
   seg_place_kernel<<<(unsigned)((num_rows + 7) / 8), 256, 0, stream>>>(
-      num_rows, max_seq, seq_lens, num_slots, w, token_index);
+      num_rows, max_seq, seq_lens, (int32_t)blocks, w, slot_start, token_index);
   return check_launch("seg_place_kernel");
 }
 
@@ -181,7 +200,8 @@ int build_segments(const int64_t* wi, const int32_t* seq_lens, const int32_t* ra
 bool tc_rank_ok(int64_t R) { return R == 16 || R == 32 || R == 64; }
 
 int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, SegTable seg,
-                int64_t K, int64_t R, int32_t stack_num, int32_t dtype, cudaStream_t stream) {
+                int64_t num_tokens, int64_t K, int64_t R, int32_t stack_num, int32_t dtype,
+                cudaStream_t stream) {
   DeviceInfo* di = nullptr;
   int st = device_info(&di);
   if (st) return st;
@@ -197,22 +217,25 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
   const bool tc = dtype != PLORA_DTYPE_F32 && tc_rank_ok(R) && K % 8 == 0 && aligned16(x) &&
                   aligned16(a) && aligned16(tmp);
   if (tc) {
-    CUtensorMap map;
+    CUtensorMap map, xmap;
     const CUtensorMapSwizzle swz = R == 16   ? CU_TENSOR_MAP_SWIZZLE_32B
                                    : R == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
                                              : CU_TENSOR_MAP_SWIZZLE_128B;
     if ((st = make_map_3d(&map, a, dtype, (uint64_t)R, (uint64_t)K, (uint64_t)seg.num_slots,
                           (uint32_t)R, kShrinkKC, swz)))
       return st;
+    if ((st = make_map_2d(&xmap, x, dtype, (uint64_t)K, (uint64_t)num_tokens, kShrinkKC, 1,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
     const dim3 grid(di->sm_count), block(kShrinkThreads);
     const bool bf = dtype == PLORA_DTYPE_BF16;
 #define LAUNCH_SHRINK(RPV)                                                               \
   if (bf)                                                                                \
     sgmv_shrink_tc_kernel<RPV, true><<<grid, block, ShrinkCfg<RPV>::kSmemBytes, stream>>>( \
-        map, args);                                                                      \
+        map, xmap, args);                                                                \
   else                                                                                   \
     sgmv_shrink_tc_kernel<RPV, false><<<grid, block, ShrinkCfg<RPV>::kSmemBytes, stream>>>( \
-        map, args);
+        map, xmap, args);
     if (R == 16) {
       LAUNCH_SHRINK(16)
     } else if (R == 32) {
@@ -377,8 +400,10 @@ int plora_sgmv_shrink(const void* x, const void* lora_a, void* tmp, const int32_
   if (!x || !lora_a || !tmp || !lora_ranks || !slot_start || !token_index)
     return fail(PLORA_ERR_INVALID_ARGUMENT, "null pointer");
   SegTable seg{slot_start, token_index, num_slots};
-  return shrink_impl(x, lora_a, tmp, lora_ranks, seg, in_features, max_rank, stack_num, dtype,
-                     static_cast<cudaStream_t>(stream));
+  if (num_tokens > (int64_t)INT32_MAX)
+    return fail(PLORA_ERR_UNSUPPORTED, "num_tokens exceeds int32 token ids");
+  return shrink_impl(x, lora_a, tmp, lora_ranks, seg, num_tokens, in_features, max_rank, stack_num,
+                     dtype, static_cast<cudaStream_t>(stream));
 }
 
 int plora_sgmv_expand(const void* tmp, const void* lora_b, void* y, const int32_t* lora_ranks,

@@ -16,10 +16,11 @@ constexpr int kSegRowsPerBlock = 256;  // rows counted per block (8 warps)
 constexpr int kSegMaxSlots = 4096;     // slot-count limit of the segment kernels
 
 // Workspace layout (bytes, each part 256-aligned):
-//   partial[num_blocks][num_slots] int32   per-block per-slot token counts,
-//                                          rewritten in place to global bases
-//   row_off[num_rows]              int32   token offset of a row within its block+slot
-//   row_info[num_rows]             int32   slot (>= 0) or -1 when inactive
+//   partial[num_slots][num_blocks] int32  per-slot per-block token counts,
+//                                         rewritten in place to the prefix over
+//                                         earlier blocks of the same slot
+//   row_off[num_rows]              int32  token offset of a row within its block+slot
+//   row_info[num_rows]             int32  slot (>= 0) or -1 when inactive
 __host__ __device__ inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 struct SegWorkspace {
@@ -97,29 +98,44 @@ __global__ void __launch_bounds__(kSegRowsPerBlock) seg_count_kernel(
     __syncthreads();
   }
   if (row < num_rows) ws.row_info[row] = key;
-  int32_t* out = ws.partial + (int64_t)blockIdx.x * num_slots;
-  for (int s = threadIdx.x; s < num_slots; s += blockDim.x) out[s] = cnt[s];
+  for (int s = threadIdx.x; s < num_slots; s += blockDim.x)
+    ws.partial[(int64_t)s * gridDim.x + blockIdx.x] = cnt[s];
 }
 
-// Pass 2 (one block): slot_start = exclusive scan over slots of the totals,
-// and partial[b][s] rewritten to the global first position of block b's
-// tokens of slot s.
+// Pass 2 (one block of 1024): per slot (one warp each, lanes over blocks),
+// partial[s][b] becomes the prefix over blocks b' < b; then slot_start is the
+// exclusive scan over slots of the per-slot totals.
 __global__ void __launch_bounds__(1024) seg_scan_kernel(int32_t num_blocks, int32_t num_slots,
                                                          SegWorkspace ws,
                                                          int32_t* __restrict__ slot_start) {
+  extern __shared__ int32_t totals[];  // [num_slots]
   __shared__ int32_t warp_sums[32];
   __shared__ int32_t carry;
-  if (threadIdx.x == 0) carry = 0;
-  __syncthreads();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  for (int s = warp; s < num_slots; s += nwarps) {
+    int32_t* row = ws.partial + (int64_t)s * num_blocks;
+    int run = 0;
+    for (int b0 = 0; b0 < num_blocks; b0 += 32) {
+      const int b = b0 + lane;
+      const int v = b < num_blocks ? row[b] : 0;
+      int incl = v;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += u;
+      }
+      if (b < num_blocks) row[b] = run + incl - v;
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) totals[s] = run;
+  }
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
   for (int s0 = 0; s0 < num_slots; s0 += blockDim.x) {
     const int s = s0 + threadIdx.x;
-    int total = 0;
-    if (s < num_slots) {
-      for (int b = 0; b < num_blocks; ++b) total += ws.partial[(int64_t)b * num_slots + s];
-    }
-    // block-wide exclusive scan of total
+    const int total = s < num_slots ? totals[s] : 0;
     int incl = total;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
@@ -129,26 +145,17 @@ __global__ void __launch_bounds__(1024) seg_scan_kernel(int32_t num_blocks, int3
     if (lane == 31) warp_sums[warp] = incl;
     __syncthreads();
     if (warp == 0) {
-      int ws_v = (lane < (int)(blockDim.x >> 5)) ? warp_sums[lane] : 0;
+      int v = (lane < nwarps) ? warp_sums[lane] : 0;
 #pragma unroll
       for (int d = 1; d < 32; d <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, ws_v, d);
-        if (lane >= d) ws_v += v;
+        const int u = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v += u;
       }
-      warp_sums[lane] = ws_v;  // inclusive over warps
+      warp_sums[lane] = v;  // inclusive over warps
     }
     __syncthreads();
     const int excl = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + incl - total;
-    if (s < num_slots) {
-      slot_start[s] = excl;
-      int run = excl;
-      for (int b = 0; b < num_blocks; ++b) {
-        int32_t* cell = ws.partial + (int64_t)b * num_slots + s;
-        const int c = *cell;
-        *cell = run;
-        run += c;
-      }
-    }
+    if (s < num_slots) slot_start[s] = excl;
     __syncthreads();
     if (threadIdx.x == blockDim.x - 1) carry = excl + total;
     __syncthreads();
@@ -156,10 +163,12 @@ __global__ void __launch_bounds__(1024) seg_scan_kernel(int32_t num_blocks, int3
   if (threadIdx.x == 0) slot_start[num_slots] = carry;
 }
 
-// Pass 3: one warp per row writes the row's token ids at its final position.
+// Pass 3: one warp per row writes the row's token ids at its final position
+// slot_start[slot] + prefix of earlier blocks + offset within the block.
 __global__ void __launch_bounds__(256) seg_place_kernel(int64_t num_rows, int64_t max_seq,
                                                          const int32_t* __restrict__ seq_lens,
-                                                         int32_t num_slots, SegWorkspace ws,
+                                                         int32_t num_blocks, SegWorkspace ws,
+                                                         const int32_t* __restrict__ slot_start,
                                                          int32_t* __restrict__ token_index) {
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -169,7 +178,8 @@ __global__ void __launch_bounds__(256) seg_place_kernel(int64_t num_rows, int64_
   int64_t l = seq_lens[row];
   l = l < 0 ? 0 : (l > max_seq ? max_seq : l);
   const int64_t blk = row / kSegRowsPerBlock;
-  const int64_t dst = (int64_t)ws.partial[blk * num_slots + key] + ws.row_off[row];
+  const int64_t dst = (int64_t)slot_start[key] + ws.partial[(int64_t)key * num_blocks + blk] +
+                      ws.row_off[row];
   const int64_t tok0 = row * max_seq;
   for (int64_t m = lane; m < l; m += 32) token_index[dst + m] = (int32_t)(tok0 + m);
 }

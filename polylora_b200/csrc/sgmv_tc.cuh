@@ -3,12 +3,13 @@
 //
 // Both kernels walk the device segment table (slot_start / token_index):
 // active tokens are grouped by slot, so one slot's LoRA weights are staged
-// in shared memory once per tile of up to 128 tokens, the tokens themselves
-// are gathered with 16-byte cp.async (rows are not contiguous in the batch),
-// and a single elected thread issues tcgen05.mma into a TMEM accumulator.
-// The per-slot weight tiles come in by TMA (cp.async.bulk.tensor into this
-// CTA's own shared memory).  Work is split evenly over a persistent grid: shrink by
-// tokens, expand by tokens x 128-column output tiles.
+// in shared memory once per tile of up to 128 tokens and a single elected
+// thread issues tcgen05.mma into a TMEM accumulator.  All bulk data moves on
+// the TMA engine into this CTA's own shared memory: the scattered token rows
+// of x by tile::gather4 (four rows per instruction, 128-byte swizzled straight
+// into the UMMA operand layout), the per-slot weight tiles by tiled TMA, and
+// the rows of y by 1-D bulk copies in and out.  Work is split evenly over a
+// persistent grid: shrink by tokens, expand by tokens x 128-column tiles.
 //
 // Reference semantics: src/polylora/sgmv.py:63-138 (_sgmv_lora_a_kernel) and
 // sgmv.py:178-275 (_sgmv_lora_b_kernel).
@@ -20,11 +21,11 @@ namespace plora {
 
 constexpr int kTileM = 128;        // tokens per MMA tile (TMEM lanes)
 constexpr int kShrinkKC = 64;      // K elements per shrink stage (one 128-byte row)
-constexpr int kShrinkStages = 6;
+constexpr int kShrinkStages = 8;
 constexpr int kExpandNT = 128;     // output columns per expand unit
-constexpr int kExpandStages = 4;
-constexpr int kShrinkThreads = 320;  // 4 gather warps, TMA, MMA, 4 epilogue warps
-constexpr int kExpandThreads = 384;  // TMA, tmp gather, MMA, idle, 8 epilogue warps
+constexpr int kYRowBytes = kExpandNT * 2 + 16;  // padded smem row: conflict-free row-per-thread access
+constexpr int kShrinkThreads = 192;  // TMA producer, MMA, 4 epilogue warps
+constexpr int kExpandThreads = 384;  // B/y producer, tmp gather, MMA, idle, 8 epilogue warps
 
 struct SegTable {
   const int32_t* slot_start;   // (num_slots + 1)
@@ -147,19 +148,29 @@ struct ShrinkCfg {
   static constexpr int kTmemCols = (2 * RP < 32) ? 32 : 2 * RP;
   static constexpr uint32_t kALayout = RP == 16 ? kSwizzle32 : (RP == 32 ? kSwizzle64 : kSwizzle128);
   static constexpr uint32_t kAAtom = 8 * RP * 2;  // 8 K-rows of one swizzle atom
+  static constexpr int kTokBytes = kTileM * 4;
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes = 1024 + kShrinkStages * kStageBytes + kBarrierBytes;
+  static constexpr int kSmemBytes = 1024 + kShrinkStages * kStageBytes + kTokBytes + kBarrierBytes;
+  static_assert(kSmemBytes <= 227 * 1024, "shrink shared memory");
 };
 
+// tmp[t, :] = x[t, :] @ A[slot(t)] for the active tokens of the table.
+//   warp 0: producer — per item, stages token ids; lane 0 then issues, per
+//           64-wide K chunk, one TMA of A[slot] (64 x RP) and ceil(cnt/4)
+//           gather4 loads of the token rows of x.
+//   warp 1: TMEM owner; lane 0 issues 4 UMMAs (128 x RP x 16) per chunk.
+//   warps 2-5: epilogue — TMEM -> registers -> bf16/fp16 rows of tmp.
 template <int RP, bool BF16>
 __global__ void __launch_bounds__(kShrinkThreads, 1)
-    sgmv_shrink_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const ShrinkArgs args) {
+    sgmv_shrink_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                          const __grid_constant__ CUtensorMap tmap_x, const ShrinkArgs args) {
   using Cfg = ShrinkCfg<RP>;
   using E = Elem<BF16>;
   constexpr int S = kShrinkStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  int32_t* tok_s = reinterpret_cast<int32_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes + Cfg::kTokBytes);
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
   uint64_t* acc_empty = acc_full + 2;
@@ -176,7 +187,7 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&full[i], 128 + 1);  // 128 gather threads (noinc) + TMA arrive
+      mbar_init(&full[i], 1);  // producer's arrive.expect_tx
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -187,7 +198,7 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 4) {
+  if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
@@ -202,66 +213,43 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   int s, cnt;
   int64_t start;
 
-  if (warp < 4) {
-    // ---------------- token gather: x rows -> K-major SW128 stage tiles
-    const int t = threadIdx.x;  // 0..127
-    const int c = t & 7;        // 16-byte chunk within the 128-byte row
-    const int r0 = t >> 3;      // rows r0 + 16 j
+  if (warp == 0) {
+    // ---------------- producer: A chunk by TMA, token rows by gather4
+    if (lane == 0) {
+      prefetch_tmap(&tmap_a);
+      prefetch_tmap(&tmap_x);
+    }
     uint32_t ctr = 0;
     bool ok = true;
     while (ok && items.next(args.seg, s, start, cnt)) {
       if (__ldg(args.ranks + s) <= 0) continue;
-      const uint8_t* rowp[8];
+      __syncwarp();
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int r = r0 + 16 * j;
-        rowp[j] = (r < cnt)
-                      ? args.x + (int64_t)__ldg(args.seg.token_index + start + r) * args.K * 2
-                      : nullptr;
+      for (int i = 0; i < kTileM / 32; ++i) {
+        const int r = lane + 32 * i;
+        tok_s[r] = __ldg(args.seg.token_index + start + min(r, cnt - 1));  // pad with the last row
       }
-      for (int kc = 0; kc < nkc; ++kc, ++ctr) {
-        const int st = ctr % S;
-        if (!mbar_wait(&empty[st], ((ctr / S) & 1) ^ 1, abort_flag)) {
-          ok = false;
-          break;
-        }
-        const int k0 = kc * kShrinkKC + c * 8;
-        const int kleft = args.K - k0;
-        const uint32_t bytes = kleft >= 8 ? 16u : (kleft > 0 ? (uint32_t)kleft * 2u : 0u);
-        const uint32_t xs = smem_u32(smem + st * Cfg::kStageBytes);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (rowp[j] != nullptr) {
-            const int r = r0 + 16 * j;
-            const uint32_t dst = xs + r * 128 + ((c ^ (r & 7)) << 4);
-            cp_async_16(dst, bytes ? rowp[j] + (int64_t)k0 * 2 : rowp[j], bytes);
-          }
-        }
-        cp_async_arrive_noinc(&full[st]);
-      }
-    }
-    cp_async_wait_all();
-  } else if (warp == 4) {
-    // ---------------- TMA: LoRA A chunk (64 x RP) of the item's slot
-    if (lane == 0) {
-      prefetch_tmap(&tmap_a);
-      uint32_t ctr = 0;
-      bool ok = true;
-      while (ok && items.next(args.seg, s, start, cnt)) {
-        if (__ldg(args.ranks + s) <= 0) continue;
+      __syncwarp();
+      if (lane == 0) {
+        const int ngroups = (cnt + 3) >> 2;
+        const uint32_t tx = Cfg::kABytes + ngroups * 4 * 128;
         for (int kc = 0; kc < nkc; ++kc, ++ctr) {
           const int st = ctr % S;
           if (!mbar_wait(&empty[st], ((ctr / S) & 1) ^ 1, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[st], Cfg::kABytes);
-          tma_load_3d(smem_u32(smem + st * Cfg::kStageBytes + Cfg::kXBytes), &tmap_a, &full[st], 0,
-                      kc * kShrinkKC, s);
+          const uint32_t xs = smem_u32(smem + st * Cfg::kStageBytes);
+          mbar_arrive_expect_tx(&full[st], tx);
+          tma_load_3d(xs + Cfg::kXBytes, &tmap_a, &full[st], 0, kc * kShrinkKC, s);
+          for (int g = 0; g < ngroups; ++g)
+            tma_gather4(xs + g * 512, &tmap_x, &full[st], kc * kShrinkKC, tok_s[4 * g],
+                        tok_s[4 * g + 1], tok_s[4 * g + 2], tok_s[4 * g + 3]);
         }
       }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
     }
-  } else if (warp == 5) {
+  } else if (warp == 1) {
     // ---------------- MMA issue (one thread)
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(BF16, false, true, kTileM, RP);
@@ -279,7 +267,6 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
             ok = false;
             break;
           }
-          fence_proxy_async_smem();
           tc_fence_after();
           const uint32_t xs = smem_u32(smem + st * Cfg::kStageBytes);
           const uint32_t as = xs + Cfg::kXBytes;
@@ -343,7 +330,7 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   }
 
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
@@ -356,25 +343,40 @@ struct ExpandCfg {
   static constexpr int kBStageBytes = 2 * kBoxBytes;
   static constexpr int kBStageStride = (kBStageBytes + 1023) & ~1023;
   static constexpr int kTmpBytes = kTileM * RP * 2;  // K-major, no swizzle
+  static constexpr int kYStageBytes = kTileM * kYRowBytes;
+  static constexpr int kBStages = RP >= 64 ? 2 : 4;  // LoRA-B tile stages
+  static constexpr int kYStages = RP >= 64 ? 3 : 4;  // y row-tile stages
   static constexpr int kTmemCols = 2 * kExpandNT;
-  static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes =
-      1024 + kExpandStages * kBStageStride + 2 * kTmpBytes + kBarrierBytes;
+  static constexpr int kBarrierBytes = 512;
+  static constexpr int kSmemBytes = 1024 + kBStages * kBStageStride + 2 * kTmpBytes +
+                                    kYStages * kYStageBytes + kBarrierBytes;
+  static_assert(kSmemBytes <= 227 * 1024, "expand shared memory");
 };
 
+// y[t, :] += scale[slot(t)] * tmp[t, :] @ B[slot(t)] (in place).
+//   warp 0: producer — lane 0 loads the B tile (RP x 128) by TMA; all lanes
+//           bulk-copy the unit's y rows (<= 256 B each) into padded smem rows.
+//   warp 1: gathers the item's tmp rows (K-major, no swizzle) with cp.async.
+//   warp 2: TMEM owner; lane 0 issues RP/16 UMMAs (128 x 128 x 16) per unit.
+//   warps 4-11: epilogue — thread = token row, 64 columns: TMEM + smem y ->
+//           smem y, then a bulk store of the row segment back to global.
 template <int RP, bool BF16>
 __global__ void __launch_bounds__(kExpandThreads, 1)
     sgmv_expand_tc_kernel(const __grid_constant__ CUtensorMap tmap_b, const ExpandArgs args) {
   using Cfg = ExpandCfg<RP>;
   using E = Elem<BF16>;
-  constexpr int S = kExpandStages;
+  constexpr int S = Cfg::kBStages;
+  constexpr int YS = Cfg::kYStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* bst_base = smem;
   uint8_t* tmp_base = smem + S * Cfg::kBStageStride;
-  uint64_t* bfull = reinterpret_cast<uint64_t*>(tmp_base + 2 * Cfg::kTmpBytes);
+  uint8_t* y_base = tmp_base + 2 * Cfg::kTmpBytes;
+  uint64_t* bfull = reinterpret_cast<uint64_t*>(y_base + YS * Cfg::kYStageBytes);
   uint64_t* bempty = bfull + S;
-  uint64_t* tfull = bempty + S;
+  uint64_t* yfull = bempty + S;
+  uint64_t* yempty = yfull + YS;
+  uint64_t* tfull = yempty + YS;
   uint64_t* tempty = tfull + 2;
   uint64_t* afull = tempty + 2;
   uint64_t* aempty = afull + 2;
@@ -394,6 +396,10 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
     for (int i = 0; i < S; ++i) {
       mbar_init(&bfull[i], 1);
       mbar_init(&bempty[i], 1);
+    }
+    for (int i = 0; i < YS; ++i) {
+      mbar_init(&yfull[i], 1);
+      mbar_init(&yempty[i], 8);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 32);
@@ -419,20 +425,37 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
   ExpandUnit u;
 
   if (warp == 0) {
-    // ---------------- TMA: LoRA B tile (RP x 128) of the unit's slot
-    if (lane == 0) {
-      prefetch_tmap(&tmap_b);
-      uint32_t ctr = 0;
-      while (units.next(args.seg, u)) {
-        if (__ldg(args.ranks + u.slot) <= 0) continue;
-        const int st = ctr % S;
-        if (!mbar_wait(&bempty[st], ((ctr / S) & 1) ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&bfull[st], Cfg::kBStageBytes);
-        const uint32_t dst = smem_u32(bst_base + st * Cfg::kBStageStride);
-        tma_load_3d(dst, &tmap_b, &bfull[st], u.tile * kExpandNT, 0, u.slot);
-        tma_load_3d(dst + Cfg::kBoxBytes, &tmap_b, &bfull[st], u.tile * kExpandNT + 64, 0, u.slot);
-        ++ctr;
+    // ---------------- producer: B tile by TMA, y rows by bulk copies
+    if (lane == 0) prefetch_tmap(&tmap_b);
+    uint32_t bctr = 0, yctr = 0;
+    bool ok = true;
+    while (ok && units.next(args.seg, u)) {
+      if (__ldg(args.ranks + u.slot) <= 0) continue;
+      const int n0 = u.tile * kExpandNT;
+      if (lane == 0) {
+        const int st = bctr % S;
+        ok = mbar_wait(&bempty[st], ((bctr / S) & 1) ^ 1, abort_flag);
+        if (ok) {
+          mbar_arrive_expect_tx(&bfull[st], Cfg::kBStageBytes);
+          const uint32_t dst = smem_u32(bst_base + st * Cfg::kBStageStride);
+          tma_load_3d(dst, &tmap_b, &bfull[st], n0, 0, u.slot);
+          tma_load_3d(dst + Cfg::kBoxBytes, &tmap_b, &bfull[st], n0 + 64, 0, u.slot);
+        }
       }
+      ++bctr;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      const int ys = yctr % YS;
+      if (!mbar_wait_warp(&yempty[ys], ((yctr / YS) & 1) ^ 1, abort_flag)) break;
+      const uint32_t row_bytes = (uint32_t)min(kExpandNT, args.N - n0) * 2u;
+      if (lane == 0) mbar_arrive_expect_tx(&yfull[ys], row_bytes * (uint32_t)(u.t1 - u.t0));
+      __syncwarp();
+      const uint32_t ybuf = smem_u32(y_base + ys * Cfg::kYStageBytes);
+      for (int r = u.t0 + lane; r < u.t1; r += 32) {
+        const int64_t tok = __ldg(args.seg.token_index + u.item_start + r);
+        bulk_load(ybuf + r * kYRowBytes, args.y + (tok * args.N + n0) * 2, row_bytes, &yfull[ys]);
+      }
+      ++yctr;
     }
   } else if (warp == 1) {
     // ---------------- tmp gather: item rows -> K-major (no swizzle) tile
@@ -483,7 +506,7 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
             ok = false;
             break;
           }
-          fence_proxy_async_smem();
+          fence_proxy_async_smem();  // cp.async (generic proxy) data -> UMMA operand
           ++item_ctr;
         }
         const int st = bctr % S;
@@ -511,27 +534,20 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
       }
     }
   } else if (warp >= 4) {
-    // ---------------- epilogue: y[token, cols] += scale * D  (in place)
+    // ---------------- epilogue: y row segment += scale * D, in shared memory, then bulk store
     const int q = warp & 3;         // TMEM lane quarter
     const int h = (warp - 4) >> 2;  // column half of the 128-column tile
     const int r = q * 32 + lane;
     uint32_t unit_ctr = 0;
+    int prev_ys = -1;
     while (units.next(args.seg, u)) {
       if (__ldg(args.ranks + u.slot) <= 0) continue;
       const float scale = __ldg(args.scales + u.slot);
       const int n_base = u.tile * kExpandNT + h * 64;
       const int ncols = min(64, args.N - n_base);  // multiple of 8 (N % 8 == 0)
       const bool active = (r >= u.t0) && (r < u.t1) && ncols > 0;
-      uint4 yv[8];
-      uint4* yrow = nullptr;
-      if (active) {
-        const int64_t tok = __ldg(args.seg.token_index + u.item_start + r);
-        yrow = reinterpret_cast<uint4*>(args.y + (tok * args.N + n_base) * 2);
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          if (c * 8 < ncols) yv[c] = yrow[c];
-      }
       const int ab = unit_ctr & 1;
+      const int ys = unit_ctr % YS;
       if (!mbar_wait_warp(&afull[ab], (unit_ctr >> 1) & 1, abort_flag)) break;
       tc_fence_after();
       uint32_t acc[4][16];
@@ -543,11 +559,16 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&aempty[ab]);
+      if (!mbar_wait_warp(&yfull[ys], (unit_ctr / YS) & 1, abort_flag)) break;
+      const uint32_t yrow = smem_u32(y_base + ys * Cfg::kYStageBytes) + r * kYRowBytes + h * 128;
       if (active) {
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           if (c * 8 < ncols) {
-            uint32_t in[4] = {yv[c].x, yv[c].y, yv[c].z, yv[c].w};
+            uint32_t in[4];
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(in[0]), "=r"(in[1]), "=r"(in[2]), "=r"(in[3])
+                         : "r"(yrow + c * 16));
             uint32_t out[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -558,12 +579,24 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
               const float y1 = E::to_f((uint16_t)(in[i] >> 16)) + scale * a1;
               out[i] = (uint32_t)E::from_f(y0) | ((uint32_t)E::from_f(y1) << 16);
             }
-            yrow[c] = make_uint4(out[0], out[1], out[2], out[3]);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(yrow + c * 16),
+                         "r"(out[0]), "r"(out[1]), "r"(out[2]), "r"(out[3])
+                         : "memory");
           }
         }
+        fence_proxy_async_smem();
+        const int64_t tok = __ldg(args.seg.token_index + u.item_start + r);
+        bulk_store(args.y + (tok * args.N + n_base) * 2, yrow, (uint32_t)ncols * 2u);
       }
+      bulk_commit();
+      // the previous unit's stage is free once this thread's stores from it were read
+      bulk_wait_read<1>();
+      __syncwarp();
+      if (lane == 0 && prev_ys >= 0) mbar_arrive(&yempty[prev_ys]);
+      prev_ys = ys;
       ++unit_ctr;
     }
+    bulk_wait<0>();
   }
 
   __syncthreads();

@@ -62,8 +62,11 @@ def _random_adapter(modules, r, seed, subset=None, scale=0.3):
 
 def _closed_form_model(base, adapters_by_row, x_kwargs):
     """Runs `base` with forward hooks adding (alpha/r) x A^T B^T per row — the
-    PEFT arithmetic restated — on the same device."""
+    PEFT arithmetic restated — on the same device, to the valid (unpadded)
+    tokens of each row as the reference does (layers.py:127-133)."""
     hooks = []
+    mask = x_kwargs.get("attention_mask")
+    lens = mask.sum(-1).tolist() if mask is not None else None
 
     def make_hook(name):
         def hook(mod, inp, out):
@@ -73,7 +76,8 @@ def _closed_form_model(base, adapters_by_row, x_kwargs):
                 if ad is None or name not in ad["layers"]:
                     continue
                 A, B, s = ad["layers"][name]
-                out[b] = out[b] + s * (x[b] @ A.t().to(x) @ B.t().to(x))
+                L = x.shape[1] if lens is None else int(lens[b])
+                out[b, :L] = out[b, :L] + s * (x[b, :L] @ A.t().to(x) @ B.t().to(x))
             return out
         return hook
 
