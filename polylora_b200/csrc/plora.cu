@@ -43,6 +43,9 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 constexpr int kMaxDevices = 64;
 
+// Shared-memory bytes of the per-slot table staged by the tensor-core kernels.
+size_t tab_bytes(int32_t ns) { return ((size_t)(3 * ns + 1) * 4 + 15) & ~(size_t)15; }
+
 struct DeviceInfo {
   int sm_count = 0;
   bool attrs_set = false;
@@ -65,8 +68,10 @@ int device_info(DeviceInfo** out) {
     if (major != 10 || minor != 0)
       return fail(PLORA_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", dev,
                   major, minor);
-#define SET_SMEM(kern, bytes) \
-  PLORA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), #kern)
+#define SET_SMEM(kern, bytes)                                                                  \
+  PLORA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,           \
+                                  (int)((bytes) + tab_bytes(kTcMaxSlots))),                     \
+             #kern)
     SET_SMEM((sgmv_shrink_tc_kernel<16, true>), ShrinkCfg<16>::kSmemBytes);
     SET_SMEM((sgmv_shrink_tc_kernel<32, true>), ShrinkCfg<32>::kSmemBytes);
     SET_SMEM((sgmv_shrink_tc_kernel<64, true>), ShrinkCfg<64>::kSmemBytes);
@@ -214,7 +219,8 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
   args.K = (int32_t)K;
   args.R = (int32_t)R;
   args.stack_num = stack_num;
-  const bool tc = dtype != PLORA_DTYPE_F32 && tc_rank_ok(R) && K % 8 == 0 && aligned16(x) &&
+  const bool tc = dtype != PLORA_DTYPE_F32 && tc_rank_ok(R) && K % 8 == 0 &&
+                  seg.num_slots <= kTcMaxSlots && aligned16(x) &&
                   aligned16(a) && aligned16(tmp);
   if (tc) {
     CUtensorMap map, xmap;
@@ -228,13 +234,14 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
                           CU_TENSOR_MAP_SWIZZLE_128B)))
       return st;
     const dim3 grid(di->sm_count), block(kShrinkThreads);
+    const size_t tb = tab_bytes(seg.num_slots);
     const bool bf = dtype == PLORA_DTYPE_BF16;
 #define LAUNCH_SHRINK(RPV)                                                               \
   if (bf)                                                                                \
-    sgmv_shrink_tc_kernel<RPV, true><<<grid, block, ShrinkCfg<RPV>::kSmemBytes, stream>>>( \
+    sgmv_shrink_tc_kernel<RPV, true><<<grid, block, ShrinkCfg<RPV>::kSmemBytes + tb, stream>>>( \
         map, xmap, args);                                                                \
   else                                                                                   \
-    sgmv_shrink_tc_kernel<RPV, false><<<grid, block, ShrinkCfg<RPV>::kSmemBytes, stream>>>( \
+    sgmv_shrink_tc_kernel<RPV, false><<<grid, block, ShrinkCfg<RPV>::kSmemBytes + tb, stream>>>( \
         map, xmap, args);
     if (R == 16) {
       LAUNCH_SHRINK(16)
@@ -271,7 +278,8 @@ int expand_impl(const void* tmp, const void* b, void* y, const int32_t* ranks, c
   args.seg = seg;
   args.R = (int32_t)R;
   args.N = (int32_t)N;
-  const bool tc = dtype != PLORA_DTYPE_F32 && tc_rank_ok(R) && N % 8 == 0 && aligned16(tmp) &&
+  const bool tc = dtype != PLORA_DTYPE_F32 && tc_rank_ok(R) && N % 8 == 0 &&
+                  seg.num_slots <= kTcMaxSlots && aligned16(tmp) &&
                   aligned16(b) && aligned16(y);
   if (tc) {
     CUtensorMap map;
@@ -279,13 +287,14 @@ int expand_impl(const void* tmp, const void* b, void* y, const int32_t* ranks, c
                           (uint32_t)R, CU_TENSOR_MAP_SWIZZLE_128B)))
       return st;
     const dim3 grid(di->sm_count), block(kExpandThreads);
+    const size_t tb = tab_bytes(seg.num_slots);
     const bool bf = dtype == PLORA_DTYPE_BF16;
 #define LAUNCH_EXPAND(RPV)                                                               \
   if (bf)                                                                                \
-    sgmv_expand_tc_kernel<RPV, true><<<grid, block, ExpandCfg<RPV>::kSmemBytes, stream>>>( \
+    sgmv_expand_tc_kernel<RPV, true><<<grid, block, ExpandCfg<RPV>::kSmemBytes + tb, stream>>>( \
         map, args);                                                                      \
   else                                                                                   \
-    sgmv_expand_tc_kernel<RPV, false><<<grid, block, ExpandCfg<RPV>::kSmemBytes, stream>>>( \
+    sgmv_expand_tc_kernel<RPV, false><<<grid, block, ExpandCfg<RPV>::kSmemBytes + tb, stream>>>( \
         map, args);
     if (R == 16) {
       LAUNCH_EXPAND(16)

@@ -52,20 +52,48 @@ struct ExpandArgs {
   int32_t R, N;
 };
 
+// Per-slot metadata staged in shared memory once per CTA (slot_start, ranks
+// and, for the expand, scales), so the schedule never waits on global loads.
+constexpr int kTcMaxSlots = 1024;  // slot-count limit of the tensor-core kernels
+
+struct SlotTab {
+  const int32_t* ss;  // (num_slots + 1) slot_start
+  const int32_t* rk;  // (num_slots) ranks of this module
+  const float* sc;    // (num_slots) scales (expand only)
+  int ns;
+};
+
+__device__ __forceinline__ size_t slot_tab_bytes(int ns) { return (size_t)(3 * ns + 1) * 4; }
+
+// Copies the table into `dst` (all threads of the CTA; caller syncs).
+__device__ __forceinline__ SlotTab stage_slot_tab(const SegTable& t, const int32_t* ranks,
+                                                  const float* scales, int32_t* dst) {
+  const int ns = t.num_slots;
+  int32_t* ss = dst;
+  int32_t* rk = dst + ns + 1;
+  float* sc = reinterpret_cast<float*>(dst + 2 * ns + 1);
+  for (int i = threadIdx.x; i <= ns; i += blockDim.x) ss[i] = __ldg(t.slot_start + i);
+  for (int i = threadIdx.x; i < ns; i += blockDim.x) {
+    rk[i] = __ldg(ranks + i);
+    sc[i] = scales ? __ldg(scales + i) : 0.f;
+  }
+  return SlotTab{ss, rk, sc, ns};
+}
+
 // Items of the shrink: maximal runs of <= 128 tokens of one slot inside the
 // CTA's contiguous share [p, end) of the slot-ordered token list.
 struct ShrinkItems {
   int64_t p, end;
   int slot;
-  __device__ void init(const SegTable& t, int64_t b, int64_t e) {
+  __device__ void init(const SlotTab& t, int64_t b, int64_t e) {
     p = b;
     end = e;
-    slot = (b < e) ? slot_of_position(t.slot_start, t.num_slots, b) : 0;
+    slot = (b < e) ? slot_of_position(t.ss, t.ns, b) : 0;
   }
-  __device__ bool next(const SegTable& t, int& s, int64_t& start, int& cnt) {
+  __device__ bool next(const SlotTab& t, int& s, int64_t& start, int& cnt) {
     if (p >= end) return false;
-    while ((int64_t)__ldg(t.slot_start + slot + 1) <= p) ++slot;
-    const int64_t lim = min(end, (int64_t)__ldg(t.slot_start + slot + 1));
+    while ((int64_t)t.ss[slot + 1] <= p) ++slot;
+    const int64_t lim = min(end, (int64_t)t.ss[slot + 1]);
     cnt = (int)min(lim - p, (int64_t)kTileM);
     s = slot;
     start = p;
@@ -77,7 +105,8 @@ struct ShrinkItems {
 // Units of the expand: the work space is (token, 128-column tile) pairs laid
 // out slot-major, then 128-token item, then column tile, then token.  A CTA
 // takes a contiguous share; a unit is one (item, column tile) with the token
-// sub-range [t0, t1) of the item that falls inside the share.
+// sub-range [t0, t1) of the item that falls inside the share.  The cursor
+// advances incrementally; only init() searches.
 struct ExpandUnit {
   int slot;
   int64_t item_start;  // first position of the item in token_index
@@ -89,37 +118,57 @@ struct ExpandUnit {
 struct ExpandUnits {
   int64_t w, wend;
   int ntiles;
-  __device__ void init(int64_t b, int64_t e, int nt) {
+  int s, item, cnt, tile, t;
+  int64_t s0, cnt_s;
+  __device__ void init(const SlotTab& tab, int64_t b, int64_t e, int nt) {
     w = b;
     wend = e;
     ntiles = nt;
-  }
-  __device__ bool next(const SegTable& t, ExpandUnit& u) {
-    if (w >= wend) return false;
-    // largest slot s with slot_start[s] * ntiles <= w
-    int lo = 0, hi = t.num_slots - 1;
+    if (b >= e) return;
+    int lo = 0, hi = tab.ns - 1;  // largest s with ss[s] * nt <= w
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
-      if ((int64_t)__ldg(t.slot_start + mid) * ntiles <= w)
+      if ((int64_t)tab.ss[mid] * nt <= w)
         lo = mid;
       else
         hi = mid - 1;
     }
-    const int s = lo;
-    const int64_t s0 = __ldg(t.slot_start + s);
-    const int64_t cnt_s = (int64_t)__ldg(t.slot_start + s + 1) - s0;
-    const int64_t local = w - s0 * ntiles;
-    const int64_t item = local / ((int64_t)kTileM * ntiles);
-    const int cnt = (int)min((int64_t)kTileM, cnt_s - item * kTileM);
-    const int64_t within = local - item * kTileM * ntiles;
+    s = lo;
+    s0 = tab.ss[s];
+    cnt_s = (int64_t)tab.ss[s + 1] - s0;
+    const int64_t local = w - s0 * nt;
+    item = (int)(local / ((int64_t)kTileM * nt));
+    cnt = (int)min((int64_t)kTileM, cnt_s - (int64_t)item * kTileM);
+    const int64_t within = local - (int64_t)item * kTileM * nt;
+    tile = (int)(within / cnt);
+    t = (int)(within % cnt);
+  }
+  __device__ bool next(const SlotTab& tab, ExpandUnit& u) {
+    if (w >= wend) return false;
     u.slot = s;
-    u.item_start = s0 + item * kTileM;
+    u.item_start = s0 + (int64_t)item * kTileM;
     u.cnt = cnt;
-    u.tile = (int)(within / cnt);
-    u.t0 = (int)(within % cnt);
-    const int64_t take = min((int64_t)(cnt - u.t0), wend - w);
-    u.t1 = u.t0 + (int)take;
+    u.tile = tile;
+    u.t0 = t;
+    const int64_t take = min((int64_t)(cnt - t), wend - w);
+    u.t1 = t + (int)take;
     w += take;
+    t = u.t1;
+    if (w < wend && t == cnt) {  // advance to the next (item, tile)
+      t = 0;
+      if (++tile == ntiles) {
+        tile = 0;
+        if ((int64_t)(++item) * kTileM >= cnt_s) {
+          item = 0;
+          do {
+            ++s;
+          } while (tab.ss[s + 1] == tab.ss[s]);  // w < wend: a later non-empty slot exists
+          s0 = tab.ss[s];
+          cnt_s = (int64_t)tab.ss[s + 1] - s0;
+        }
+        cnt = (int)min((int64_t)kTileM, cnt_s - (int64_t)item * kTileM);
+      }
+    }
     return true;
   }
 };
@@ -148,16 +197,14 @@ struct ShrinkCfg {
   static constexpr int kTmemCols = (2 * RP < 32) ? 32 : 2 * RP;
   static constexpr uint32_t kALayout = RP == 16 ? kSwizzle32 : (RP == 32 ? kSwizzle64 : kSwizzle128);
   static constexpr uint32_t kAAtom = 8 * RP * 2;  // 8 K-rows of one swizzle atom
-  static constexpr int kTokBytes = kTileM * 4;
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes = 1024 + kShrinkStages * kStageBytes + kTokBytes + kBarrierBytes;
-  static_assert(kSmemBytes <= 227 * 1024, "shrink shared memory");
+  // + slot table (3 * num_slots + 1 ints), sized at launch
+  static constexpr int kSmemBytes = 1024 + kShrinkStages * kStageBytes + kBarrierBytes;
 };
 
 // tmp[t, :] = x[t, :] @ A[slot(t)] for the active tokens of the table.
-//   warp 0: producer — per item, stages token ids; lane 0 then issues, per
-//           64-wide K chunk, one TMA of A[slot] (64 x RP) and ceil(cnt/4)
-//           gather4 loads of the token rows of x.
+//   warp 0: producer — per 64-wide K chunk, lane 0 loads A[slot] (64 x RP) by
+//           TMA and lane g gathers token rows 4g..4g+3 of the item (gather4).
 //   warp 1: TMEM owner; lane 0 issues 4 UMMAs (128 x RP x 16) per chunk.
 //   warps 2-5: epilogue — TMEM -> registers -> bf16/fp16 rows of tmp.
 template <int RP, bool BF16>
@@ -169,14 +216,14 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   constexpr int S = kShrinkStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  int32_t* tok_s = reinterpret_cast<int32_t*>(smem + S * Cfg::kStageBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes + Cfg::kTokBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int32_t* tab_mem = reinterpret_cast<int32_t*>(smem + S * Cfg::kStageBytes + Cfg::kBarrierBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -185,6 +232,7 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
   if (begin >= end) return;  // uniform across the CTA
 
+  const SlotTab tab = stage_slot_tab(args.seg, args.ranks, nullptr, tab_mem);
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);  // producer's arrive.expect_tx
@@ -209,45 +257,42 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   const int nkc = (args.K + kShrinkKC - 1) / kShrinkKC;
 
   ShrinkItems items;
-  items.init(args.seg, begin, end);
+  items.init(tab, begin, end);
   int s, cnt;
   int64_t start;
 
   if (warp == 0) {
-    // ---------------- producer: A chunk by TMA, token rows by gather4
+    // ---------------- producer: A chunk by TMA (lane 0), token rows by gather4 (lane g)
     if (lane == 0) {
       prefetch_tmap(&tmap_a);
       prefetch_tmap(&tmap_x);
     }
     uint32_t ctr = 0;
     bool ok = true;
-    while (ok && items.next(args.seg, s, start, cnt)) {
-      if (__ldg(args.ranks + s) <= 0) continue;
-      __syncwarp();
+    while (ok && items.next(tab, s, start, cnt)) {
+      if (tab.rk[s] <= 0) continue;
+      int tok[4];
 #pragma unroll
-      for (int i = 0; i < kTileM / 32; ++i) {
-        const int r = lane + 32 * i;
-        tok_s[r] = __ldg(args.seg.token_index + start + min(r, cnt - 1));  // pad with the last row
-      }
-      __syncwarp();
-      if (lane == 0) {
-        const int ngroups = (cnt + 3) >> 2;
-        const uint32_t tx = Cfg::kABytes + ngroups * 4 * 128;
-        for (int kc = 0; kc < nkc; ++kc, ++ctr) {
-          const int st = ctr % S;
-          if (!mbar_wait(&empty[st], ((ctr / S) & 1) ^ 1, abort_flag)) {
-            ok = false;
-            break;
+      for (int i = 0; i < 4; ++i)  // rows 4*lane .. 4*lane+3, padded with the last row
+        tok[i] = __ldg(args.seg.token_index + start + min(4 * lane + i, cnt - 1));
+      const int ngroups = (cnt + 3) >> 2;
+      const uint32_t tx = Cfg::kABytes + ngroups * 4 * 128;
+      for (int kc = 0; kc < nkc; ++kc, ++ctr) {
+        const int st = ctr % S;
+        const uint32_t xs = smem_u32(smem + st * Cfg::kStageBytes);
+        if (lane == 0) {
+          ok = mbar_wait(&empty[st], ((ctr / S) & 1) ^ 1, abort_flag);
+          if (ok) {
+            mbar_arrive_expect_tx(&full[st], tx);
+            tma_load_3d(xs + Cfg::kXBytes, &tmap_a, &full[st], 0, kc * kShrinkKC, s);
           }
-          const uint32_t xs = smem_u32(smem + st * Cfg::kStageBytes);
-          mbar_arrive_expect_tx(&full[st], tx);
-          tma_load_3d(xs + Cfg::kXBytes, &tmap_a, &full[st], 0, kc * kShrinkKC, s);
-          for (int g = 0; g < ngroups; ++g)
-            tma_gather4(xs + g * 512, &tmap_x, &full[st], kc * kShrinkKC, tok_s[4 * g],
-                        tok_s[4 * g + 1], tok_s[4 * g + 2], tok_s[4 * g + 3]);
         }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (lane < ngroups)
+          tma_gather4(xs + lane * 512, &tmap_x, &full[st], kc * kShrinkKC, tok[0], tok[1], tok[2],
+                      tok[3]);
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
     }
   } else if (warp == 1) {
     // ---------------- MMA issue (one thread)
@@ -255,8 +300,8 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
       const uint32_t idesc = idesc_f16(BF16, false, true, kTileM, RP);
       uint32_t ctr = 0, item_ctr = 0;
       bool issued = false, ok = true;
-      while (ok && items.next(args.seg, s, start, cnt)) {
-        if (__ldg(args.ranks + s) <= 0) continue;
+      while (ok && items.next(tab, s, start, cnt)) {
+        if (tab.rk[s] <= 0) continue;
         const int ab = item_ctr & 1;
         if (!mbar_wait(&acc_empty[ab], ((item_ctr >> 1) & 1) ^ 1, abort_flag)) break;
         tc_fence_after();
@@ -292,10 +337,12 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   } else {
     // ---------------- epilogue: TMEM -> registers -> tmp rows
     const int q = warp & 3;  // TMEM lane quarter of this warp
+    const int r = q * 32 + lane;
     uint32_t item_ctr = 0;
-    while (items.next(args.seg, s, start, cnt)) {
-      const int rank = __ldg(args.ranks + s);
+    while (items.next(tab, s, start, cnt)) {
+      const int rank = tab.rk[s];
       if (rank <= 0) continue;
+      const int64_t tok = (r < cnt) ? __ldg(args.seg.token_index + start + r) : 0;
       const int ab = item_ctr & 1;
       if (!mbar_wait_warp(&acc_full[ab], (item_ctr >> 1) & 1, abort_flag)) break;
       tc_fence_after();
@@ -307,10 +354,8 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[ab]);
-      const int r = q * 32 + lane;
       if (r < cnt) {
         const int n_eff = min(rank * args.stack_num, args.R);
-        const int64_t tok = __ldg(args.seg.token_index + start + r);
         uint4* dst = reinterpret_cast<uint4*>(args.tmp + tok * args.R * 2);
 #pragma unroll
         for (int ch = 0; ch < RP / 8; ++ch) {
@@ -348,9 +393,9 @@ struct ExpandCfg {
   static constexpr int kYStages = RP >= 64 ? 3 : 4;  // y row-tile stages
   static constexpr int kTmemCols = 2 * kExpandNT;
   static constexpr int kBarrierBytes = 512;
+  // + slot table (3 * num_slots + 1 ints), sized at launch
   static constexpr int kSmemBytes = 1024 + kBStages * kBStageStride + 2 * kTmpBytes +
                                     kYStages * kYStageBytes + kBarrierBytes;
-  static_assert(kSmemBytes <= 227 * 1024, "expand shared memory");
 };
 
 // y[t, :] += scale[slot(t)] * tmp[t, :] @ B[slot(t)] (in place).
@@ -383,6 +428,7 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
   uint64_t* drain = aempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int32_t* tab_mem = reinterpret_cast<int32_t*>(y_base + YS * Cfg::kYStageBytes + Cfg::kBarrierBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -392,6 +438,7 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
   const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
   if (begin >= end) return;
 
+  const SlotTab tab = stage_slot_tab(args.seg, args.ranks, args.scales, tab_mem);
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&bfull[i], 1);
@@ -421,16 +468,26 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   ExpandUnits units;
-  units.init(begin, end, ntiles);
+  units.init(tab, begin, end, ntiles);
   ExpandUnit u;
 
   if (warp == 0) {
     // ---------------- producer: B tile by TMA, y rows by bulk copies
     if (lane == 0) prefetch_tmap(&tmap_b);
     uint32_t bctr = 0, yctr = 0;
+    int64_t prev = -1;
+    int64_t tok[4] = {0, 0, 0, 0};  // token of rows lane + 32 i of the current item
     bool ok = true;
-    while (ok && units.next(args.seg, u)) {
-      if (__ldg(args.ranks + u.slot) <= 0) continue;
+    while (ok && units.next(tab, u)) {
+      if (tab.rk[u.slot] <= 0) continue;
+      if (u.item_start != prev) {
+        prev = u.item_start;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = lane + 32 * i;
+          tok[i] = r < u.cnt ? __ldg(args.seg.token_index + u.item_start + r) : 0;
+        }
+      }
       const int n0 = u.tile * kExpandNT;
       if (lane == 0) {
         const int st = bctr % S;
@@ -451,9 +508,12 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
       if (lane == 0) mbar_arrive_expect_tx(&yfull[ys], row_bytes * (uint32_t)(u.t1 - u.t0));
       __syncwarp();
       const uint32_t ybuf = smem_u32(y_base + ys * Cfg::kYStageBytes);
-      for (int r = u.t0 + lane; r < u.t1; r += 32) {
-        const int64_t tok = __ldg(args.seg.token_index + u.item_start + r);
-        bulk_load(ybuf + r * kYRowBytes, args.y + (tok * args.N + n0) * 2, row_bytes, &yfull[ys]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = lane + 32 * i;
+        if (r >= u.t0 && r < u.t1)
+          bulk_load(ybuf + r * kYRowBytes, args.y + (tok[i] * args.N + n0) * 2, row_bytes,
+                    &yfull[ys]);
       }
       ++yctr;
     }
@@ -461,8 +521,8 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
     // ---------------- tmp gather: item rows -> K-major (no swizzle) tile
     uint32_t item_ctr = 0;
     int64_t prev = -1;
-    while (units.next(args.seg, u)) {
-      const int rank = __ldg(args.ranks + u.slot);
+    while (units.next(tab, u)) {
+      const int rank = tab.rk[u.slot];
       if (rank <= 0 || u.item_start == prev) continue;
       prev = u.item_start;
       const int tb = item_ctr & 1;
@@ -496,8 +556,8 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
       int64_t prev = -1;
       int tb = 0;
       bool issued = false, ok = true;
-      while (ok && units.next(args.seg, u)) {
-        if (__ldg(args.ranks + u.slot) <= 0) continue;
+      while (ok && units.next(tab, u)) {
+        if (tab.rk[u.slot] <= 0) continue;
         if (u.item_start != prev) {
           if (prev >= 0) umma_commit(&tempty[tb]);  // previous tile free once its MMAs finish
           prev = u.item_start;
@@ -540,9 +600,14 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
     const int r = q * 32 + lane;
     uint32_t unit_ctr = 0;
     int prev_ys = -1;
-    while (units.next(args.seg, u)) {
-      if (__ldg(args.ranks + u.slot) <= 0) continue;
-      const float scale = __ldg(args.scales + u.slot);
+    int64_t prev = -1, tok = 0;
+    while (units.next(tab, u)) {
+      if (tab.rk[u.slot] <= 0) continue;
+      if (u.item_start != prev) {
+        prev = u.item_start;
+        tok = (r < u.cnt) ? __ldg(args.seg.token_index + u.item_start + r) : 0;
+      }
+      const float scale = tab.sc[u.slot];
       const int n_base = u.tile * kExpandNT + h * 64;
       const int ncols = min(64, args.N - n_base);  // multiple of 8 (N % 8 == 0)
       const bool active = (r >= u.t0) && (r < u.t1) && ncols > 0;
@@ -585,7 +650,6 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
           }
         }
         fence_proxy_async_smem();
-        const int64_t tok = __ldg(args.seg.token_index + u.item_start + r);
         bulk_store(args.y + (tok * args.N + n_base) * 2, yrow, (uint32_t)ncols * 2u);
       }
       bulk_commit();
