@@ -124,7 +124,7 @@ int make_map_3d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, uint
 }
 
 // 2-D tiled map over a contiguous (d1, d0) 16-bit tensor.
-int make_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, uint64_t d1,
+[[maybe_unused]] int make_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, uint64_t d1,
                 uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz) {
   auto enc = tensor_map_encoder();
   if (!enc) return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -223,26 +223,24 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
                   seg.num_slots <= kTcMaxSlots && aligned16(x) &&
                   aligned16(a) && aligned16(tmp);
   if (tc) {
-    CUtensorMap map, xmap;
+    CUtensorMap map;
     const CUtensorMapSwizzle swz = R == 16   ? CU_TENSOR_MAP_SWIZZLE_32B
                                    : R == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
                                              : CU_TENSOR_MAP_SWIZZLE_128B;
     if ((st = make_map_3d(&map, a, dtype, (uint64_t)R, (uint64_t)K, (uint64_t)seg.num_slots,
                           (uint32_t)R, kShrinkKC, swz)))
       return st;
-    if ((st = make_map_2d(&xmap, x, dtype, (uint64_t)K, (uint64_t)num_tokens, kShrinkKC, 1,
-                          CU_TENSOR_MAP_SWIZZLE_128B)))
-      return st;
+    (void)num_tokens;
     const dim3 grid(di->sm_count), block(kShrinkThreads);
     const size_t tb = tab_bytes(seg.num_slots);
     const bool bf = dtype == PLORA_DTYPE_BF16;
 #define LAUNCH_SHRINK(RPV)                                                               \
   if (bf)                                                                                \
     sgmv_shrink_tc_kernel<RPV, true><<<grid, block, ShrinkCfg<RPV>::kSmemBytes + tb, stream>>>( \
-        map, xmap, args);                                                                \
+        map, args);                                                                \
   else                                                                                   \
     sgmv_shrink_tc_kernel<RPV, false><<<grid, block, ShrinkCfg<RPV>::kSmemBytes + tb, stream>>>( \
-        map, xmap, args);
+        map, args);
     if (R == 16) {
       LAUNCH_SHRINK(16)
     } else if (R == 32) {

@@ -22,10 +22,12 @@ namespace plora {
 constexpr int kTileM = 128;        // tokens per MMA tile (TMEM lanes)
 constexpr int kShrinkKC = 64;      // K elements per shrink stage (one 128-byte row)
 constexpr int kShrinkStages = 8;
+constexpr int kShrinkDepth = 6;    // cp.async groups a gather thread keeps in flight (<= stages)
 constexpr int kExpandNT = 128;     // output columns per expand unit
 constexpr int kYRowBytes = kExpandNT * 2 + 16;  // padded smem row: conflict-free row-per-thread access
-constexpr int kShrinkThreads = 192;  // TMA producer, MMA, 4 epilogue warps
-constexpr int kExpandThreads = 384;  // B/y producer, tmp gather, MMA, idle, 8 epilogue warps
+constexpr int kExpandDepth = 3;    // y-row cp.async groups a loader thread keeps in flight
+constexpr int kShrinkThreads = 320;  // 4 gather warps, A TMA, MMA, 4 epilogue warps
+constexpr int kExpandThreads = 512;  // B TMA, MMA, tmp gather, idle, 4 y-load warps, 8 epilogue warps
 
 struct SegTable {
   const int32_t* slot_start;   // (num_slots + 1)
@@ -200,20 +202,24 @@ struct ShrinkCfg {
   static constexpr int kBarrierBytes = 256;
   // + slot table (3 * num_slots + 1 ints), sized at launch
   static constexpr int kSmemBytes = 1024 + kShrinkStages * kStageBytes + kBarrierBytes;
+  static_assert(kShrinkDepth <= kShrinkStages, "gather depth must not exceed the stages");
 };
 
 // tmp[t, :] = x[t, :] @ A[slot(t)] for the active tokens of the table.
-//   warp 0: producer — per 64-wide K chunk, lane 0 loads A[slot] (64 x RP) by
-//           TMA and lane g gathers token rows 4g..4g+3 of the item (gather4).
-//   warp 1: TMEM owner; lane 0 issues 4 UMMAs (128 x RP x 16) per chunk.
-//   warps 2-5: epilogue — TMEM -> registers -> bf16/fp16 rows of tmp.
+//   warps 0-3: token-row gather — 16-byte cp.async pieces into the 128-byte
+//           swizzled K-major stage tile (four 128-byte rows per warp
+//           instruction); each thread keeps kShrinkDepth stages in flight and
+//           signals a stage once its group has landed.
+//   warp 4: TMEM owner; lane 0 loads A[slot] (64 x RP) per stage by TMA.
+//   warp 5: lane 0 issues 4 UMMAs (128 x RP x 16) per stage.
+//   warps 6-9: epilogue — TMEM -> registers -> bf16/fp16 rows of tmp.
 template <int RP, bool BF16>
 __global__ void __launch_bounds__(kShrinkThreads, 1)
-    sgmv_shrink_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                          const __grid_constant__ CUtensorMap tmap_x, const ShrinkArgs args) {
+    sgmv_shrink_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const ShrinkArgs args) {
   using Cfg = ShrinkCfg<RP>;
   using E = Elem<BF16>;
   constexpr int S = kShrinkStages;
+  constexpr int D = kShrinkDepth;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
@@ -235,7 +241,7 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   const SlotTab tab = stage_slot_tab(args.seg, args.ranks, nullptr, tab_mem);
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&full[i], 1);  // producer's arrive.expect_tx
+      mbar_init(&full[i], 128 + 1);  // 128 gather threads + the A loader's expect_tx
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -246,7 +252,7 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == 4) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
@@ -261,40 +267,74 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   int s, cnt;
   int64_t start;
 
-  if (warp == 0) {
-    // ---------------- producer: A chunk by TMA (lane 0), token rows by gather4 (lane g)
-    if (lane == 0) {
-      prefetch_tmap(&tmap_a);
-      prefetch_tmap(&tmap_x);
-    }
-    uint32_t ctr = 0;
+  if (warp < 4) {
+    // ---------------- token-row gather
+    const int t = threadIdx.x;  // 0..127
+    const int c = t & 7;        // 16-byte piece of the 128-byte row chunk
+    const int r0 = t >> 3;      // rows r0 + 16 j
+    uint32_t ctr = 0, signaled = 0;
     bool ok = true;
     while (ok && items.next(tab, s, start, cnt)) {
       if (tab.rk[s] <= 0) continue;
-      int tok[4];
+      const uint8_t* rowp[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)  // rows 4*lane .. 4*lane+3, padded with the last row
-        tok[i] = __ldg(args.seg.token_index + start + min(4 * lane + i, cnt - 1));
-      const int ngroups = (cnt + 3) >> 2;
-      const uint32_t tx = Cfg::kABytes + ngroups * 4 * 128;
-      for (int kc = 0; kc < nkc; ++kc, ++ctr) {
+      for (int j = 0; j < 8; ++j) {
+        const int r = r0 + 16 * j;
+        rowp[j] = (r < cnt) ? args.x + (int64_t)__ldg(args.seg.token_index + start + r) * args.K * 2
+                            : nullptr;
+      }
+      for (int kc = 0; kc < nkc; ++kc) {
         const int st = ctr % S;
+        if (!mbar_wait(&empty[st], ((ctr / S) & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int k0 = kc * kShrinkKC + c * 8;
+        const int kleft = args.K - k0;
+        const uint32_t bytes = kleft >= 8 ? 16u : (kleft > 0 ? (uint32_t)kleft * 2u : 0u);
         const uint32_t xs = smem_u32(smem + st * Cfg::kStageBytes);
-        if (lane == 0) {
-          ok = mbar_wait(&empty[st], ((ctr / S) & 1) ^ 1, abort_flag);
-          if (ok) {
-            mbar_arrive_expect_tx(&full[st], tx);
-            tma_load_3d(xs + Cfg::kXBytes, &tmap_a, &full[st], 0, kc * kShrinkKC, s);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (rowp[j] != nullptr) {
+            const int r = r0 + 16 * j;
+            cp_async_16(xs + r * 128 + ((c ^ (r & 7)) << 4), bytes ? rowp[j] + (int64_t)k0 * 2 : rowp[j],
+                        bytes);
           }
         }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        if (lane < ngroups)
-          tma_gather4(xs + lane * 512, &tmap_x, &full[st], kc * kShrinkKC, tok[0], tok[1], tok[2],
-                      tok[3]);
+        cp_async_commit();
+        ++ctr;
+        if (ctr - signaled == D) {  // oldest group must land before its stage is handed over
+          cp_async_wait_group<D - 1>();
+          fence_proxy_async_smem();
+          mbar_arrive(&full[signaled % S]);
+          ++signaled;
+        }
       }
     }
-  } else if (warp == 1) {
+    cp_async_wait_group<0>();
+    fence_proxy_async_smem();
+    for (; signaled < ctr; ++signaled) mbar_arrive(&full[signaled % S]);
+  } else if (warp == 4) {
+    // ---------------- A chunk loader (TMA)
+    if (lane == 0) {
+      prefetch_tmap(&tmap_a);
+      uint32_t ctr = 0;
+      bool ok = true;
+      while (ok && items.next(tab, s, start, cnt)) {
+        if (tab.rk[s] <= 0) continue;
+        for (int kc = 0; kc < nkc; ++kc, ++ctr) {
+          const int st = ctr % S;
+          if (!mbar_wait(&empty[st], ((ctr / S) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[st], Cfg::kABytes);
+          tma_load_3d(smem_u32(smem + st * Cfg::kStageBytes + Cfg::kXBytes), &tmap_a, &full[st], 0,
+                      kc * kShrinkKC, s);
+        }
+      }
+    }
+  } else if (warp == 5) {
     // ---------------- MMA issue (one thread)
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(BF16, false, true, kTileM, RP);
@@ -375,7 +415,7 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   }
 
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 4) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
@@ -393,18 +433,22 @@ struct ExpandCfg {
   static constexpr int kYStages = RP >= 64 ? 3 : 4;  // y row-tile stages
   static constexpr int kTmemCols = 2 * kExpandNT;
   static constexpr int kBarrierBytes = 512;
+  static constexpr int kTokBytes = 2 * kTileM * 4;
   // + slot table (3 * num_slots + 1 ints), sized at launch
   static constexpr int kSmemBytes = 1024 + kBStages * kBStageStride + 2 * kTmpBytes +
-                                    kYStages * kYStageBytes + kBarrierBytes;
+                                    kYStages * kYStageBytes + kBarrierBytes + kTokBytes;
+  static_assert(kExpandDepth <= kYStages, "y depth must not exceed the stages");
 };
 
 // y[t, :] += scale[slot(t)] * tmp[t, :] @ B[slot(t)] (in place).
-//   warp 0: producer — lane 0 loads the B tile (RP x 128) by TMA; all lanes
-//           bulk-copy the unit's y rows (<= 256 B each) into padded smem rows.
-//   warp 1: gathers the item's tmp rows (K-major, no swizzle) with cp.async.
-//   warp 2: TMEM owner; lane 0 issues RP/16 UMMAs (128 x 128 x 16) per unit.
-//   warps 4-11: epilogue — thread = token row, 64 columns: TMEM + smem y ->
-//           smem y, then a bulk store of the row segment back to global.
+//   warp 0: lane 0 loads the B tile (RP x 128) per unit by TMA.
+//   warp 1: TMEM owner; lane 0 issues RP/16 UMMAs (128 x 128 x 16) per unit.
+//   warp 2: gathers the item's tmp rows (K-major, no swizzle) with cp.async.
+//   warps 4-7: y-row loaders — coalesced 16-byte cp.async (16 threads per
+//           256-byte row segment) into padded smem rows, kExpandDepth units
+//           in flight per thread.
+//   warps 8-15: epilogue — thread = token row, 64 columns: TMEM + smem y ->
+//           smem y; then all 256 threads write the tile back coalesced.
 template <int RP, bool BF16>
 __global__ void __launch_bounds__(kExpandThreads, 1)
     sgmv_expand_tc_kernel(const __grid_constant__ CUtensorMap tmap_b, const ExpandArgs args) {
@@ -412,6 +456,7 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
   using E = Elem<BF16>;
   constexpr int S = Cfg::kBStages;
   constexpr int YS = Cfg::kYStages;
+  constexpr int YD = kExpandDepth;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* bst_base = smem;
@@ -426,9 +471,11 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
   uint64_t* afull = tempty + 2;
   uint64_t* aempty = afull + 2;
   uint64_t* drain = aempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* esync = drain + 1;  // epilogue-warp rendezvous, one phase per unit
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(esync + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int32_t* tab_mem = reinterpret_cast<int32_t*>(y_base + YS * Cfg::kYStageBytes + Cfg::kBarrierBytes);
+  int32_t* tok_e = reinterpret_cast<int32_t*>(y_base + YS * Cfg::kYStageBytes + Cfg::kBarrierBytes);
+  int32_t* tab_mem = tok_e + 2 * kTileM;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -445,8 +492,8 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
       mbar_init(&bempty[i], 1);
     }
     for (int i = 0; i < YS; ++i) {
-      mbar_init(&yfull[i], 1);
-      mbar_init(&yempty[i], 8);
+      mbar_init(&yfull[i], 128);  // y loader threads
+      mbar_init(&yempty[i], 8);   // epilogue warps
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 32);
@@ -455,10 +502,11 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
       mbar_init(&aempty[i], 8);
     }
     mbar_init(drain, 1);
+    mbar_init(esync, 8);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 2) {
+  if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
@@ -472,83 +520,23 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
   ExpandUnit u;
 
   if (warp == 0) {
-    // ---------------- producer: B tile by TMA, y rows by bulk copies
-    if (lane == 0) prefetch_tmap(&tmap_b);
-    uint32_t bctr = 0, yctr = 0;
-    int64_t prev = -1;
-    int64_t tok[4] = {0, 0, 0, 0};  // token of rows lane + 32 i of the current item
-    bool ok = true;
-    while (ok && units.next(tab, u)) {
-      if (tab.rk[u.slot] <= 0) continue;
-      if (u.item_start != prev) {
-        prev = u.item_start;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = lane + 32 * i;
-          tok[i] = r < u.cnt ? __ldg(args.seg.token_index + u.item_start + r) : 0;
-        }
-      }
-      const int n0 = u.tile * kExpandNT;
-      if (lane == 0) {
+    // ---------------- B tile loader (TMA)
+    if (lane == 0) {
+      prefetch_tmap(&tmap_b);
+      uint32_t bctr = 0;
+      while (units.next(tab, u)) {
+        if (tab.rk[u.slot] <= 0) continue;
         const int st = bctr % S;
-        ok = mbar_wait(&bempty[st], ((bctr / S) & 1) ^ 1, abort_flag);
-        if (ok) {
-          mbar_arrive_expect_tx(&bfull[st], Cfg::kBStageBytes);
-          const uint32_t dst = smem_u32(bst_base + st * Cfg::kBStageStride);
-          tma_load_3d(dst, &tmap_b, &bfull[st], n0, 0, u.slot);
-          tma_load_3d(dst + Cfg::kBoxBytes, &tmap_b, &bfull[st], n0 + 64, 0, u.slot);
-        }
+        if (!mbar_wait(&bempty[st], ((bctr / S) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&bfull[st], Cfg::kBStageBytes);
+        const uint32_t dst = smem_u32(bst_base + st * Cfg::kBStageStride);
+        const int n0 = u.tile * kExpandNT;
+        tma_load_3d(dst, &tmap_b, &bfull[st], n0, 0, u.slot);
+        tma_load_3d(dst + Cfg::kBoxBytes, &tmap_b, &bfull[st], n0 + 64, 0, u.slot);
+        ++bctr;
       }
-      ++bctr;
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      const int ys = yctr % YS;
-      if (!mbar_wait_warp(&yempty[ys], ((yctr / YS) & 1) ^ 1, abort_flag)) break;
-      const uint32_t row_bytes = (uint32_t)min(kExpandNT, args.N - n0) * 2u;
-      if (lane == 0) mbar_arrive_expect_tx(&yfull[ys], row_bytes * (uint32_t)(u.t1 - u.t0));
-      __syncwarp();
-      const uint32_t ybuf = smem_u32(y_base + ys * Cfg::kYStageBytes);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = lane + 32 * i;
-        if (r >= u.t0 && r < u.t1)
-          bulk_load(ybuf + r * kYRowBytes, args.y + (tok[i] * args.N + n0) * 2, row_bytes,
-                    &yfull[ys]);
-      }
-      ++yctr;
     }
   } else if (warp == 1) {
-    // ---------------- tmp gather: item rows -> K-major (no swizzle) tile
-    uint32_t item_ctr = 0;
-    int64_t prev = -1;
-    while (units.next(tab, u)) {
-      const int rank = tab.rk[u.slot];
-      if (rank <= 0 || u.item_start == prev) continue;
-      prev = u.item_start;
-      const int tb = item_ctr & 1;
-      if (!mbar_wait(&tempty[tb], ((item_ctr >> 1) & 1) ^ 1, abort_flag)) break;
-      const int kr = min(rank, args.R);
-      const uint32_t tbuf = smem_u32(tmp_base + tb * Cfg::kTmpBytes);
-#pragma unroll
-      for (int rr = 0; rr < kTileM / 32; ++rr) {
-        const int r = lane + 32 * rr;
-        if (r < u.cnt) {
-          const uint8_t* src =
-              args.tmp + (int64_t)__ldg(args.seg.token_index + u.item_start + r) * args.R * 2;
-#pragma unroll
-          for (int c = 0; c < RP / 8; ++c) {
-            const int kleft = kr - c * 8;
-            const uint32_t bytes = kleft >= 8 ? 16u : (kleft > 0 ? (uint32_t)kleft * 2u : 0u);
-            const uint32_t dst = tbuf + (r >> 3) * (RP * 16) + c * 128 + (r & 7) * 16;
-            cp_async_16(dst, bytes ? src + c * 16 : src, bytes);
-          }
-        }
-      }
-      cp_async_arrive_noinc(&tfull[tb]);
-      ++item_ctr;
-    }
-    cp_async_wait_all();
-  } else if (warp == 2) {
     // ---------------- MMA issue (one thread)
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(BF16, false, true, kTileM, kExpandNT);
@@ -593,23 +581,101 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
         mbar_drain(drain, 0);
       }
     }
-  } else if (warp >= 4) {
-    // ---------------- epilogue: y row segment += scale * D, in shared memory, then bulk store
+  } else if (warp == 2) {
+    // ---------------- tmp gather: item rows -> K-major (no swizzle) tile
+    uint32_t item_ctr = 0;
+    int64_t prev = -1;
+    while (units.next(tab, u)) {
+      const int rank = tab.rk[u.slot];
+      if (rank <= 0 || u.item_start == prev) continue;
+      prev = u.item_start;
+      const int tb = item_ctr & 1;
+      if (!mbar_wait(&tempty[tb], ((item_ctr >> 1) & 1) ^ 1, abort_flag)) break;
+      const int kr = min(rank, args.R);
+      const uint32_t tbuf = smem_u32(tmp_base + tb * Cfg::kTmpBytes);
+#pragma unroll
+      for (int rr = 0; rr < kTileM / 32; ++rr) {
+        const int r = lane + 32 * rr;
+        if (r < u.cnt) {
+          const uint8_t* src =
+              args.tmp + (int64_t)__ldg(args.seg.token_index + u.item_start + r) * args.R * 2;
+#pragma unroll
+          for (int c = 0; c < RP / 8; ++c) {
+            const int kleft = kr - c * 8;
+            const uint32_t bytes = kleft >= 8 ? 16u : (kleft > 0 ? (uint32_t)kleft * 2u : 0u);
+            const uint32_t dst = tbuf + (r >> 3) * (RP * 16) + c * 128 + (r & 7) * 16;
+            cp_async_16(dst, bytes ? src + c * 16 : src, bytes);
+          }
+        }
+      }
+      cp_async_arrive_noinc(&tfull[tb]);
+      ++item_ctr;
+    }
+    cp_async_wait_all();
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------- y row loaders: 16 threads per 256-byte row segment
+    const int t = threadIdx.x - 128;  // 0..127
+    const int c = t & 15;             // 16-byte piece
+    const int rr = t >> 4;            // rows rr + 8 k
+    uint32_t yctr = 0, signaled = 0;
+    int64_t prev = -1;
+    int32_t tok[kTileM / 8];
+    bool ok = true;
+    while (ok && units.next(tab, u)) {
+      if (tab.rk[u.slot] <= 0) continue;
+      if (u.item_start != prev) {
+        prev = u.item_start;
+#pragma unroll
+        for (int k = 0; k < kTileM / 8; ++k) {
+          const int r = rr + 8 * k;
+          tok[k] = r < u.cnt ? __ldg(args.seg.token_index + u.item_start + r) : 0;
+        }
+      }
+      const int ys = yctr % YS;
+      if (!mbar_wait(&yempty[ys], ((yctr / YS) & 1) ^ 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const int n0 = u.tile * kExpandNT;
+      const bool piece = c * 8 < args.N - n0;  // N % 8 == 0: pieces are all-or-nothing
+      const uint32_t ybuf = smem_u32(y_base + ys * Cfg::kYStageBytes);
+#pragma unroll
+      for (int k = 0; k < kTileM / 8; ++k) {
+        const int r = rr + 8 * k;
+        if (piece && r >= u.t0 && r < u.t1)
+          cp_async_16(ybuf + r * kYRowBytes + c * 16, args.y + ((int64_t)tok[k] * args.N + n0 + c * 8) * 2,
+                      16);
+      }
+      cp_async_commit();
+      ++yctr;
+      if (yctr - signaled == YD) {
+        cp_async_wait_group<YD - 1>();
+        mbar_arrive(&yfull[signaled % YS]);
+        ++signaled;
+      }
+    }
+    cp_async_wait_group<0>();
+    for (; signaled < yctr; ++signaled) mbar_arrive(&yfull[signaled % YS]);
+  } else if (warp >= 8) {
+    // ---------------- epilogue
     const int q = warp & 3;         // TMEM lane quarter
-    const int h = (warp - 4) >> 2;  // column half of the 128-column tile
-    const int r = q * 32 + lane;
-    uint32_t unit_ctr = 0;
-    int prev_ys = -1;
-    int64_t prev = -1, tok = 0;
+    const int h = (warp - 8) >> 2;  // column half of the 128-column tile
+    const int r = q * 32 + lane;    // token row of the compute phase
+    const int et = threadIdx.x - 256;  // 0..255 in the write-back phase
+    uint32_t unit_ctr = 0, item_ctr = 0;
+    int64_t prev = -1;
+    int32_t* tokb = tok_e;
     while (units.next(tab, u)) {
       if (tab.rk[u.slot] <= 0) continue;
       if (u.item_start != prev) {
         prev = u.item_start;
-        tok = (r < u.cnt) ? __ldg(args.seg.token_index + u.item_start + r) : 0;
+        tokb = tok_e + (item_ctr & 1) * kTileM;
+        ++item_ctr;
+        if (et < kTileM) tokb[et] = et < u.cnt ? __ldg(args.seg.token_index + u.item_start + et) : 0;
       }
       const float scale = tab.sc[u.slot];
-      const int n_base = u.tile * kExpandNT + h * 64;
-      const int ncols = min(64, args.N - n_base);  // multiple of 8 (N % 8 == 0)
+      const int n0 = u.tile * kExpandNT;
+      const int ncols = min(64, args.N - n0 - h * 64);  // multiple of 8 (N % 8 == 0)
       const bool active = (r >= u.t0) && (r < u.t1) && ncols > 0;
       const int ab = unit_ctr & 1;
       const int ys = unit_ctr % YS;
@@ -625,7 +691,8 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&aempty[ab]);
       if (!mbar_wait_warp(&yfull[ys], (unit_ctr / YS) & 1, abort_flag)) break;
-      const uint32_t yrow = smem_u32(y_base + ys * Cfg::kYStageBytes) + r * kYRowBytes + h * 128;
+      const uint32_t ybuf = smem_u32(y_base + ys * Cfg::kYStageBytes);
+      const uint32_t yrow = ybuf + r * kYRowBytes + h * 128;
       if (active) {
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
@@ -649,22 +716,30 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
                          : "memory");
           }
         }
-        fence_proxy_async_smem();
-        bulk_store(args.y + (tok * args.N + n_base) * 2, yrow, (uint32_t)ncols * 2u);
       }
-      bulk_commit();
-      // the previous unit's stage is free once this thread's stores from it were read
-      bulk_wait_read<1>();
+      // the whole tile is updated and the item's token ids are visible
       __syncwarp();
-      if (lane == 0 && prev_ys >= 0) mbar_arrive(&yempty[prev_ys]);
-      prev_ys = ys;
+      if (lane == 0) mbar_arrive(esync);
+      if (!mbar_wait_warp(esync, unit_ctr & 1, abort_flag)) break;
+      const int wc = et & 15;
+      if (wc * 8 < args.N - n0) {
+        for (int wr = u.t0 + (et >> 4); wr < u.t1; wr += 16) {
+          uint32_t v[4];
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                       : "r"(ybuf + wr * kYRowBytes + wc * 16));
+          *reinterpret_cast<uint4*>(args.y + ((int64_t)tokb[wr] * args.N + n0 + wc * 8) * 2) =
+              make_uint4(v[0], v[1], v[2], v[3]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&yempty[ys]);
       ++unit_ctr;
     }
-    bulk_wait<0>();
   }
 
   __syncthreads();
-  if (warp == 2) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
