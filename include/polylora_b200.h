@@ -121,6 +121,27 @@ int plora_sgmv_b_fwd(const void* tmp, const void* lora_b, void* y, const int32_t
                      int64_t out_features, int32_t num_slots, int32_t dtype, void* workspace,
                      size_t workspace_size, void* stream);
 
+/* plora_sgmv_a_fwd without a caller-provided workspace, for callers that
+ * cannot allocate device memory at call time: code running inside a region
+ * that forbids cudaMalloc (it synchronises the device), embedders whose
+ * memory is a fixed pool they do not control, and foreign-language callers
+ * that own no CUDA allocator.  No counterpart in the reference (its operators
+ * always allocate through torch).
+ * Its scratch is a static device array of PLORA_NOALLOC_SCRATCH_BYTES that
+ * every GPU loading this library holds until process exit; a batch whose
+ * segment scratch + table (plora_workspace_size) exceeds it is rejected with
+ * PLORA_ERR_UNSUPPORTED.  The first call on each device looks up the array's
+ * device address (make that first call before any stream capture).  All
+ * calls share the array: calls that overlap on the GPU (other streams,
+ * other threads) race and must be serialised by the caller.  Nothing in the
+ * array needs to start at zero; each call rewrites what it reads. */
+#define PLORA_NOALLOC_SCRATCH_BYTES (8u << 20)
+int plora_sgmv_a_fwd_noalloc(const void* x, const void* lora_a, void* tmp, const int32_t* seq_lens,
+                             const int64_t* weight_indices, const int32_t* lora_ranks,
+                             int64_t num_rows, int64_t max_seq, int64_t in_features,
+                             int64_t max_rank, int32_t num_slots, int32_t stack_num, int32_t dtype,
+                             void* stream);
+
 /* Shrink over a prebuilt segment table (plora_build_segments).  Same math as
  * plora_sgmv_a_fwd; `lora_ranks` may hold ranks of a different module than
  * the table was built with: tokens whose slot rank is 0 here are skipped. */

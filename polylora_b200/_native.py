@@ -28,6 +28,8 @@ DEV_WAIT_TIMEOUT = 1
 DEV_SLOT_RANGE = 2
 DEV_RANK_RANGE = 4
 
+NOALLOC_SCRATCH_BYTES = 8 << 20  # PLORA_NOALLOC_SCRATCH_BYTES
+
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int32
 _i64 = ctypes.c_int64
@@ -113,6 +115,13 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [
             _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
             _i64, _i64, _i64, _i32, _i32, _c_void_p,
+        ],
+    ),
+    "plora_sgmv_a_fwd_noalloc": (
+        ctypes.c_int,
+        [
+            _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+            _i64, _i64, _i64, _i64, _i32, _i32, _i32, _c_void_p,
         ],
     ),
     "plora_slot_fill": (

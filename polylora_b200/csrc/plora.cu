@@ -17,6 +17,12 @@
 
 using namespace plora;
 
+// Scratch of plora_sgmv_a_fwd_noalloc: segment scratch + slot table for one
+// batch, resident on every device that loads the library.  Host code must not
+// use this symbol as a pointer; it is a host-side stand-in for the device
+// array, whose address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[PLORA_NOALLOC_SCRATCH_BYTES];
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -500,6 +506,56 @@ int plora_slot_fill(const plora_slot_module* modules, int32_t num_modules, int32
   else
     slot_fill_kernel<__half><<<grid, block, 0, s>>>(modules, num_modules, slot, max_rank, img);
   return check_launch("slot_fill_kernel");
+}
+
+// Device address of g_noalloc_scratch, looked up once per device with that
+// device current (the first plora_sgmv_a_fwd_noalloc call on the device).
+namespace {
+void* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  PLORA_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(PLORA_ERR_UNSUPPORTED, "device ordinal %d", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    PLORA_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(noalloc scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return PLORA_OK;
+}
+}  // namespace
+
+extern "C" int plora_sgmv_a_fwd_noalloc(const void* x, const void* lora_a, void* tmp,
+                                        const int32_t* seq_lens, const int64_t* weight_indices,
+                                        const int32_t* lora_ranks, int64_t num_rows,
+                                        int64_t max_seq, int64_t in_features, int64_t max_rank,
+                                        int32_t num_slots, int32_t stack_num, int32_t dtype,
+                                        void* stream) {
+  g_last_error.clear();
+  int st = check_common(dtype, num_slots, max_rank);
+  if (st) return st;
+  if (num_rows < 0 || max_seq < 0) return fail(PLORA_ERR_INVALID_ARGUMENT, "negative num_rows/max_seq");
+  if (num_rows == 0 || max_seq == 0) return PLORA_OK;
+  const size_t need = fwd_workspace_bytes(num_rows, max_seq, num_slots);
+  if (need > (size_t)PLORA_NOALLOC_SCRATCH_BYTES)
+    return fail(PLORA_ERR_UNSUPPORTED,
+                "batch needs %zu bytes of scratch; the static scratch of plora_sgmv_a_fwd_noalloc "
+                "holds %u bytes (use plora_sgmv_a_fwd with a workspace)",
+                need, (unsigned)PLORA_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  if ((st = noalloc_scratch(&scratch))) return st;
+  FwdWorkspace w = carve_fwd(scratch, num_rows, max_seq, num_slots);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((st = build_segments(weight_indices, seq_lens, lora_ranks, num_rows, max_seq, num_slots,
+                           w.slot_start, w.token_index, scratch, need, s)))
+    return st;
+  return plora_sgmv_shrink(x, lora_a, tmp, lora_ranks, w.slot_start, w.token_index,
+                           num_rows * max_seq, in_features, max_rank, num_slots, stack_num, dtype,
+                           stream);
 }
 
 }  // extern "C"
