@@ -71,6 +71,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// Longest time one try_wait may park the calling warp (ns).  A parked warp
+// issues no instructions, so waiting roles leave the issue slots to the roles
+// that move data; the phase completing wakes it earlier.
+constexpr uint32_t kSuspendHintNs = 100u * 1000u;
+
+__device__ __forceinline__ bool mbar_try_wait_parked(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return done != 0;
+}
+
 // Waits until the phase with the given parity of `bar` has completed.  Gives
 // up when `abort_flag` (shared) is raised by another role or after
 // kWaitLimitNs; on expiry raises the device status and the abort flag.
@@ -79,15 +96,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0u) {
-      if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        *abort_flag = 1;
-        raise_status(PLORA_DEV_WAIT_TIMEOUT);
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_parked(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      raise_status(PLORA_DEV_WAIT_TIMEOUT);
+      return false;
     }
   }
 }
@@ -142,6 +157,12 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// Starts fetching the cache line holding `p` into L2 (no register result, so a
+// thread can keep many lines in flight beyond its register-staged loads).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
 // 3-D tiled TMA load into this CTA's shared memory, completing on `bar` by byte count.

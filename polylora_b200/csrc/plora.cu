@@ -13,7 +13,7 @@
 #include "common.cuh"
 #include "segments.cuh"
 #include "sgmv_simt.cuh"
-#include "sgmv_tc.cuh"
+#include "sgmv_mma.cuh"
 
 using namespace plora;
 
@@ -78,12 +78,12 @@ int device_info(DeviceInfo** out) {
   PLORA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,           \
                                   (int)((bytes) + tab_bytes(kTcMaxSlots))),                     \
              #kern)
-    SET_SMEM((sgmv_shrink_tc_kernel<16, true>), ShrinkCfg<16>::kSmemBytes);
-    SET_SMEM((sgmv_shrink_tc_kernel<32, true>), ShrinkCfg<32>::kSmemBytes);
-    SET_SMEM((sgmv_shrink_tc_kernel<64, true>), ShrinkCfg<64>::kSmemBytes);
-    SET_SMEM((sgmv_shrink_tc_kernel<16, false>), ShrinkCfg<16>::kSmemBytes);
-    SET_SMEM((sgmv_shrink_tc_kernel<32, false>), ShrinkCfg<32>::kSmemBytes);
-    SET_SMEM((sgmv_shrink_tc_kernel<64, false>), ShrinkCfg<64>::kSmemBytes);
+    SET_SMEM((sgmv_shrink_mma_kernel<16, true>), ShrinkMmaCfg<16>::kSmemBytes);
+    SET_SMEM((sgmv_shrink_mma_kernel<32, true>), ShrinkMmaCfg<32>::kSmemBytes);
+    SET_SMEM((sgmv_shrink_mma_kernel<64, true>), ShrinkMmaCfg<64>::kSmemBytes);
+    SET_SMEM((sgmv_shrink_mma_kernel<16, false>), ShrinkMmaCfg<16>::kSmemBytes);
+    SET_SMEM((sgmv_shrink_mma_kernel<32, false>), ShrinkMmaCfg<32>::kSmemBytes);
+    SET_SMEM((sgmv_shrink_mma_kernel<64, false>), ShrinkMmaCfg<64>::kSmemBytes);
     SET_SMEM((sgmv_expand_tc_kernel<16, true>), ExpandCfg<16>::kSmemBytes);
     SET_SMEM((sgmv_expand_tc_kernel<32, true>), ExpandCfg<32>::kSmemBytes);
     SET_SMEM((sgmv_expand_tc_kernel<64, true>), ExpandCfg<64>::kSmemBytes);
@@ -234,18 +234,18 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
                                    : R == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
                                              : CU_TENSOR_MAP_SWIZZLE_128B;
     if ((st = make_map_3d(&map, a, dtype, (uint64_t)R, (uint64_t)K, (uint64_t)seg.num_slots,
-                          (uint32_t)R, kShrinkKC, swz)))
+                          (uint32_t)R, kWinBoxRows, swz)))
       return st;
     (void)num_tokens;
-    const dim3 grid(di->sm_count), block(kShrinkThreads);
+    const dim3 grid(di->sm_count), block(kMmaThreads);
     const size_t tb = tab_bytes(seg.num_slots);
     const bool bf = dtype == PLORA_DTYPE_BF16;
-#define LAUNCH_SHRINK(RPV)                                                               \
-  if (bf)                                                                                \
-    sgmv_shrink_tc_kernel<RPV, true><<<grid, block, ShrinkCfg<RPV>::kSmemBytes + tb, stream>>>( \
-        map, args);                                                                \
-  else                                                                                   \
-    sgmv_shrink_tc_kernel<RPV, false><<<grid, block, ShrinkCfg<RPV>::kSmemBytes + tb, stream>>>( \
+#define LAUNCH_SHRINK(RPV)                                                                     \
+  if (bf)                                                                                      \
+    sgmv_shrink_mma_kernel<RPV, true><<<grid, block, ShrinkMmaCfg<RPV>::kSmemBytes + tb, stream>>>( \
+        map, args);                                                                            \
+  else                                                                                         \
+    sgmv_shrink_mma_kernel<RPV, false><<<grid, block, ShrinkMmaCfg<RPV>::kSmemBytes + tb, stream>>>( \
         map, args);
     if (R == 16) {
       LAUNCH_SHRINK(16)
@@ -255,7 +255,7 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
       LAUNCH_SHRINK(64)
     }
 #undef LAUNCH_SHRINK
-    return check_launch("sgmv_shrink_tc_kernel");
+    return check_launch("sgmv_shrink_mma_kernel");
   }
   if (R > kSimtMaxRank) return fail(PLORA_ERR_UNSUPPORTED, "max_rank %lld > %d", (long long)R, kSimtMaxRank);
   const dim3 grid(di->sm_count * 8), block(kSimtThreads);

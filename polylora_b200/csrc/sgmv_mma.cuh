@@ -1,0 +1,368 @@
+// SGMV shrink with the activation rows streamed straight into registers.
+//
+// The shrink is a gather-and-reduce over HBM: every active token reads its
+// K-wide row of x once, and the rank-R reduction is tiny.  Its speed is set by
+// how many bytes each SM keeps in flight, so x never passes through shared
+// memory: each warp loads 16 bytes per lane (a quad of lanes covers 64
+// contiguous bytes of one row), regroups the words across the quad into
+// mma.sync fragments and multiplies against the slot's LoRA-A weights, which
+// are the only operand staged in shared memory (64 KB windows by TMA,
+// swizzled so that ldmatrix.trans reads them without bank conflicts).
+//
+// Work split: a CTA takes a contiguous share of the slot-ordered token list,
+// cut into items of <= 128 tokens of one slot.  An item is 16-token tiles x
+// K ranges, one (tile, K range) pair per warp; the per-warp fp32 partial
+// sums are reduced through shared memory at the end of the item.
+//
+// Reference semantics: src/polylora/sgmv.py:63-138 (_sgmv_lora_a_kernel).
+#pragma once
+
+#include "sgmv_tc.cuh"
+
+namespace plora {
+
+constexpr int kMmaWarps = 16;                      // compute warps
+constexpr int kMmaThreads = kMmaWarps * 32;
+constexpr int kWinBytes = 64 * 1024;               // one LoRA weight window
+constexpr int kWinBoxRows = 256;                   // rows per weight TMA box
+
+template <int RP>
+struct ShrinkMmaCfg {
+  static constexpr int kWinRows = kWinBytes / (RP * 2);  // K rows per window
+  static constexpr int kBoxBytes = kWinBoxRows * RP * 2;
+  static constexpr int kNT = RP / 8;                      // n8 tiles of the rank
+  static constexpr int kU = RP == 16 ? 4 : (RP == 32 ? 3 : 2);  // 32-column blocks per load batch
+  static constexpr int kPartBytes = kMmaWarps * 16 * RP * 4;    // one 16 x RP fp32 tile per warp
+  static constexpr int kBarrierBytes = 64;
+  // + slot table (3 * num_slots + 1 ints), sized at launch
+  static constexpr int kSmemBytes = 1024 + 2 * kWinBytes + kPartBytes + kBarrierBytes;
+};
+
+// 4x4 transpose of 32-bit words across the four lanes of a quad: lane t
+// holds w[i] = M[t][i] on entry and M[i][t] on exit.
+__device__ __forceinline__ void quad_transpose(uint32_t (&w)[4], int t) {
+  const bool hi = t & 2;
+  uint32_t s0 = hi ? w[0] : w[2], s1 = hi ? w[1] : w[3];
+  uint32_t r0 = __shfl_xor_sync(0xffffffffu, s0, 2), r1 = __shfl_xor_sync(0xffffffffu, s1, 2);
+  if (hi) {
+    w[0] = r0;
+    w[1] = r1;
+  } else {
+    w[2] = r0;
+    w[3] = r1;
+  }
+  const bool odd = t & 1;
+  s0 = odd ? w[0] : w[1];
+  s1 = odd ? w[2] : w[3];
+  r0 = __shfl_xor_sync(0xffffffffu, s0, 1);
+  r1 = __shfl_xor_sync(0xffffffffu, s1, 1);
+  if (odd) {
+    w[0] = r0;
+    w[2] = r1;
+  } else {
+    w[1] = r0;
+    w[3] = r1;
+  }
+}
+
+// 16-byte streaming load that does not allocate in L1 (rows are read once).
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// d += a (16x16, row) * b (16x8, col); fp32 accumulate.
+template <bool BF16>
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+  if constexpr (BF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+// Shared-memory byte offset of 16-byte chunk j of row k of a weight window
+// written by TMA with the swizzle that matches its row width (32/64/128 B
+// for RP = 16/32/64): the chunk index is XORed with address bits 7 and up.
+template <int RP>
+__device__ __forceinline__ uint32_t win_offset(int k, int j) {
+  constexpr int kRowBytes = RP * 2;
+  const uint32_t off = (uint32_t)k * kRowBytes;
+  return off + 16u * ((uint32_t)j ^ ((off >> 7) & (RP / 8 - 1)));
+}
+
+// Sequence of (slot, window) pairs over the CTA's items with rank > 0, in the
+// order every warp consumes them.
+struct WinCursor {
+  ShrinkItems it;
+  int slot, w, nwin;
+  bool valid;
+  __device__ void init(const SlotTab& tab, int64_t b, int64_t e, int nw) {
+    it.init(tab, b, e);
+    nwin = nw;
+    slot = -1;
+    w = 0;
+    valid = true;
+    advance(tab);
+  }
+  __device__ void advance(const SlotTab& tab) {
+    if (slot >= 0 && ++w < nwin) return;
+    w = 0;
+    int s, cnt;
+    int64_t start;
+    while (it.next(tab, s, start, cnt))
+      if (tab.rk[s] > 0) {
+        slot = s;
+        return;
+      }
+    valid = false;
+  }
+};
+
+// tmp[t, :] = x[t, :] @ A[slot(t)] for the active tokens of the table.
+// 16 warps; an item is 16-token tiles x K ranges, one pair per warp.  The
+// slot's LoRA-A rows stream through two 64 KB windows: windows 0 and 1 are
+// issued at start, and the last warp to release window c issues c + 2.
+template <int RP, bool BF16>
+__global__ void __launch_bounds__(kMmaThreads, 1)
+    sgmv_shrink_mma_kernel(const __grid_constant__ CUtensorMap tmap_a, const ShrinkArgs args) {
+  using Cfg = ShrinkMmaCfg<RP>;
+  using E = Elem<BF16>;
+  constexpr int W = Cfg::kWinRows;
+  constexpr int U = Cfg::kU;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  float* part = reinterpret_cast<float*>(smem + 2 * kWinBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kWinBytes + Cfg::kPartBytes);
+  uint32_t* released = reinterpret_cast<uint32_t*>(full + 2);  // per buffer, monotonic
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(released + 2);
+  int32_t* tab_mem =
+      reinterpret_cast<int32_t*>(smem + 2 * kWinBytes + Cfg::kPartBytes + Cfg::kBarrierBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t total = __ldg(args.seg.slot_start + args.seg.num_slots);
+  const int64_t begin = total * blockIdx.x / gridDim.x;
+  const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
+  if (begin >= end) return;  // uniform across the CTA
+
+  const SlotTab tab = stage_slot_tab(args.seg, args.ranks, nullptr, tab_mem);
+  const int K = args.K;
+  const int nwin = (K + W - 1) / W;
+  auto issue = [&](const WinCursor& wc, int b) {  // one thread
+    const int rows = min(W, K - wc.w * W);
+    const int boxes = (rows + kWinBoxRows - 1) / kWinBoxRows;
+    mbar_arrive_expect_tx(&full[b], boxes * Cfg::kBoxBytes);
+    for (int q = 0; q < boxes; ++q)
+      tma_load_3d(smem_u32(smem + b * kWinBytes + q * Cfg::kBoxBytes), &tmap_a, &full[b], 0,
+                  wc.w * W + q * kWinBoxRows, wc.slot);
+  };
+  __syncthreads();  // slot table staged
+  WinCursor ic;     // the window this warp would issue after its next release
+  ic.init(tab, begin, end, nwin);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) mbar_init(&full[i], 1);
+    released[0] = released[1] = 0;
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmap_a);
+    for (int b = 0; b < 2 && ic.valid; ++b) {
+      issue(ic, b);
+      ic.advance(tab);
+    }
+  } else {
+    ic.advance(tab);
+    ic.advance(tab);
+  }
+  __syncthreads();
+
+  ShrinkItems items;
+  items.init(tab, begin, end);
+  int s, cnt;
+  int64_t start;
+  const int g = lane >> 2;  // fragment row group
+  const int t = lane & 3;   // lane within the quad
+  const uint32_t win_base = smem_u32(smem);
+  uint32_t c_base = 0;  // window counter at the start of the item
+  bool ok = true;
+  while (items.next(tab, s, start, cnt)) {
+    const int rank = tab.rk[s];
+    if (rank <= 0) continue;
+    const int tiles = (cnt + 15) >> 4;
+    const int KS = max(1, kMmaWarps / tiles);
+    const bool active = warp < tiles * KS;
+    const int tile = active ? warp / KS : 0;
+    const int ks = active ? warp - tile * KS : 0;
+    const int r0 = tile * 16 + g;
+    const bool v0 = active && r0 < cnt, v1 = active && r0 + 8 < cnt;
+    const uint8_t* x0 = args.x + (v0 ? (int64_t)__ldg(args.seg.token_index + start + r0) : 0) * K * 2;
+    const uint8_t* x1 = args.x + (v1 ? (int64_t)__ldg(args.seg.token_index + start + r0 + 8) : 0) * K * 2;
+
+    // this warp's 32-column blocks of window w: [b0, b1); cursors over
+    // (window, block) skip windows without blocks
+    struct Cur {
+      int w, blk, end;
+    };
+    auto range = [&](Cur& c) {
+      const int nb = (min(W, K - c.w * W) + 31) >> 5;
+      c.blk = active ? ks * nb / KS : 0;
+      c.end = active ? (ks + 1) * nb / KS : 0;
+    };
+    auto first = [&](Cur& c) {
+      c.w = 0;
+      range(c);
+      while (c.blk >= c.end && ++c.w < nwin) range(c);
+    };
+    auto step = [&](Cur& c) {
+      if (++c.blk >= c.end)
+        while (++c.w < nwin) {
+          range(c);
+          if (c.blk < c.end) break;
+        }
+    };
+    Cur lc, mc;  // load cursor, compute cursor (same sequence)
+    first(lc);
+    first(mc);
+
+    struct Batch {
+      uint4 x0[U], x1[U];
+    };
+    auto load_batch = [&](Batch& B) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (lc.w < nwin) {
+          const int col = lc.w * W + lc.blk * 32 + 8 * t;
+          const bool in = col < K;
+          B.x0[u] = (v0 && in) ? ld_stream16(x0 + col * 2) : make_uint4(0u, 0u, 0u, 0u);
+          B.x1[u] = (v1 && in) ? ld_stream16(x1 + col * 2) : make_uint4(0u, 0u, 0u, 0u);
+          step(lc);
+        }
+      }
+    };
+
+    float acc[Cfg::kNT][4];
+#pragma unroll
+    for (int j = 0; j < Cfg::kNT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    int cw = -1;  // window of this item the warp currently holds
+    // releases the held window; the last of the 16 releasers refills its buffer
+    auto release = [&]() {
+      const uint32_t b = (c_base + cw) & 1;
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();
+        if (atomicAdd(&released[b], 1u) % kMmaWarps == kMmaWarps - 1 && ic.valid) {
+          fence_proxy_async_smem();
+          issue(ic, b);
+        }
+      }
+      ic.advance(tab);
+    };
+    // moves the hold forward to window `to` of the item
+    auto hold = [&](int to) {
+      while (cw < to) {
+        if (cw >= 0) release();
+        ++cw;
+        const uint32_t c = c_base + cw;
+        if (ok) ok = mbar_wait_warp(&full[c & 1], (c >> 1) & 1, abort_flag);
+      }
+    };
+    auto compute_batch = [&](Batch& B) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (mc.w >= nwin) break;
+        hold(mc.w);
+        uint32_t a0[4] = {B.x0[u].x, B.x0[u].y, B.x0[u].z, B.x0[u].w};
+        uint32_t a1[4] = {B.x1[u].x, B.x1[u].y, B.x1[u].z, B.x1[u].w};
+        quad_transpose(a0, t);
+        quad_transpose(a1, t);
+        // k16 step s: cols 16 s + {2t, 2t + 1} and 16 s + 8 + {2t, 2t + 1}
+        const uint32_t fa[2][4] = {{a0[0], a1[0], a0[1], a1[1]}, {a0[2], a1[2], a0[3], a1[3]}};
+        const int krow = mc.blk * 32 + 8 * (lane >> 3) + (lane & 7);
+        const uint32_t wb = win_base + ((c_base + mc.w) & 1) * kWinBytes;
+#pragma unroll
+        for (int j = 0; j < Cfg::kNT; ++j) {
+          uint32_t bf[4];
+          ldsm_x4_trans(wb + win_offset<RP>(krow, j), bf);
+          if (ok) {
+            mma_16816<BF16>(acc[j], fa[0], bf[0], bf[1]);
+            mma_16816<BF16>(acc[j], fa[1], bf[2], bf[3]);
+          }
+        }
+        step(mc);
+      }
+    };
+
+    Batch A, B;
+    load_batch(A);
+    for (;;) {
+      const bool more_b = lc.w < nwin;
+      if (more_b) load_batch(B);
+      compute_batch(A);
+      if (!more_b) break;
+      const bool more_a = lc.w < nwin;
+      if (more_a) load_batch(A);
+      compute_batch(B);
+      if (!more_a) break;
+    }
+    hold(nwin - 1);  // windows without blocks of this warp are passed through
+    release();
+    c_base += nwin;
+
+    // partial sums -> shared memory -> reduced, rounded rows of tmp
+    if (active) {
+      float* p = part + (size_t)warp * 16 * RP;
+#pragma unroll
+      for (int j = 0; j < Cfg::kNT; ++j) {
+        *reinterpret_cast<float2*>(p + g * RP + 8 * j + 2 * t) = make_float2(acc[j][0], acc[j][1]);
+        *reinterpret_cast<float2*>(p + (g + 8) * RP + 8 * j + 2 * t) = make_float2(acc[j][2], acc[j][3]);
+      }
+    }
+    named_barrier(1, kMmaWarps * 32);
+    const int n_eff = min(rank * args.stack_num, args.R);
+    for (int u = threadIdx.x; u < tiles * 16 * (RP / 8); u += kMmaWarps * 32) {
+      const int row = u / (RP / 8), cg = u - row * (RP / 8);
+      if (row >= cnt) continue;
+      const int tl = row >> 4, rr = row & 15;
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+      for (int q = 0; q < KS; ++q) {
+        const float* p = part + ((size_t)(tl * KS + q) * 16 + rr) * RP + cg * 8;
+        const float4 lo = *reinterpret_cast<const float4*>(p);
+        const float4 hi = *reinterpret_cast<const float4*>(p + 4);
+        v[0] += lo.x; v[1] += lo.y; v[2] += lo.z; v[3] += lo.w;
+        v[4] += hi.x; v[5] += hi.y; v[6] += hi.z; v[7] += hi.w;
+      }
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c0 = cg * 8 + 2 * i;
+        o[i] = (uint32_t)E::from_f(c0 < n_eff ? v[2 * i] : 0.f) |
+               ((uint32_t)E::from_f(c0 + 1 < n_eff ? v[2 * i + 1] : 0.f) << 16);
+      }
+      const int64_t tok = __ldg(args.seg.token_index + start + row);
+      *reinterpret_cast<uint4*>(args.tmp + (tok * args.R + cg * 8) * 2) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    named_barrier(1, kMmaWarps * 32);
+  }
+}
+
+}  // namespace plora

@@ -21,13 +21,9 @@ namespace plora {
 
 constexpr int kTileM = 128;        // tokens per MMA tile (TMEM lanes)
 constexpr int kShrinkKC = 64;      // K elements per shrink stage (one 128-byte row)
-constexpr int kShrinkStages = 8;
-constexpr int kShrinkDepth = 6;    // cp.async groups a gather thread keeps in flight (<= stages)
 constexpr int kExpandNT = 128;     // output columns per expand unit
-constexpr int kYRowBytes = kExpandNT * 2 + 16;  // padded smem row: conflict-free row-per-thread access
-constexpr int kExpandDepth = 3;    // y-row cp.async groups a loader thread keeps in flight
-constexpr int kShrinkThreads = 320;  // 4 gather warps, A TMA, MMA, 4 epilogue warps
-constexpr int kExpandThreads = 512;  // B TMA, MMA, tmp gather, idle, 4 y-load warps, 8 epilogue warps
+constexpr int kShrinkThreads = 704;  // 16 producer warps, A TMA, MMA, 4 epilogue warps
+constexpr int kExpandThreads = 768;  // B TMA, MMA, tmp gather, idle, 4 TMEM readers, 16 y streams
 
 struct SegTable {
   const int32_t* slot_start;   // (num_slots + 1)
@@ -182,7 +178,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 // Time-bounded wait that ignores the abort flag (used to drain own work).
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = global_timer_ns();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_parked(bar, parity)) {
     if (global_timer_ns() - t0 > kWaitLimitNs) {
       raise_status(PLORA_DEV_WAIT_TIMEOUT);
       return;
@@ -191,45 +187,53 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
 }
 
 // ============================================================== shrink
+constexpr int kShrinkProducerWarps = 16;
+constexpr int kShrinkMaxStages = 32;
+constexpr int kShrinkRingBytes = 144 * 1024;  // stage ring budget (x tile + A chunk per stage)
+#ifndef PLORA_SHRINK_PREFETCH
+#define PLORA_SHRINK_PREFETCH 0
+#endif
+constexpr int kShrinkPrefetch = PLORA_SHRINK_PREFETCH;  // chunk groups fetched into L2 ahead of the register loads
+
 template <int RP>
 struct ShrinkCfg {
-  static constexpr int kXBytes = kTileM * kShrinkKC * 2;  // 16 KB, K-major SW128
-  static constexpr int kABytes = kShrinkKC * RP * 2;      // MN-major, swizzle = RP*2 bytes
-  static constexpr int kStageBytes = kXBytes + ((kABytes + 1023) & ~1023);
+  static constexpr int kABytes = kShrinkKC * RP * 2;  // MN-major, swizzle = RP*2 bytes
   static constexpr int kTmemCols = (2 * RP < 32) ? 32 : 2 * RP;
   static constexpr uint32_t kALayout = RP == 16 ? kSwizzle32 : (RP == 32 ? kSwizzle64 : kSwizzle128);
   static constexpr uint32_t kAAtom = 8 * RP * 2;  // 8 K-rows of one swizzle atom
-  static constexpr int kBarrierBytes = 256;
+  static constexpr int kBarrierBytes = 1024;
+  // ring + tail pad (the UMMA reads 128 rows from any stage) + barriers;
   // + slot table (3 * num_slots + 1 ints), sized at launch
-  static constexpr int kSmemBytes = 1024 + kShrinkStages * kStageBytes + kBarrierBytes;
-  static_assert(kShrinkDepth <= kShrinkStages, "gather depth must not exceed the stages");
+  static constexpr int kSmemBytes = 1024 + kShrinkRingBytes + kTileM * 128 + kBarrierBytes;
 };
 
 // tmp[t, :] = x[t, :] @ A[slot(t)] for the active tokens of the table.
-//   warps 0-3: token-row gather — 16-byte cp.async pieces into the 128-byte
-//           swizzled K-major stage tile (four 128-byte rows per warp
-//           instruction); each thread keeps kShrinkDepth stages in flight and
-//           signals a stage once its group has landed.
-//   warp 4: TMEM owner; lane 0 loads A[slot] (64 x RP) per stage by TMA.
-//   warp 5: lane 0 issues 4 UMMAs (128 x RP x 16) per stage.
-//   warps 6-9: epilogue — TMEM -> registers -> bf16/fp16 rows of tmp.
+//   warps 0-15: producers, one warp per token row: a warp-wide 16-byte load
+//           covers four 64-wide K chunks of one row (512 contiguous bytes);
+//           the next group of chunks is loaded while the current one is
+//           stored into the 128-byte-swizzled K-major stage tiles.
+//   warp 16: TMEM owner; lane 0 loads A[slot] (64 x RP) per stage by TMA.
+//   warp 17: lane 0 issues 4 UMMAs (128 x RP x 16) per stage.
+//   warps 18-21: epilogue — TMEM -> registers -> bf16/fp16 rows of tmp.
+// Stage tiles are `rows_pad` rows apart (the CTA's largest item rounded up
+// to 8): the UMMA reads 128 rows per stage and ignores the rows past the
+// item, so small items do not waste the ring.
 template <int RP, bool BF16>
 __global__ void __launch_bounds__(kShrinkThreads, 1)
     sgmv_shrink_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const ShrinkArgs args) {
   using Cfg = ShrinkCfg<RP>;
   using E = Elem<BF16>;
-  constexpr int S = kShrinkStages;
-  constexpr int D = kShrinkDepth;
+  constexpr int PW = kShrinkProducerWarps;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
-  uint64_t* empty = full + S;
-  uint64_t* acc_full = empty + S;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kShrinkRingBytes + kTileM * 128);
+  uint64_t* empty = full + kShrinkMaxStages;
+  uint64_t* acc_full = empty + kShrinkMaxStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int32_t* tab_mem = reinterpret_cast<int32_t*>(smem + S * Cfg::kStageBytes + Cfg::kBarrierBytes);
+  int32_t* tab_mem = reinterpret_cast<int32_t*>(smem + kShrinkRingBytes + kTileM * 128 + Cfg::kBarrierBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -239,9 +243,23 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   if (begin >= end) return;  // uniform across the CTA
 
   const SlotTab tab = stage_slot_tab(args.seg, args.ranks, nullptr, tab_mem);
+  __syncthreads();
+  // ring geometry from the CTA's largest item
+  int max_cnt = 1;
+  {
+    ShrinkItems it;
+    it.init(tab, begin, end);
+    int s, c;
+    int64_t st;
+    while (it.next(tab, s, st, c)) max_cnt = max(max_cnt, c);
+  }
+  const int rows_pad = (max_cnt + 7) & ~7;
+  const int stage_bytes = rows_pad * 128 + Cfg::kABytes;  // x tile then A chunk, 1024-aligned
+  const int S = min(kShrinkMaxStages, kShrinkRingBytes / stage_bytes);
+
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&full[i], 128 + 1);  // 128 gather threads + the A loader's expect_tx
+      mbar_init(&full[i], PW + 1);  // producer warps + the A loader's expect_tx
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -252,7 +270,7 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 4) {
+  if (warp == PW) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
@@ -261,60 +279,101 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int nkc = (args.K + kShrinkKC - 1) / kShrinkKC;
+  const int ngroups = (nkc + 3) >> 2;
+  const uint32_t ring = smem_u32(smem);
 
   ShrinkItems items;
   items.init(tab, begin, end);
   int s, cnt;
   int64_t start;
 
-  if (warp < 4) {
-    // ---------------- token-row gather
-    const int t = threadIdx.x;  // 0..127
-    const int c = t & 7;        // 16-byte piece of the 128-byte row chunk
-    const int r0 = t >> 3;      // rows r0 + 16 j
-    uint32_t ctr = 0, signaled = 0;
+  if (warp < PW) {
+    // ---------------- producers: rows warp + 16 i of each item, four at a time
+    const int sub = lane >> 3;  // which of the 4 chunks of a group this lane loads
+    const int pc = lane & 7;    // 16-byte piece within the 128-byte chunk
+    uint32_t base_ctr = 0;      // stage counter of the item's first chunk
     bool ok = true;
     while (ok && items.next(tab, s, start, cnt)) {
       if (tab.rk[s] <= 0) continue;
-      const uint8_t* rowp[8];
+      const int nrows = cnt > warp ? (cnt - warp + PW - 1) / PW : 0;  // <= 8
+      const int nrb = nrows > 4 ? 2 : 1;  // row blocks; a warp without rows still arrives
+      const int tok_mine = lane < nrows ? __ldg(args.seg.token_index + start + warp + PW * lane) : 0;
+      const int npairs = ngroups * nrb;  // (chunk group, row block) steps, group-major
+      // loads rows 4 rb .. 4 rb + 3 of this warp for chunk group g
+      auto load = [&](int p, uint4 (&dst)[4]) {
+        const int g = p / nrb, rb = p - g * nrb;
+        const int k0 = (4 * g + sub) * kShrinkKC + pc * 8;
+        if (kShrinkPrefetch > 0 && rb == 0) {  // lines of group g + kShrinkPrefetch into L2
+          const int kp = (4 * (g + kShrinkPrefetch) + sub) * kShrinkKC;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int r = r0 + 16 * j;
-        rowp[j] = (r < cnt) ? args.x + (int64_t)__ldg(args.seg.token_index + start + r) * args.K * 2
-                            : nullptr;
-      }
-      for (int kc = 0; kc < nkc; ++kc) {
-        const int st = ctr % S;
-        if (!mbar_wait(&empty[st], ((ctr / S) & 1) ^ 1, abort_flag)) {
+          for (int i = 0; i < 8; ++i) {
+            const int tok = __shfl_sync(0xffffffffu, tok_mine, i);
+            if (pc == 0 && i < nrows && kp < args.K) prefetch_l2(args.x + ((int64_t)tok * args.K + kp) * 2);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int i = 4 * rb + j;
+          const int tok = __shfl_sync(0xffffffffu, tok_mine, i);
+          if (i < nrows && k0 < args.K)
+            dst[j] = __ldg(reinterpret_cast<const uint4*>(args.x + ((int64_t)tok * args.K + k0) * 2));
+          else
+            dst[j] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      };
+      // stores step p into its stages; the first row block waits for the
+      // stages to be free, the last one publishes them
+      auto store = [&](int p, const uint4 (&src)[4]) -> bool {
+        const int g = p / nrb, rb = p - g * nrb;
+        if (rb == 0) {
+          for (int q = 0; q < 4; ++q) {
+            const int kc = 4 * g + q;
+            if (kc >= nkc) break;
+            const uint32_t ctr = base_ctr + kc;
+            if (!mbar_wait_warp(&empty[ctr % S], ((ctr / S) & 1) ^ 1, abort_flag)) return false;
+          }
+        }
+        const int kc = 4 * g + sub;
+        const uint32_t st = (base_ctr + kc) % S;
+        if (kc < nkc) {
+          const uint32_t xs = ring + st * stage_bytes;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int i = 4 * rb + j;
+            if (i < nrows) {
+              const int r = warp + PW * i;
+              const uint32_t dst = xs + r * 128 + ((pc ^ (r & 7)) << 4);
+              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(src[j].x),
+                           "r"(src[j].y), "r"(src[j].z), "r"(src[j].w)
+                           : "memory");
+            }
+          }
+        }
+        if (rb == nrb - 1) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (pc == 0 && kc < nkc) mbar_arrive(&full[st]);  // one arrival per warp per stage
+        }
+        return true;
+      };
+      uint4 ra[4], rb_[4];
+      load(0, ra);
+      for (int p = 0; p < npairs; p += 2) {
+        if (p + 1 < npairs) load(p + 1, rb_);
+        if (!store(p, ra)) {
           ok = false;
           break;
         }
-        const int k0 = kc * kShrinkKC + c * 8;
-        const int kleft = args.K - k0;
-        const uint32_t bytes = kleft >= 8 ? 16u : (kleft > 0 ? (uint32_t)kleft * 2u : 0u);
-        const uint32_t xs = smem_u32(smem + st * Cfg::kStageBytes);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (rowp[j] != nullptr) {
-            const int r = r0 + 16 * j;
-            cp_async_16(xs + r * 128 + ((c ^ (r & 7)) << 4), bytes ? rowp[j] + (int64_t)k0 * 2 : rowp[j],
-                        bytes);
-          }
-        }
-        cp_async_commit();
-        ++ctr;
-        if (ctr - signaled == D) {  // oldest group must land before its stage is handed over
-          cp_async_wait_group<D - 1>();
-          fence_proxy_async_smem();
-          mbar_arrive(&full[signaled % S]);
-          ++signaled;
+        if (p + 1 >= npairs) break;
+        if (p + 2 < npairs) load(p + 2, ra);
+        if (!store(p + 1, rb_)) {
+          ok = false;
+          break;
         }
       }
+      base_ctr += nkc;
     }
-    cp_async_wait_group<0>();
-    fence_proxy_async_smem();
-    for (; signaled < ctr; ++signaled) mbar_arrive(&full[signaled % S]);
-  } else if (warp == 4) {
+  } else if (warp == PW) {
     // ---------------- A chunk loader (TMA)
     if (lane == 0) {
       prefetch_tmap(&tmap_a);
@@ -329,12 +388,12 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[st], Cfg::kABytes);
-          tma_load_3d(smem_u32(smem + st * Cfg::kStageBytes + Cfg::kXBytes), &tmap_a, &full[st], 0,
+          tma_load_3d(ring + st * stage_bytes + rows_pad * 128, &tmap_a, &full[st], 0,
                       kc * kShrinkKC, s);
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == PW + 1) {
     // ---------------- MMA issue (one thread)
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(BF16, false, true, kTileM, RP);
@@ -353,8 +412,8 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t xs = smem_u32(smem + st * Cfg::kStageBytes);
-          const uint32_t as = xs + Cfg::kXBytes;
+          const uint32_t xs = ring + st * stage_bytes;
+          const uint32_t as = xs + rows_pad * 128;
 #pragma unroll
           for (int kk = 0; kk < kShrinkKC / 16; ++kk) {
             const uint64_t adesc = smem_desc(xs + kk * 32, 16, 1024, kSwizzle128);
@@ -415,67 +474,78 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   }
 
   __syncthreads();
-  if (warp == 4) {
+  if (warp == PW) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
 }
 
 // ============================================================== expand
+constexpr int kExpandStreamWarps = 16;
+constexpr int kDeltaRowBytes = kExpandNT * 2 + 16;  // padded smem row: conflict-free both ways
+#ifndef PLORA_EXPAND_PREFETCH
+#define PLORA_EXPAND_PREFETCH 4
+#endif
+constexpr int kExpandPrefetch = PLORA_EXPAND_PREFETCH;  // column tiles of the same rows fetched into L2 ahead
+
 template <int RP>
 struct ExpandCfg {
   static constexpr int kBoxBytes = RP * 128;  // RP rows x 64 columns, MN-major SW128
   static constexpr int kBStageBytes = 2 * kBoxBytes;
   static constexpr int kBStageStride = (kBStageBytes + 1023) & ~1023;
   static constexpr int kTmpBytes = kTileM * RP * 2;  // K-major, no swizzle
-  static constexpr int kYStageBytes = kTileM * kYRowBytes;
-  static constexpr int kBStages = RP >= 64 ? 2 : 4;  // LoRA-B tile stages
-  static constexpr int kYStages = RP >= 64 ? 3 : 4;  // y row-tile stages
+  static constexpr int kDeltaBytes = kTileM * kDeltaRowBytes;
+  static constexpr int kBStages = 4;  // LoRA-B tile stages
   static constexpr int kTmemCols = 2 * kExpandNT;
   static constexpr int kBarrierBytes = 512;
-  static constexpr int kTokBytes = 2 * kTileM * 4;
   // + slot table (3 * num_slots + 1 ints), sized at launch
-  static constexpr int kSmemBytes = 1024 + kBStages * kBStageStride + 2 * kTmpBytes +
-                                    kYStages * kYStageBytes + kBarrierBytes + kTokBytes;
-  static_assert(kExpandDepth <= kYStages, "y depth must not exceed the stages");
+  static constexpr int kSmemBytes =
+      1024 + kBStages * kBStageStride + 2 * kTmpBytes + 2 * kDeltaBytes + kBarrierBytes;
 };
 
-// y[t, :] += scale[slot(t)] * tmp[t, :] @ B[slot(t)] (in place).
+// Register set of one stream warp for one unit: four 16-byte y pieces (rows
+// 32 j + 2 w + h, piece c of the 256-byte row segment) and their token rows.
+struct YSet {
+  uint4 v[4];
+  int32_t tok[4];
+  int n0;
+  uint32_t mask;  // bit j: piece j is active
+};
+
+// y[t, :] += round(scale[slot(t)] * tmp[t, :] @ B[slot(t)]) (in place), the
+// reference's order: the fp32 product is scaled, rounded to the activation
+// type, then added to the base output.
 //   warp 0: lane 0 loads the B tile (RP x 128) per unit by TMA.
 //   warp 1: TMEM owner; lane 0 issues RP/16 UMMAs (128 x 128 x 16) per unit.
 //   warp 2: gathers the item's tmp rows (K-major, no swizzle) with cp.async.
-//   warps 4-7: y-row loaders — coalesced 16-byte cp.async (16 threads per
-//           256-byte row segment) into padded smem rows, kExpandDepth units
-//           in flight per thread.
-//   warps 8-15: epilogue — thread = token row, 64 columns: TMEM + smem y ->
-//           smem y; then all 256 threads write the tile back coalesced.
+//   warps 4-7: TMEM readers — thread = token row: scaled, rounded delta rows
+//           into a double-buffered padded smem tile.
+//   warps 8-23: y streams — a half warp per 256-byte row segment, 16-byte
+//           loads issued one unit ahead into registers, delta added from
+//           smem, 16-byte stores back in place.
 template <int RP, bool BF16>
 __global__ void __launch_bounds__(kExpandThreads, 1)
     sgmv_expand_tc_kernel(const __grid_constant__ CUtensorMap tmap_b, const ExpandArgs args) {
   using Cfg = ExpandCfg<RP>;
   using E = Elem<BF16>;
   constexpr int S = Cfg::kBStages;
-  constexpr int YS = Cfg::kYStages;
-  constexpr int YD = kExpandDepth;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* bst_base = smem;
   uint8_t* tmp_base = smem + S * Cfg::kBStageStride;
-  uint8_t* y_base = tmp_base + 2 * Cfg::kTmpBytes;
-  uint64_t* bfull = reinterpret_cast<uint64_t*>(y_base + YS * Cfg::kYStageBytes);
+  uint8_t* d_base = tmp_base + 2 * Cfg::kTmpBytes;
+  uint64_t* bfull = reinterpret_cast<uint64_t*>(d_base + 2 * Cfg::kDeltaBytes);
   uint64_t* bempty = bfull + S;
-  uint64_t* yfull = bempty + S;
-  uint64_t* yempty = yfull + YS;
-  uint64_t* tfull = yempty + YS;
+  uint64_t* tfull = bempty + S;
   uint64_t* tempty = tfull + 2;
   uint64_t* afull = tempty + 2;
   uint64_t* aempty = afull + 2;
-  uint64_t* drain = aempty + 2;
-  uint64_t* esync = drain + 1;  // epilogue-warp rendezvous, one phase per unit
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(esync + 1);
+  uint64_t* dfull = aempty + 2;
+  uint64_t* dempty = dfull + 2;
+  uint64_t* drain = dempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int32_t* tok_e = reinterpret_cast<int32_t*>(y_base + YS * Cfg::kYStageBytes + Cfg::kBarrierBytes);
-  int32_t* tab_mem = tok_e + 2 * kTileM;
+  int32_t* tab_mem = reinterpret_cast<int32_t*>(d_base + 2 * Cfg::kDeltaBytes + Cfg::kBarrierBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -491,18 +561,15 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
       mbar_init(&bfull[i], 1);
       mbar_init(&bempty[i], 1);
     }
-    for (int i = 0; i < YS; ++i) {
-      mbar_init(&yfull[i], 128);  // y loader threads
-      mbar_init(&yempty[i], 8);   // epilogue warps
-    }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 32);
       mbar_init(&tempty[i], 1);
       mbar_init(&afull[i], 1);
-      mbar_init(&aempty[i], 8);
+      mbar_init(&aempty[i], 4);
+      mbar_init(&dfull[i], 4);
+      mbar_init(&dempty[i], kExpandStreamWarps);
     }
     mbar_init(drain, 1);
-    mbar_init(esync, 8);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -613,128 +680,139 @@ __global__ void __launch_bounds__(kExpandThreads, 1)
     }
     cp_async_wait_all();
   } else if (warp >= 4 && warp < 8) {
-    // ---------------- y row loaders: 16 threads per 256-byte row segment
-    const int t = threadIdx.x - 128;  // 0..127
-    const int c = t & 15;             // 16-byte piece
-    const int rr = t >> 4;            // rows rr + 8 k
-    uint32_t yctr = 0, signaled = 0;
-    int64_t prev = -1;
-    int32_t tok[kTileM / 8];
-    bool ok = true;
-    while (ok && units.next(tab, u)) {
-      if (tab.rk[u.slot] <= 0) continue;
-      if (u.item_start != prev) {
-        prev = u.item_start;
-#pragma unroll
-        for (int k = 0; k < kTileM / 8; ++k) {
-          const int r = rr + 8 * k;
-          tok[k] = r < u.cnt ? __ldg(args.seg.token_index + u.item_start + r) : 0;
-        }
-      }
-      const int ys = yctr % YS;
-      if (!mbar_wait(&yempty[ys], ((yctr / YS) & 1) ^ 1, abort_flag)) {
-        ok = false;
-        break;
-      }
-      const int n0 = u.tile * kExpandNT;
-      const bool piece = c * 8 < args.N - n0;  // N % 8 == 0: pieces are all-or-nothing
-      const uint32_t ybuf = smem_u32(y_base + ys * Cfg::kYStageBytes);
-#pragma unroll
-      for (int k = 0; k < kTileM / 8; ++k) {
-        const int r = rr + 8 * k;
-        if (piece && r >= u.t0 && r < u.t1)
-          cp_async_16(ybuf + r * kYRowBytes + c * 16, args.y + ((int64_t)tok[k] * args.N + n0 + c * 8) * 2,
-                      16);
-      }
-      cp_async_commit();
-      ++yctr;
-      if (yctr - signaled == YD) {
-        cp_async_wait_group<YD - 1>();
-        mbar_arrive(&yfull[signaled % YS]);
-        ++signaled;
-      }
-    }
-    cp_async_wait_group<0>();
-    for (; signaled < yctr; ++signaled) mbar_arrive(&yfull[signaled % YS]);
-  } else if (warp >= 8) {
-    // ---------------- epilogue
-    const int q = warp & 3;         // TMEM lane quarter
-    const int h = (warp - 8) >> 2;  // column half of the 128-column tile
-    const int r = q * 32 + lane;    // token row of the compute phase
-    const int et = threadIdx.x - 256;  // 0..255 in the write-back phase
-    uint32_t unit_ctr = 0, item_ctr = 0;
-    int64_t prev = -1;
-    int32_t* tokb = tok_e;
+    // ---------------- TMEM readers: scaled, rounded delta rows -> smem
+    const int q = warp & 3;       // TMEM lane quarter
+    const int r = q * 32 + lane;  // token row of the item
+    uint32_t unit_ctr = 0;
     while (units.next(tab, u)) {
       if (tab.rk[u.slot] <= 0) continue;
-      if (u.item_start != prev) {
-        prev = u.item_start;
-        tokb = tok_e + (item_ctr & 1) * kTileM;
-        ++item_ctr;
-        if (et < kTileM) tokb[et] = et < u.cnt ? __ldg(args.seg.token_index + u.item_start + et) : 0;
-      }
       const float scale = tab.sc[u.slot];
-      const int n0 = u.tile * kExpandNT;
-      const int ncols = min(64, args.N - n0 - h * 64);  // multiple of 8 (N % 8 == 0)
-      const bool active = (r >= u.t0) && (r < u.t1) && ncols > 0;
       const int ab = unit_ctr & 1;
-      const int ys = unit_ctr % YS;
-      if (!mbar_wait_warp(&afull[ab], (unit_ctr >> 1) & 1, abort_flag)) break;
+      const uint32_t ph = (unit_ctr >> 1) & 1;
+      if (!mbar_wait_warp(&afull[ab], ph, abort_flag)) break;
+      if (!mbar_wait_warp(&dempty[ab], ph ^ 1, abort_flag)) break;
       tc_fence_after();
-      uint32_t acc[4][16];
+      const uint32_t drow = smem_u32(d_base + ab * Cfg::kDeltaBytes) + r * kDeltaRowBytes;
 #pragma unroll
-      for (int g = 0; g < 4; ++g)
-        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + ab * kExpandNT + h * 64 + g * 16,
-                  acc[g]);
-      tmem_wait_ld();
+      for (int qc = 0; qc < kExpandNT / 32; ++qc) {
+        uint32_t acc[2][16];
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + ab * kExpandNT + qc * 32;
+        tmem_ld16(taddr, acc[0]);
+        tmem_ld16(taddr + 16, acc[1]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int j = c * 8 + 2 * i;
+            const float a0 = scale * __uint_as_float(acc[j >> 4][j & 15]);
+            const float a1 = scale * __uint_as_float(acc[(j + 1) >> 4][(j + 1) & 15]);
+            w[i] = (uint32_t)E::from_f(a0) | ((uint32_t)E::from_f(a1) << 16);
+          }
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(drow + qc * 64 + c * 16),
+                       "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                       : "memory");
+        }
+      }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&aempty[ab]);
-      if (!mbar_wait_warp(&yfull[ys], (unit_ctr / YS) & 1, abort_flag)) break;
-      const uint32_t ybuf = smem_u32(y_base + ys * Cfg::kYStageBytes);
-      const uint32_t yrow = ybuf + r * kYRowBytes + h * 128;
-      if (active) {
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          if (c * 8 < ncols) {
-            uint32_t in[4];
-            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                         : "=r"(in[0]), "=r"(in[1]), "=r"(in[2]), "=r"(in[3])
-                         : "r"(yrow + c * 16));
-            uint32_t out[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int j = c * 8 + 2 * i;
-              const float a0 = __uint_as_float(acc[j >> 4][j & 15]);
-              const float a1 = __uint_as_float(acc[(j + 1) >> 4][(j + 1) & 15]);
-              const float y0 = E::to_f((uint16_t)(in[i] & 0xFFFFu)) + scale * a0;
-              const float y1 = E::to_f((uint16_t)(in[i] >> 16)) + scale * a1;
-              out[i] = (uint32_t)E::from_f(y0) | ((uint32_t)E::from_f(y1) << 16);
-            }
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(yrow + c * 16),
-                         "r"(out[0]), "r"(out[1]), "r"(out[2]), "r"(out[3])
-                         : "memory");
-          }
-        }
+      if (lane == 0) {
+        mbar_arrive(&aempty[ab]);
+        mbar_arrive(&dfull[ab]);
       }
-      // the whole tile is updated and the item's token ids are visible
-      __syncwarp();
-      if (lane == 0) mbar_arrive(esync);
-      if (!mbar_wait_warp(esync, unit_ctr & 1, abort_flag)) break;
-      const int wc = et & 15;
-      if (wc * 8 < args.N - n0) {
-        for (int wr = u.t0 + (et >> 4); wr < u.t1; wr += 16) {
-          uint32_t v[4];
-          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
-                       : "r"(ybuf + wr * kYRowBytes + wc * 16));
-          *reinterpret_cast<uint4*>(args.y + ((int64_t)tokb[wr] * args.N + n0 + wc * 8) * 2) =
-              make_uint4(v[0], v[1], v[2], v[3]);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&yempty[ys]);
       ++unit_ctr;
+    }
+  } else if (warp >= 8) {
+    // ---------------- y streams
+    const int sw = warp - 8;  // 0..15
+    const int hr = 2 * sw + (lane >> 4);
+    const int c = lane & 15;
+    ExpandUnits pre = units;  // prefetch cursor, one active unit ahead
+    int64_t p_item = -1;
+    int32_t p_tok[4] = {0, 0, 0, 0};
+    // issues the loads of the next active unit of `pre` into `set`
+    auto prefetch = [&](YSet& set) -> bool {
+      ExpandUnit pu;
+      bool found = false;
+      while (pre.next(tab, pu)) {
+        if (tab.rk[pu.slot] > 0) {
+          found = true;
+          break;
+        }
+      }
+      if (!found) return false;
+      // lanes c = 0 and c = 8 own the two 128-byte lines of a row segment
+      auto prefetch_tile = [&](int tile) {
+        const int col = tile * kExpandNT + c * 8;
+        if ((c & 7) == 0 && col < args.N) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (32 * j + hr < pu.cnt) prefetch_l2(args.y + ((int64_t)p_tok[j] * args.N + col) * 2);
+        }
+      };
+      if (pu.item_start != p_item) {
+        p_item = pu.item_start;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int r = 32 * j + hr;
+          p_tok[j] = r < pu.cnt ? __ldg(args.seg.token_index + pu.item_start + r) : 0;
+        }
+        for (int a = 1; a < kExpandPrefetch; ++a) prefetch_tile(pu.tile + a);
+      }
+      prefetch_tile(pu.tile + kExpandPrefetch);
+      set.n0 = pu.tile * kExpandNT;
+      const bool piece = c * 8 < args.N - set.n0;  // N % 8 == 0: pieces are all-or-nothing
+      set.mask = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int r = 32 * j + hr;
+        set.tok[j] = p_tok[j];
+        if (piece && r >= pu.t0 && r < pu.t1) {
+          set.mask |= 1u << j;
+          set.v[j] = *reinterpret_cast<const uint4*>(args.y + ((int64_t)p_tok[j] * args.N + set.n0 + c * 8) * 2);
+        }
+      }
+      return true;
+    };
+    // adds the delta tile of unit `unit_ctr` to `set` and stores it
+    auto apply = [&](YSet& set, uint32_t unit_ctr) -> bool {
+      const int db = unit_ctr & 1;
+      if (!mbar_wait_warp(&dfull[db], (unit_ctr >> 1) & 1, abort_flag)) return false;
+      const uint32_t dtile = smem_u32(d_base + db * Cfg::kDeltaBytes);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (set.mask & (1u << j)) {
+          const int r = 32 * j + hr;
+          uint32_t d[4];
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                       : "r"(dtile + r * kDeltaRowBytes + c * 16));
+          uint32_t yv[4] = {set.v[j].x, set.v[j].y, set.v[j].z, set.v[j].w};
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float y0 = E::to_f((uint16_t)(yv[i] & 0xFFFFu)) + E::to_f((uint16_t)(d[i] & 0xFFFFu));
+            const float y1 = E::to_f((uint16_t)(yv[i] >> 16)) + E::to_f((uint16_t)(d[i] >> 16));
+            o[i] = (uint32_t)E::from_f(y0) | ((uint32_t)E::from_f(y1) << 16);
+          }
+          *reinterpret_cast<uint4*>(args.y + ((int64_t)set.tok[j] * args.N + set.n0 + c * 8) * 2) =
+              make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dempty[db]);
+      return true;
+    };
+    YSet s0, s1;
+    uint32_t unit_ctr = 0;
+    bool have = prefetch(s0);
+    while (have) {
+      bool more = prefetch(s1);
+      if (!apply(s0, unit_ctr++)) break;
+      if (!more) break;
+      have = prefetch(s0);
+      if (!apply(s1, unit_ctr++)) break;
     }
   }
 
