@@ -175,6 +175,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// 5-D tiled TMA load (box starting at (0, 0, 0, 0, c4)), completing on `bar`.
+__device__ __forceinline__ void tma_load_5d_outer(uint32_t dst, const void* tmap, uint64_t* bar,
+                                                  int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %3, %3, %3, %4}], [%2];" ::"r"(dst),
+      "l"(tmap), "r"(smem_u32(bar)), "r"(0), "r"(c4)
+      : "memory");
+}
+
 // Four rows (row0..row3) x box width of a 2-D tensor into consecutive rows of
 // shared memory (tile::gather4; the tensor map's box is one row high).
 __device__ __forceinline__ void tma_gather4(uint32_t dst, const void* tmap, uint64_t* bar, int col,

@@ -129,6 +129,29 @@ int make_map_3d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, uint
   return PLORA_OK;
 }
 
+// LoRA-A (num_slots, K, R) viewed as 5-D (R, e:2, m:4, cc:4, block) with
+// row k = 32 block + 8 m + 2 cc + e, so that a box lands each 32-row block
+// in (cc, m, e) order: shared-memory row position 8 cc + 2 m + e.  Slots are
+// folded into the block index (K % 32 == 0); the box covers `blocks` blocks.
+int make_map_lora_a_blocks(CUtensorMap* map, const void* base, int dtype, uint64_t R, uint64_t K,
+                           uint64_t num_slots, uint32_t blocks, CUtensorMapSwizzle swz) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const uint64_t row = R * 2;
+  const cuuint64_t dims[5] = {R, 2, 4, 4, num_slots * (K / 32)};
+  const cuuint64_t strides[4] = {row, 8 * row, 2 * row, 32 * row};
+  const cuuint32_t box[5] = {(cuuint32_t)R, 2, 4, 4, blocks};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUtensorMapDataType dt = dtype == PLORA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, dt, 5, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled (LoRA-A blocks) failed (%d)", (int)r);
+  return PLORA_OK;
+}
+
 // 2-D tiled map over a contiguous (d1, d0) 16-bit tensor.
 [[maybe_unused]] int make_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, uint64_t d1,
                 uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz) {
@@ -225,16 +248,18 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
   args.K = (int32_t)K;
   args.R = (int32_t)R;
   args.stack_num = stack_num;
-  const bool tc = dtype != PLORA_DTYPE_F32 && tc_rank_ok(R) && K % 8 == 0 &&
+  const bool tc = dtype != PLORA_DTYPE_F32 && tc_rank_ok(R) && K % 32 == 0 &&
                   seg.num_slots <= kTcMaxSlots && aligned16(x) &&
                   aligned16(a) && aligned16(tmp);
   if (tc) {
-    CUtensorMap map;
+    CUtensorMap map8, map1;
     const CUtensorMapSwizzle swz = R == 16   ? CU_TENSOR_MAP_SWIZZLE_32B
                                    : R == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
                                              : CU_TENSOR_MAP_SWIZZLE_128B;
-    if ((st = make_map_3d(&map, a, dtype, (uint64_t)R, (uint64_t)K, (uint64_t)seg.num_slots,
-                          (uint32_t)R, kWinBoxRows, swz)))
+    if ((st = make_map_lora_a_blocks(&map8, a, dtype, (uint64_t)R, (uint64_t)K,
+                                     (uint64_t)seg.num_slots, kWinBoxRows / 32, swz)) ||
+        (st = make_map_lora_a_blocks(&map1, a, dtype, (uint64_t)R, (uint64_t)K,
+                                     (uint64_t)seg.num_slots, 1, swz)))
       return st;
     (void)num_tokens;
     const dim3 grid(di->sm_count), block(kMmaThreads);
@@ -243,10 +268,10 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
 #define LAUNCH_SHRINK(RPV)                                                                     \
   if (bf)                                                                                      \
     sgmv_shrink_mma_kernel<RPV, true><<<grid, block, ShrinkMmaCfg<RPV>::kSmemBytes + tb, stream>>>( \
-        map, args);                                                                            \
+        map8, map1, args);                                                                     \
   else                                                                                         \
     sgmv_shrink_mma_kernel<RPV, false><<<grid, block, ShrinkMmaCfg<RPV>::kSmemBytes + tb, stream>>>( \
-        map, args);
+        map8, map1, args);
     if (R == 16) {
       LAUNCH_SHRINK(16)
     } else if (R == 32) {

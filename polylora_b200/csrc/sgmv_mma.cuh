@@ -2,12 +2,14 @@
 //
 // The shrink is a gather-and-reduce over HBM: every active token reads its
 // K-wide row of x once, and the rank-R reduction is tiny.  Its speed is set by
-// how many bytes each SM keeps in flight, so x never passes through shared
-// memory: each warp loads 16 bytes per lane (a quad of lanes covers 64
-// contiguous bytes of one row), regroups the words across the quad into
-// mma.sync fragments and multiplies against the slot's LoRA-A weights, which
-// are the only operand staged in shared memory (64 KB windows by TMA,
-// swizzled so that ldmatrix.trans reads them without bank conflicts).
+// how many bytes each SM keeps in flight and how few instructions it spends
+// per byte, so x never passes through shared memory: each lane loads 16 bytes
+// (8 consecutive k of one token) and those four registers are, as they are,
+// the B fragments of two m16n8k16 steps of D^T = A^T x^T.  The k order this
+// implies inside a 32-column block (lane quad t owns k = 8t .. 8t + 7) is
+// applied to the LoRA-A rows instead: a 5-D TMA view writes each 32-row block
+// of the slot's weights in the order the ldmatrix.trans fragments read them,
+// so every 8x8 matrix is 8 consecutive swizzled rows (no bank conflicts).
 //
 // Work split: a CTA takes a contiguous share of the slot-ordered token list,
 // cut into items of <= 128 tokens of one slot.  An item is 16-token tiles x
@@ -24,14 +26,15 @@ namespace plora {
 constexpr int kMmaWarps = 16;                      // compute warps
 constexpr int kMmaThreads = kMmaWarps * 32;
 constexpr int kWinBytes = 64 * 1024;               // one LoRA weight window
-constexpr int kWinBoxRows = 256;                   // rows per weight TMA box
+constexpr int kWinBoxRows = 256;                   // rows per weight TMA box (8 blocks of 32)
 
 template <int RP>
 struct ShrinkMmaCfg {
   static constexpr int kWinRows = kWinBytes / (RP * 2);  // K rows per window
   static constexpr int kBoxBytes = kWinBoxRows * RP * 2;
-  static constexpr int kNT = RP / 8;                      // n8 tiles of the rank
-  static constexpr int kU = RP == 16 ? 4 : (RP == 32 ? 3 : 2);  // 32-column blocks per load batch
+  // 32-column blocks per load batch (two batches alternate); larger batches
+  // spill at the 128-register budget of 16 warps and measured slower
+  static constexpr int kU = RP == 64 ? 2 : 4;
   static constexpr int kPartBytes = kMmaWarps * 16 * RP * 4;    // one 16 x RP fp32 tile per warp
   static constexpr int kBarrierBytes = 64;
   // + slot table (3 * num_slots + 1 ints), sized at launch
@@ -99,9 +102,10 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
   }
 }
 
-// Shared-memory byte offset of 16-byte chunk j of row k of a weight window
-// written by TMA with the swizzle that matches its row width (32/64/128 B
-// for RP = 16/32/64): the chunk index is XORed with address bits 7 and up.
+// Shared-memory byte offset of 16-byte chunk j of row position k of a weight
+// window written by TMA with the swizzle that matches its row width (32/64/128
+// B for RP = 16/32/64): the chunk index is XORed with address bits 7 and up.
+// Within a 32-row block, position 8 cc + 2 m + e holds weight row 8 m + 2 cc + e.
 template <int RP>
 __device__ __forceinline__ uint32_t win_offset(int k, int j) {
   constexpr int kRowBytes = RP * 2;
@@ -143,7 +147,8 @@ struct WinCursor {
 // issued at start, and the last warp to release window c issues c + 2.
 template <int RP, bool BF16>
 __global__ void __launch_bounds__(kMmaThreads, 1)
-    sgmv_shrink_mma_kernel(const __grid_constant__ CUtensorMap tmap_a, const ShrinkArgs args) {
+    sgmv_shrink_mma_kernel(const __grid_constant__ CUtensorMap tmap_a8,
+                           const __grid_constant__ CUtensorMap tmap_a1, const ShrinkArgs args) {
   using Cfg = ShrinkMmaCfg<RP>;
   using E = Elem<BF16>;
   constexpr int W = Cfg::kWinRows;
@@ -167,13 +172,15 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   const SlotTab tab = stage_slot_tab(args.seg, args.ranks, nullptr, tab_mem);
   const int K = args.K;
   const int nwin = (K + W - 1) / W;
+  const int kblocks = K >> 5;  // 32-row blocks per slot
   auto issue = [&](const WinCursor& wc, int b) {  // one thread
-    const int rows = min(W, K - wc.w * W);
-    const int boxes = (rows + kWinBoxRows - 1) / kWinBoxRows;
-    mbar_arrive_expect_tx(&full[b], boxes * Cfg::kBoxBytes);
-    for (int q = 0; q < boxes; ++q)
-      tma_load_3d(smem_u32(smem + b * kWinBytes + q * Cfg::kBoxBytes), &tmap_a, &full[b], 0,
-                  wc.w * W + q * kWinBoxRows, wc.slot);
+    const int nb = min(W, K - wc.w * W) >> 5;
+    mbar_arrive_expect_tx(&full[b], nb * 32 * RP * 2);
+    const int blk0 = wc.slot * kblocks + wc.w * (W >> 5);
+    const uint32_t dst = smem_u32(smem + b * kWinBytes);
+    int q = 0;
+    for (; q + 8 <= nb; q += 8) tma_load_5d_outer(dst + q * 32 * RP * 2, &tmap_a8, &full[b], blk0 + q);
+    for (; q < nb; ++q) tma_load_5d_outer(dst + q * 32 * RP * 2, &tmap_a1, &full[b], blk0 + q);
   };
   __syncthreads();  // slot table staged
   WinCursor ic;     // the window this warp would issue after its next release
@@ -183,7 +190,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     released[0] = released[1] = 0;
     *abort_flag = 0;
     fence_barrier_init();
-    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_a8);
+    prefetch_tmap(&tmap_a1);
     for (int b = 0; b < 2 && ic.valid; ++b) {
       issue(ic, b);
       ic.advance(tab);
@@ -258,9 +266,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       }
     };
 
-    float acc[Cfg::kNT][4];
+    float acc[RP / 16][2][4];  // D^T tiles: rank rows 16 rt .., tokens 8 nt ..
 #pragma unroll
-    for (int j = 0; j < Cfg::kNT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    for (int rt = 0; rt < RP / 16; ++rt)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) acc[rt][nt][0] = acc[rt][nt][1] = acc[rt][nt][2] = acc[rt][nt][3] = 0.f;
     int cw = -1;  // window of this item the warp currently holds
     // releases the held window; the last of the 16 releasers refills its buffer
     auto release = [&]() {
@@ -289,21 +299,22 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       for (int u = 0; u < U; ++u) {
         if (mc.w >= nwin) break;
         hold(mc.w);
-        uint32_t a0[4] = {B.x0[u].x, B.x0[u].y, B.x0[u].z, B.x0[u].w};
-        uint32_t a1[4] = {B.x1[u].x, B.x1[u].y, B.x1[u].z, B.x1[u].w};
-        quad_transpose(a0, t);
-        quad_transpose(a1, t);
-        // k16 step s: cols 16 s + {2t, 2t + 1} and 16 s + 8 + {2t, 2t + 1}
-        const uint32_t fa[2][4] = {{a0[0], a1[0], a0[1], a1[1]}, {a0[2], a1[2], a0[3], a1[3]}};
-        const int krow = mc.blk * 32 + 8 * (lane >> 3) + (lane & 7);
+        // B fragments of k16 step s: tokens g (x0) and 8 + g (x1), k = 8t + 4s + {0,1} / {2,3}
+        const uint32_t fb0[2][2] = {{B.x0[u].x, B.x0[u].y}, {B.x0[u].z, B.x0[u].w}};
+        const uint32_t fb1[2][2] = {{B.x1[u].x, B.x1[u].y}, {B.x1[u].z, B.x1[u].w}};
         const uint32_t wb = win_base + ((c_base + mc.w) & 1) * kWinBytes;
+        const int mi = lane >> 3;
 #pragma unroll
-        for (int j = 0; j < Cfg::kNT; ++j) {
-          uint32_t bf[4];
-          ldsm_x4_trans(wb + win_offset<RP>(krow, j), bf);
-          if (ok) {
-            mma_16816<BF16>(acc[j], fa[0], bf[0], bf[1]);
-            mma_16816<BF16>(acc[j], fa[1], bf[2], bf[3]);
+        for (int st = 0; st < 2; ++st) {
+          const int pos = mc.blk * 32 + (2 * st + (mi >> 1)) * 8 + (lane & 7);
+#pragma unroll
+          for (int rt = 0; rt < RP / 16; ++rt) {
+            uint32_t fa[4];
+            ldsm_x4_trans(wb + win_offset<RP>(pos, 2 * rt + (mi & 1)), fa);
+            if (ok) {
+              mma_16816<BF16>(acc[rt][0], fa, fb0[st][0], fb0[st][1]);
+              mma_16816<BF16>(acc[rt][1], fa, fb1[st][0], fb1[st][1]);
+            }
           }
         }
         step(mc);
@@ -327,13 +338,18 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     c_base += nwin;
 
     // partial sums -> shared memory -> reduced, rounded rows of tmp
-    if (active) {
+    if (active) {  // part[warp][token 0..15][rank]
       float* p = part + (size_t)warp * 16 * RP;
 #pragma unroll
-      for (int j = 0; j < Cfg::kNT; ++j) {
-        *reinterpret_cast<float2*>(p + g * RP + 8 * j + 2 * t) = make_float2(acc[j][0], acc[j][1]);
-        *reinterpret_cast<float2*>(p + (g + 8) * RP + 8 * j + 2 * t) = make_float2(acc[j][2], acc[j][3]);
-      }
+      for (int rt = 0; rt < RP / 16; ++rt)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int tk = 8 * nt + 2 * t, r = 16 * rt + g;
+          p[tk * RP + r] = acc[rt][nt][0];
+          p[(tk + 1) * RP + r] = acc[rt][nt][1];
+          p[tk * RP + r + 8] = acc[rt][nt][2];
+          p[(tk + 1) * RP + r + 8] = acc[rt][nt][3];
+        }
     }
     named_barrier(1, kMmaWarps * 32);
     const int n_eff = min(rank * args.stack_num, args.R);

@@ -96,6 +96,8 @@ TC_CASES = [
     (9, 300, 1, 200, 200, 11, 16, [0, 16], "bfloat16"),
     (10, 64, 3, 1024, 2048, 17, 16, [4, 16], "float16"),
     (11, 2, 1000, 256, 128, 3, 16, [16], "bfloat16"),
+    (12, 40, 2, 800, 640, 6, 16, [4, 8, 16], "bfloat16"),  # K = 3 x 256 + 32: single-block tail boxes
+    (13, 50, 1, 224, 96, 4, 32, [8, 32], "bfloat16"),  # K = 7 x 32: tail boxes only
 ]
 
 
