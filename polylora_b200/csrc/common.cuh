@@ -175,6 +175,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// 4-D tiled TMA load (box starting at (0, 0, c2, c3)), completing on `bar`.
+__device__ __forceinline__ void tma_load_4d_outer(uint32_t dst, const void* tmap, uint64_t* bar,
+                                                  int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(tmap), "r"(smem_u32(bar)), "r"(0), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 // 5-D tiled TMA load (box starting at (0, 0, 0, 0, c4)), completing on `bar`.
 __device__ __forceinline__ void tma_load_5d_outer(uint32_t dst, const void* tmap, uint64_t* bar,
                                                   int c4) {

@@ -84,12 +84,12 @@ int device_info(DeviceInfo** out) {
     SET_SMEM((sgmv_shrink_mma_kernel<16, false>), ShrinkMmaCfg<16>::kSmemBytes);
     SET_SMEM((sgmv_shrink_mma_kernel<32, false>), ShrinkMmaCfg<32>::kSmemBytes);
     SET_SMEM((sgmv_shrink_mma_kernel<64, false>), ShrinkMmaCfg<64>::kSmemBytes);
-    SET_SMEM((sgmv_expand_tc_kernel<16, true>), ExpandCfg<16>::kSmemBytes);
-    SET_SMEM((sgmv_expand_tc_kernel<32, true>), ExpandCfg<32>::kSmemBytes);
-    SET_SMEM((sgmv_expand_tc_kernel<64, true>), ExpandCfg<64>::kSmemBytes);
-    SET_SMEM((sgmv_expand_tc_kernel<16, false>), ExpandCfg<16>::kSmemBytes);
-    SET_SMEM((sgmv_expand_tc_kernel<32, false>), ExpandCfg<32>::kSmemBytes);
-    SET_SMEM((sgmv_expand_tc_kernel<64, false>), ExpandCfg<64>::kSmemBytes);
+    SET_SMEM((sgmv_expand_mma_kernel<16, true>), ExpandMmaCfg<16>::kSmemBytes);
+    SET_SMEM((sgmv_expand_mma_kernel<32, true>), ExpandMmaCfg<32>::kSmemBytes);
+    SET_SMEM((sgmv_expand_mma_kernel<64, true>), ExpandMmaCfg<64>::kSmemBytes);
+    SET_SMEM((sgmv_expand_mma_kernel<16, false>), ExpandMmaCfg<16>::kSmemBytes);
+    SET_SMEM((sgmv_expand_mma_kernel<32, false>), ExpandMmaCfg<32>::kSmemBytes);
+    SET_SMEM((sgmv_expand_mma_kernel<64, false>), ExpandMmaCfg<64>::kSmemBytes);
 #undef SET_SMEM
     d.attrs_set = true;
   }
@@ -112,7 +112,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 // 3-D tiled map over a contiguous (d2, d1, d0) 16-bit tensor.
-int make_map_3d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, uint64_t d1,
+[[maybe_unused]] int make_map_3d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, uint64_t d1,
                 uint64_t d2, uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz) {
   auto enc = tensor_map_encoder();
   if (!enc) return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -149,6 +149,27 @@ int make_map_lora_a_blocks(CUtensorMap* map, const void* base, int dtype, uint64
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled (LoRA-A blocks) failed (%d)", (int)r);
+  return PLORA_OK;
+}
+
+// LoRA-B (num_slots, R, N) viewed as 4-D (64 columns, R, N / 64 chunks, slot):
+// a box lands `chunks` 64-column chunks of all R rows, chunk-major, each chunk
+// R rows of 128 bytes with the 128-byte swizzle.  Requires N % 64 == 0.
+int make_map_lora_b_chunks(CUtensorMap* map, const void* base, int dtype, uint64_t R, uint64_t N,
+                           uint64_t num_slots, uint32_t chunks) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[4] = {64, R, N / 64, num_slots};
+  const cuuint64_t strides[3] = {N * 2, 128, R * N * 2};
+  const cuuint32_t box[4] = {64, (cuuint32_t)R, chunks, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt = dtype == PLORA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled (LoRA-B chunks) failed (%d)", (int)r);
   return PLORA_OK;
 }
 
@@ -307,24 +328,29 @@ int expand_impl(const void* tmp, const void* b, void* y, const int32_t* ranks, c
   args.seg = seg;
   args.R = (int32_t)R;
   args.N = (int32_t)N;
-  const bool tc = dtype != PLORA_DTYPE_F32 && tc_rank_ok(R) && N % 8 == 0 &&
+  const bool tc = dtype != PLORA_DTYPE_F32 && tc_rank_ok(R) && N % 64 == 0 &&
                   seg.num_slots <= kTcMaxSlots && aligned16(tmp) &&
                   aligned16(b) && aligned16(y);
   if (tc) {
-    CUtensorMap map;
-    if ((st = make_map_3d(&map, b, dtype, (uint64_t)N, (uint64_t)R, (uint64_t)seg.num_slots, 64,
-                          (uint32_t)R, CU_TENSOR_MAP_SWIZZLE_128B)))
+    CUtensorMap mapn, map1;
+    const uint32_t box = R == 16 ? ExpandMmaCfg<16>::kBoxChunks
+                         : R == 32 ? ExpandMmaCfg<32>::kBoxChunks
+                                   : ExpandMmaCfg<64>::kBoxChunks;
+    if ((st = make_map_lora_b_chunks(&mapn, b, dtype, (uint64_t)R, (uint64_t)N,
+                                     (uint64_t)seg.num_slots, box)) ||
+        (st = make_map_lora_b_chunks(&map1, b, dtype, (uint64_t)R, (uint64_t)N,
+                                     (uint64_t)seg.num_slots, 1)))
       return st;
-    const dim3 grid(di->sm_count), block(kExpandThreads);
+    const dim3 grid(di->sm_count), block(kMmaThreads);
     const size_t tb = tab_bytes(seg.num_slots);
     const bool bf = dtype == PLORA_DTYPE_BF16;
-#define LAUNCH_EXPAND(RPV)                                                               \
-  if (bf)                                                                                \
-    sgmv_expand_tc_kernel<RPV, true><<<grid, block, ExpandCfg<RPV>::kSmemBytes + tb, stream>>>( \
-        map, args);                                                                      \
-  else                                                                                   \
-    sgmv_expand_tc_kernel<RPV, false><<<grid, block, ExpandCfg<RPV>::kSmemBytes + tb, stream>>>( \
-        map, args);
+#define LAUNCH_EXPAND(RPV)                                                                     \
+  if (bf)                                                                                      \
+    sgmv_expand_mma_kernel<RPV, true><<<grid, block, ExpandMmaCfg<RPV>::kSmemBytes + tb, stream>>>( \
+        mapn, map1, args);                                                                     \
+  else                                                                                         \
+    sgmv_expand_mma_kernel<RPV, false><<<grid, block, ExpandMmaCfg<RPV>::kSmemBytes + tb, stream>>>( \
+        mapn, map1, args);
     if (R == 16) {
       LAUNCH_EXPAND(16)
     } else if (R == 32) {
@@ -333,7 +359,7 @@ int expand_impl(const void* tmp, const void* b, void* y, const int32_t* ranks, c
       LAUNCH_EXPAND(64)
     }
 #undef LAUNCH_EXPAND
-    return check_launch("sgmv_expand_tc_kernel");
+    return check_launch("sgmv_expand_mma_kernel");
   }
   if (R > kSimtMaxRank) return fail(PLORA_ERR_UNSUPPORTED, "max_rank %lld > %d", (long long)R, kSimtMaxRank);
   const dim3 grid(di->sm_count * 8), block(kSimtThreads);

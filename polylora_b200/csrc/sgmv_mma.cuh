@@ -34,7 +34,7 @@ struct ShrinkMmaCfg {
   static constexpr int kBoxBytes = kWinBoxRows * RP * 2;
   // 32-column blocks per load batch (two batches alternate); larger batches
   // spill at the 128-register budget of 16 warps and measured slower
-  static constexpr int kU = RP == 64 ? 2 : 4;
+  static constexpr int kU = RP == 16 ? 4 : (RP == 32 ? 3 : 2);
   static constexpr int kPartBytes = kMmaWarps * 16 * RP * 4;    // one 16 x RP fp32 tile per warp
   static constexpr int kBarrierBytes = 64;
   // + slot table (3 * num_slots + 1 ints), sized at launch
@@ -378,6 +378,270 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       *reinterpret_cast<uint4*>(args.tmp + (tok * args.R + cg * 8) * 2) = make_uint4(o[0], o[1], o[2], o[3]);
     }
     named_barrier(1, kMmaWarps * 32);
+  }
+}
+
+// ============================================================== expand
+// y[t, :] += round(scale * tmp[t, :] @ B[slot(t)]) in place, with the
+// reference's rounding order (the fp32 product is scaled and rounded to the
+// activation type, then added to the base output and rounded again).
+//
+// The y rows are the only large stream (read and written once), so they stay
+// in registers: a lane loads 16 bytes (8 consecutive columns) of a token row,
+// the mma.sync D fragments of the matching 32-column block are rounded, packed
+// and regrouped across the lane quad so that each lane holds the delta of its
+// own 8 columns, added, and stored back.  tmp rows (R values per token) are
+// loaded once per tile as A fragments; the slot's LoRA-B rows stream through
+// 64 KB windows (a 4-D TMA view lands 64-column chunks of all R rows, 128-byte
+// swizzled, so ldmatrix.trans reads them without bank conflicts).
+//
+// Work split: as the shrink, items of <= 128 tokens of one slot inside the
+// CTA's token share; an item is 16-token tiles x column ranges of each window.
+//
+// Reference semantics: src/polylora/sgmv.py:178-275 (_sgmv_lora_b_kernel).
+template <int RP>
+struct ExpandMmaCfg {
+  static constexpr int kWinCols = kWinBytes / (RP * 2);  // N columns per window
+  static constexpr int kChunkBytes = RP * 128;           // 64 columns x RP rows
+  static constexpr int kBoxChunks = kWinCols / 64 < 16 ? kWinCols / 64 : 16;
+  static constexpr int kU = RP == 64 ? 2 : 3;            // 32-column blocks per load batch
+  static constexpr int kBarrierBytes = 64;
+  // + slot table (3 * num_slots + 1 ints), sized at launch
+  static constexpr int kSmemBytes = 1024 + 2 * kWinBytes + kBarrierBytes;
+};
+
+template <int RP, bool BF16>
+__global__ void __launch_bounds__(kMmaThreads, 1)
+    sgmv_expand_mma_kernel(const __grid_constant__ CUtensorMap tmap_bn,
+                           const __grid_constant__ CUtensorMap tmap_b1, const ExpandArgs args) {
+  using Cfg = ExpandMmaCfg<RP>;
+  using E = Elem<BF16>;
+  constexpr int W = Cfg::kWinCols;
+  constexpr int U = Cfg::kU;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kWinBytes);
+  uint32_t* released = reinterpret_cast<uint32_t*>(full + 2);  // per buffer, monotonic
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(released + 2);
+  int32_t* tab_mem = reinterpret_cast<int32_t*>(smem + 2 * kWinBytes + Cfg::kBarrierBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t total = __ldg(args.seg.slot_start + args.seg.num_slots);
+  const int64_t begin = total * blockIdx.x / gridDim.x;
+  const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
+  if (begin >= end) return;  // uniform across the CTA
+
+  const SlotTab tab = stage_slot_tab(args.seg, args.ranks, args.scales, tab_mem);
+  const int N = args.N;
+  const int nwin = (N + W - 1) / W;
+  const int nchunks = N >> 6;  // 64-column chunks per row
+  auto issue = [&](const WinCursor& wc, int b) {  // one thread
+    const int nc = min(W, N - wc.w * W) >> 6;
+    mbar_arrive_expect_tx(&full[b], nc * Cfg::kChunkBytes);
+    const int ch0 = wc.w * (W >> 6);
+    const uint32_t dst = smem_u32(smem + b * kWinBytes);
+    int q = 0;
+    for (; q + Cfg::kBoxChunks <= nc; q += Cfg::kBoxChunks)
+      tma_load_4d_outer(dst + q * Cfg::kChunkBytes, &tmap_bn, &full[b], ch0 + q, wc.slot);
+    for (; q < nc; ++q) tma_load_4d_outer(dst + q * Cfg::kChunkBytes, &tmap_b1, &full[b], ch0 + q, wc.slot);
+  };
+  (void)nchunks;
+  __syncthreads();  // slot table staged
+  WinCursor ic;     // the window this warp would issue after its next release
+  ic.init(tab, begin, end, nwin);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) mbar_init(&full[i], 1);
+    released[0] = released[1] = 0;
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmap_bn);
+    prefetch_tmap(&tmap_b1);
+    for (int b = 0; b < 2 && ic.valid; ++b) {
+      issue(ic, b);
+      ic.advance(tab);
+    }
+  } else {
+    ic.advance(tab);
+    ic.advance(tab);
+  }
+  __syncthreads();
+
+  ShrinkItems items;
+  items.init(tab, begin, end);
+  int s, cnt;
+  int64_t start;
+  const int g = lane >> 2;  // fragment row group
+  const int t = lane & 3;   // lane within the quad
+  const uint32_t win_base = smem_u32(smem);
+  uint32_t c_base = 0;  // window counter at the start of the item
+  bool ok = true;
+  while (items.next(tab, s, start, cnt)) {
+    const int rank = tab.rk[s];
+    if (rank <= 0) continue;
+    const float scale = tab.sc[s];
+    const int tiles = (cnt + 15) >> 4;
+    const int CS = max(1, kMmaWarps / tiles);
+    const bool active = warp < tiles * CS;
+    const int tile = active ? warp / CS : 0;
+    const int cs = active ? warp - tile * CS : 0;
+    const int r0 = tile * 16 + g;
+    const bool v0 = active && r0 < cnt, v1 = active && r0 + 8 < cnt;
+    const int64_t tok0 = v0 ? (int64_t)__ldg(args.seg.token_index + start + r0) : 0;
+    const int64_t tok1 = v1 ? (int64_t)__ldg(args.seg.token_index + start + r0 + 8) : 0;
+    uint8_t* y0 = args.y + tok0 * N * 2;
+    uint8_t* y1 = args.y + tok1 * N * 2;
+
+    // A fragments: tmp rows of this tile, columns >= min(rank, R) read as zero
+    uint32_t fa[RP / 16][4];
+    {
+      const int kr = min(rank, args.R);
+      const uint8_t* t0 = args.tmp + tok0 * args.R * 2;
+      const uint8_t* t1 = args.tmp + tok1 * args.R * 2;
+      auto ld2 = [&](const uint8_t* row, bool v, int k) -> uint32_t {
+        if (!v || k >= kr) return 0u;
+        const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(row + k * 2));
+        return k + 1 < kr ? w : (w & 0xFFFFu);
+      };
+#pragma unroll
+      for (int st = 0; st < RP / 16; ++st) {
+        fa[st][0] = ld2(t0, v0, 16 * st + 2 * t);
+        fa[st][1] = ld2(t1, v1, 16 * st + 2 * t);
+        fa[st][2] = ld2(t0, v0, 16 * st + 8 + 2 * t);
+        fa[st][3] = ld2(t1, v1, 16 * st + 8 + 2 * t);
+      }
+    }
+
+    struct Cur {
+      int w, blk, end;
+    };
+    auto range = [&](Cur& c) {
+      const int nb = min(W, N - c.w * W) >> 5;
+      c.blk = active ? cs * nb / CS : 0;
+      c.end = active ? (cs + 1) * nb / CS : 0;
+    };
+    auto first = [&](Cur& c) {
+      c.w = 0;
+      range(c);
+      while (c.blk >= c.end && ++c.w < nwin) range(c);
+    };
+    auto step = [&](Cur& c) {
+      if (++c.blk >= c.end)
+        while (++c.w < nwin) {
+          range(c);
+          if (c.blk < c.end) break;
+        }
+    };
+    Cur lc, mc;  // load cursor, compute cursor (same sequence)
+    first(lc);
+    first(mc);
+
+    struct Batch {
+      uint4 y0[U], y1[U];
+    };
+    auto load_batch = [&](Batch& B) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (lc.w < nwin) {
+          const int col = lc.w * W + lc.blk * 32 + 8 * t;
+          B.y0[u] = v0 ? ld_stream16(y0 + col * 2) : make_uint4(0u, 0u, 0u, 0u);
+          B.y1[u] = v1 ? ld_stream16(y1 + col * 2) : make_uint4(0u, 0u, 0u, 0u);
+          step(lc);
+        }
+      }
+    };
+
+    int cw = -1;  // window of this item the warp currently holds
+    auto release = [&]() {
+      const uint32_t b = (c_base + cw) & 1;
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();
+        if (atomicAdd(&released[b], 1u) % kMmaWarps == kMmaWarps - 1 && ic.valid) {
+          fence_proxy_async_smem();
+          issue(ic, b);
+        }
+      }
+      ic.advance(tab);
+    };
+    auto hold = [&](int to) {
+      while (cw < to) {
+        if (cw >= 0) release();
+        ++cw;
+        const uint32_t c = c_base + cw;
+        if (ok) ok = mbar_wait_warp(&full[c & 1], (c >> 1) & 1, abort_flag);
+      }
+    };
+    // y + delta for the 8 columns of a lane: words hold bf16/fp16 pairs
+    auto add_store = [&](uint8_t* row, bool v, int col, const uint4& yv, const uint32_t (&d)[4]) {
+      const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float lo = E::to_f((uint16_t)(yw[i] & 0xFFFFu)) + E::to_f((uint16_t)(d[i] & 0xFFFFu));
+        const float hi = E::to_f((uint16_t)(yw[i] >> 16)) + E::to_f((uint16_t)(d[i] >> 16));
+        o[i] = (uint32_t)E::from_f(lo) | ((uint32_t)E::from_f(hi) << 16);
+      }
+      if (v) *reinterpret_cast<uint4*>(row + col * 2) = make_uint4(o[0], o[1], o[2], o[3]);
+    };
+    auto compute_batch = [&](Batch& B) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (mc.w >= nwin) break;
+        hold(mc.w);
+        const uint32_t wb = win_base + ((c_base + mc.w) & 1) * kWinBytes;
+        const int cwin = mc.blk * 32;  // block column inside the window
+        float acc[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        const int m = lane >> 3;  // ldmatrix matrix of this lane: tile jb + (m >> 1), k half m & 1
+#pragma unroll
+        for (int st = 0; st < RP / 16; ++st) {
+#pragma unroll
+          for (int jb = 0; jb < 4; jb += 2) {
+            const int c0 = cwin + 8 * (jb + (m >> 1));
+            const int k = 16 * st + 8 * (m & 1) + (lane & 7);
+            const uint32_t addr = wb + (c0 >> 6) * Cfg::kChunkBytes + k * 128 +
+                                  16 * (((c0 >> 3) & 7) ^ (k & 7));
+            uint32_t bf[4];
+            ldsm_x4_trans(addr, bf);
+            if (ok) {
+              mma_16816<BF16>(acc[jb], fa[st], bf[0], bf[1]);
+              mma_16816<BF16>(acc[jb + 1], fa[st], bf[2], bf[3]);
+            }
+          }
+        }
+        // delta words (tile j, row g / g + 8), regrouped to the lane's 8 columns
+        uint32_t d0[4], d1[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          d0[j] = (uint32_t)E::from_f(scale * acc[j][0]) | ((uint32_t)E::from_f(scale * acc[j][1]) << 16);
+          d1[j] = (uint32_t)E::from_f(scale * acc[j][2]) | ((uint32_t)E::from_f(scale * acc[j][3]) << 16);
+        }
+        quad_transpose(d0, t);
+        quad_transpose(d1, t);
+        const int col = mc.w * W + cwin + 8 * t;
+        add_store(y0, v0 && ok, col, B.y0[u], d0);
+        add_store(y1, v1 && ok, col, B.y1[u], d1);
+        step(mc);
+      }
+    };
+
+    Batch A, B;
+    load_batch(A);
+    for (;;) {
+      const bool more_b = lc.w < nwin;
+      if (more_b) load_batch(B);
+      compute_batch(A);
+      if (!more_b) break;
+      const bool more_a = lc.w < nwin;
+      if (more_a) load_batch(A);
+      compute_batch(B);
+      if (!more_a) break;
+    }
+    hold(nwin - 1);  // windows without blocks of this warp are passed through
+    release();
+    c_base += nwin;
   }
 }
 
