@@ -190,7 +190,8 @@ def run_ours(args):
     import torch.distributed as dist
 
     from polylora_b200 import _native
-    from polylora_b200.sgmv import build_segments, sgmv_expand, sgmv_lora_a_fwd, sgmv_lora_b_fwd, sgmv_shrink
+    from polylora_b200.sgmv import (build_segments, sgmv_expand, sgmv_lora_a_fwd, sgmv_lora_b_fwd, sgmv_shrink,
+                                    sgmv_shrink_expand)
 
     world, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -209,10 +210,12 @@ def run_ours(args):
     y = torch.randn(T_TOKENS, 1, N_OUT, device=dev, generator=g).to(torch.bfloat16)
     stream = torch.cuda.Stream(device=dev)
 
+    tmp_buf = torch.empty(T_TOKENS, 1, MAX_RANK, device=dev, dtype=torch.bfloat16)
+
     def step(tmp_out=None):
         table = build_segments(wi, seq, ranks, 1)
-        tmp = sgmv_shrink(x, A, table, ranks, out=tmp_out)
-        sgmv_expand(tmp, Bw, y, table, ranks, scales)
+        tmp = tmp_buf if tmp_out is None else tmp_out
+        sgmv_shrink_expand(x, A, Bw, y, table, ranks, scales, tmp=tmp)
         return table, tmp
 
     def barrier():
@@ -260,16 +263,33 @@ def run_ours(args):
     elapsed_ms = max_over_ranks(ev0.elapsed_time(ev1))
     ms_per_step = elapsed_ms / args.steps
 
-    # ---- per-kernel durations (same stream, CUDA events around graph replays of one kernel)
-    def time_kernel(fn, reps):
+    # ---- per-kernel durations with L2 flushed before every launch: CUDA events on
+    # `stream` around replays of a graph [flush, kernel] minus replays of [flush],
+    # the flush writing 256 MiB then reading another 256 MiB (L2 is 126 MB)
+    flush_w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_r = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    flush_sink = torch.empty((), dtype=torch.float32, device=dev)
+
+    def flush():
+        flush_w.fill_(7)
+        torch.sum(flush_r, dim=0, out=flush_sink)
+
+    def graph_of(fns):
         with torch.cuda.stream(stream):
-            fn()
+            for f in fns:
+                f()
             torch.cuda.synchronize()
             gk = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gk, stream=stream):
-                fn()
+                for f in fns:
+                    f()
             gk.replay()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        return gk
+
+    def replay_ms(gk, reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
             a.record(stream)
             for _ in range(reps):
                 gk.replay()
@@ -277,10 +297,18 @@ def run_ours(args):
         b.synchronize()
         return a.elapsed_time(b) / reps
 
-    reps = max(args.steps, 10)
+    def time_kernel(fn, reps):
+        g_flush = graph_of([flush])
+        g_both = graph_of([flush, fn])
+        samples = sorted(replay_ms(g_both, reps) - replay_ms(g_flush, reps) for _ in range(3))
+        return samples[1]
+
+    reps = max(args.steps // 2, 10)
     shrink_ms = time_kernel(lambda: sgmv_shrink(x, A, table, ranks, out=tmp), reps)
     expand_ms = time_kernel(lambda: sgmv_expand(tmp, Bw, y, table, ranks, scales), reps)
+    pair_ms = time_kernel(lambda: sgmv_shrink_expand(x, A, Bw, y, table, ranks, scales, tmp=tmp), reps)
     seg_ms = time_kernel(lambda: build_segments(wi, seq, ranks, 1), reps)
+    del flush_w, flush_r
     clocks = sampler.stop()
 
     # ---- end to end through the public drop-in operators with host buffers
@@ -350,13 +378,15 @@ def run_ours(args):
         "config": {
             "workload": "BASELINE config 2 SGMV op: T=16384 token rows per GPU, K=N=4096, 64 slots + __base__, "
                         "max_rank 16, ranks U{0,4,8,16}, 20% base rows",
-            "step": "device segment table + sgmv shrink + sgmv expand (fused scale/add-back), CUDA graph",
-            "l2": "inputs larger than L2 (x 128 MiB + y 128 MiB per GPU)",
+            "step": "device segment table + sgmv shrink + sgmv expand (fused scale/add-back) issued as one "
+                    "call, the expand overlapping the shrink's end; CUDA graph",
+            "l2": "step: inputs larger than L2 (x 128 MiB + y 128 MiB per GPU); per-kernel times: L2 flushed "
+                  "(256 MiB write + 256 MiB read) before every launch, outside the timed difference",
             "parallelism": f"row data-parallel x{world}, independent slot caches, no collective in the step",
             "active_tokens_per_gpu": t_act,
         },
         "roofline": {
-            "kernel": "sgmv_expand_tc_kernel<16,bf16>",
+            "kernel": "sgmv_expand_mma_kernel<16,bf16>",
             "bound": "hbm",
             "achieved": achieved_expand,
             "peak": peak,
@@ -371,6 +401,8 @@ def run_ours(args):
             "shrink": {"avg_launch_ms": shrink_ms, "bytes": b_shrink, "gbs": achieved_shrink, "frac": achieved_shrink / peak},
             "expand": {"avg_launch_ms": expand_ms, "bytes": b_expand, "gbs": achieved_expand, "frac": achieved_expand / peak},
             "segments": {"avg_ms": seg_ms, "launches": 3},
+            "shrink_expand_call": {"avg_ms": pair_ms, "bytes": b_shrink + b_expand,
+                                   "gbs": (b_shrink + b_expand) / (pair_ms * 1e-3) / 1e9},
             "step_combined_gbs": b_comb / (ms_per_step * 1e-3) / 1e9,
         },
         "cpu_baseline": cb,

@@ -156,6 +156,21 @@ int plora_sgmv_expand(const void* tmp, const void* lora_b, void* y, const int32_
                       int64_t num_tokens, int64_t max_rank, int64_t out_features,
                       int32_t num_slots, int32_t dtype, void* stream);
 
+/* Shrink then expand of one wrapped Linear over a prebuilt segment table:
+ * tmp = x A[slot] (stack_num 1), then y += scale tmp B[slot] in place.  The
+ * same math as plora_sgmv_shrink followed by plora_sgmv_expand, and the
+ * call a layer of the reference makes twice (layers.py:42-58, the
+ * _SGMV_LORA_A_FWD / _SGMV_LORA_B_FWD pair).  Issued together, the expand is
+ * launched to overlap the end of the shrink: it stages its tables, its LoRA-B
+ * windows and its first rows of y while the shrink finishes, and reads tmp
+ * only once the shrink has completed. */
+int plora_sgmv_shrink_expand(const void* x, const void* lora_a, void* tmp, const void* lora_b,
+                             void* y, const int32_t* lora_ranks, const float* scalings,
+                             const int32_t* slot_start, const int32_t* token_index,
+                             int64_t num_tokens, int64_t in_features, int64_t max_rank,
+                             int64_t out_features, int32_t num_slots, int32_t dtype,
+                             void* stream);
+
 /* ---------------------------------------------------------------------------
  * GPU slot refill: src/polylora/cache.py:97-150 (_allocate_or_evict zeroing +
  * _load_adapter_into_slot copies).  One pinned host->device copy of a packed

@@ -117,6 +117,13 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
             _i64, _i64, _i64, _i32, _i32, _c_void_p,
         ],
     ),
+    "plora_sgmv_shrink_expand": (
+        ctypes.c_int,
+        [
+            _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+            _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i32, _i32, _c_void_p,
+        ],
+    ),
     "plora_sgmv_a_fwd_noalloc": (
         ctypes.c_int,
         [

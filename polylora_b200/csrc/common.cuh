@@ -159,6 +159,16 @@ __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialisation may start before its predecessor in the stream has finished;
+// griddep_wait() returns once that predecessor grid has completed and its
+// memory is visible (at once for an ordinary launch).  griddep_launch()
+// lets the next such kernel start as SMs free up.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Starts fetching the cache line holding `p` into L2 (no register result, so a
 // thread can keep many lines in flight beyond its register-staged loads).
 __device__ __forceinline__ void prefetch_l2(const void* p) {

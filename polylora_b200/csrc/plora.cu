@@ -254,6 +254,25 @@ int build_segments(const int64_t* wi, const int32_t* seq_lens, const int32_t* ra
 // Tensor-core path eligibility (16-bit types, rank tile 16/32/64, 16-byte rows).
 bool tc_rank_ok(int64_t R) { return R == 16 || R == 32 || R == 64; }
 
+// Launches `kernel` with programmatic stream serialisation when `pdl` is set:
+// the kernel may then start while its predecessor in the stream finishes and
+// must call griddep_wait() before reading anything that predecessor writes.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, SegTable seg,
                 int64_t num_tokens, int64_t K, int64_t R, int32_t stack_num, int32_t dtype,
                 cudaStream_t stream) {
@@ -286,13 +305,11 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
     const dim3 grid(di->sm_count), block(kMmaThreads);
     const size_t tb = tab_bytes(seg.num_slots);
     const bool bf = dtype == PLORA_DTYPE_BF16;
-#define LAUNCH_SHRINK(RPV)                                                                     \
-  if (bf)                                                                                      \
-    sgmv_shrink_mma_kernel<RPV, true><<<grid, block, ShrinkMmaCfg<RPV>::kSmemBytes + tb, stream>>>( \
-        map8, map1, args);                                                                     \
-  else                                                                                         \
-    sgmv_shrink_mma_kernel<RPV, false><<<grid, block, ShrinkMmaCfg<RPV>::kSmemBytes + tb, stream>>>( \
-        map8, map1, args);
+    // the kernel reads its inputs only after griddep_wait(): always launched programmatically
+#define LAUNCH_SHRINK(RPV)                                                                         \
+  PLORA_CUDA(launch_kernel(bf ? sgmv_shrink_mma_kernel<RPV, true> : sgmv_shrink_mma_kernel<RPV, false>, \
+                           grid, block, ShrinkMmaCfg<RPV>::kSmemBytes + tb, stream, true, map8, map1, args), \
+             "launch sgmv_shrink_mma_kernel");
     if (R == 16) {
       LAUNCH_SHRINK(16)
     } else if (R == 32) {
@@ -315,7 +332,8 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
 }
 
 int expand_impl(const void* tmp, const void* b, void* y, const int32_t* ranks, const float* scales,
-                SegTable seg, int64_t R, int64_t N, int32_t dtype, cudaStream_t stream) {
+                SegTable seg, int64_t R, int64_t N, int32_t dtype, cudaStream_t stream,
+                bool after_shrink = false) {
   DeviceInfo* di = nullptr;
   int st = device_info(&di);
   if (st) return st;
@@ -344,13 +362,13 @@ int expand_impl(const void* tmp, const void* b, void* y, const int32_t* ranks, c
     const dim3 grid(di->sm_count), block(kMmaThreads);
     const size_t tb = tab_bytes(seg.num_slots);
     const bool bf = dtype == PLORA_DTYPE_BF16;
-#define LAUNCH_EXPAND(RPV)                                                                     \
-  if (bf)                                                                                      \
-    sgmv_expand_mma_kernel<RPV, true><<<grid, block, ExpandMmaCfg<RPV>::kSmemBytes + tb, stream>>>( \
-        mapn, map1, args);                                                                     \
-  else                                                                                         \
-    sgmv_expand_mma_kernel<RPV, false><<<grid, block, ExpandMmaCfg<RPV>::kSmemBytes + tb, stream>>>( \
-        mapn, map1, args);
+    // programmatic only right after this library's shrink (after_shrink): the kernel reads
+    // the segment table, LoRA-B and y before griddep_wait(), tmp after it
+#define LAUNCH_EXPAND(RPV)                                                                         \
+  PLORA_CUDA(launch_kernel(bf ? sgmv_expand_mma_kernel<RPV, true> : sgmv_expand_mma_kernel<RPV, false>, \
+                           grid, block, ExpandMmaCfg<RPV>::kSmemBytes + tb, stream, after_shrink, mapn, \
+                           map1, args),                                                            \
+             "launch sgmv_expand_mma_kernel");
     if (R == 16) {
       LAUNCH_EXPAND(16)
     } else if (R == 32) {
@@ -485,6 +503,32 @@ int plora_sgmv_expand(const void* tmp, const void* lora_b, void* y, const int32_
   SegTable seg{slot_start, token_index, num_slots};
   return expand_impl(tmp, lora_b, y, lora_ranks, scalings, seg, max_rank, out_features, dtype,
                      static_cast<cudaStream_t>(stream));
+}
+
+int plora_sgmv_shrink_expand(const void* x, const void* lora_a, void* tmp, const void* lora_b,
+                             void* y, const int32_t* lora_ranks, const float* scalings,
+                             const int32_t* slot_start, const int32_t* token_index,
+                             int64_t num_tokens, int64_t in_features, int64_t max_rank,
+                             int64_t out_features, int32_t num_slots, int32_t dtype,
+                             void* stream) {
+  g_last_error.clear();
+  int st = check_common(dtype, num_slots, max_rank);
+  if (st) return st;
+  if (in_features < 1 || in_features > INT32_MAX || out_features < 1 || out_features > INT32_MAX)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "in_features/out_features");
+  if (num_tokens == 0) return PLORA_OK;
+  if (!x || !lora_a || !tmp || !lora_b || !y || !lora_ranks || !scalings || !slot_start ||
+      !token_index)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "null pointer");
+  if (num_tokens > (int64_t)INT32_MAX)
+    return fail(PLORA_ERR_UNSUPPORTED, "num_tokens exceeds int32 token ids");
+  SegTable seg{slot_start, token_index, num_slots};
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((st = shrink_impl(x, lora_a, tmp, lora_ranks, seg, num_tokens, in_features, max_rank, 1,
+                        dtype, s)))
+    return st;
+  return expand_impl(tmp, lora_b, y, lora_ranks, scalings, seg, max_rank, out_features, dtype, s,
+                     /*after_shrink=*/true);
 }
 
 int plora_sgmv_a_fwd(const void* x, const void* lora_a, void* tmp, const int32_t* seq_lens,

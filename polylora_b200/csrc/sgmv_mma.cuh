@@ -164,6 +164,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  griddep_wait();    // inputs (segment table, x) come from earlier kernels
+  griddep_launch();  // the expand may start on SMs this grid releases
   const int64_t total = __ldg(args.seg.slot_start + args.seg.num_slots);
   const int64_t begin = total * blockIdx.x / gridDim.x;
   const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
@@ -492,25 +494,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     uint8_t* y0 = args.y + tok0 * N * 2;
     uint8_t* y1 = args.y + tok1 * N * 2;
 
-    // A fragments: tmp rows of this tile, columns >= min(rank, R) read as zero
-    uint32_t fa[RP / 16][4];
-    {
-      const int kr = min(rank, args.R);
-      const uint8_t* t0 = args.tmp + tok0 * args.R * 2;
-      const uint8_t* t1 = args.tmp + tok1 * args.R * 2;
-      auto ld2 = [&](const uint8_t* row, bool v, int k) -> uint32_t {
-        if (!v || k >= kr) return 0u;
-        const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(row + k * 2));
-        return k + 1 < kr ? w : (w & 0xFFFFu);
-      };
-#pragma unroll
-      for (int st = 0; st < RP / 16; ++st) {
-        fa[st][0] = ld2(t0, v0, 16 * st + 2 * t);
-        fa[st][1] = ld2(t1, v1, 16 * st + 2 * t);
-        fa[st][2] = ld2(t0, v0, 16 * st + 8 + 2 * t);
-        fa[st][3] = ld2(t1, v1, 16 * st + 8 + 2 * t);
-      }
-    }
+    uint32_t fa[RP / 16][4];  // A fragments (tmp rows), filled once the first y batch is in flight
 
     struct Cur {
       int w, blk, end;
@@ -629,6 +613,27 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
 
     Batch A, B;
     load_batch(A);
+    // tmp is the previous kernel's output: everything above (slot table, LoRA-B
+    // windows, the first y batch) may overlap its tail under programmatic launch
+    griddep_wait();
+    // A fragments: tmp rows of this tile, columns >= min(rank, R) read as zero
+    {
+      const int kr = min(rank, args.R);
+      const uint8_t* t0 = args.tmp + tok0 * args.R * 2;
+      const uint8_t* t1 = args.tmp + tok1 * args.R * 2;
+      auto ld2 = [&](const uint8_t* row, bool v, int k) -> uint32_t {
+        if (!v || k >= kr) return 0u;
+        const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(row + k * 2));
+        return k + 1 < kr ? w : (w & 0xFFFFu);
+      };
+#pragma unroll
+      for (int st = 0; st < RP / 16; ++st) {
+        fa[st][0] = ld2(t0, v0, 16 * st + 2 * t);
+        fa[st][1] = ld2(t1, v1, 16 * st + 2 * t);
+        fa[st][2] = ld2(t0, v0, 16 * st + 8 + 2 * t);
+        fa[st][3] = ld2(t1, v1, 16 * st + 8 + 2 * t);
+      }
+    }
     for (;;) {
       const bool more_b = lc.w < nwin;
       if (more_b) load_batch(B);

@@ -14,7 +14,7 @@ from torch import nn
 
 from .cache import GpuAdapterCache
 from .context import LoraBatchContext, get_lora_context
-from .sgmv import SegmentTable, build_segments, sgmv_expand, sgmv_shrink
+from .sgmv import SegmentTable, build_segments, sgmv_shrink_expand
 
 
 class MultiLoraLinear(nn.Module):
@@ -44,8 +44,10 @@ class MultiLoraLinear(nn.Module):
         self.cache.wait_ready()
         name = self.module_name
         ranks = self.cache.ranks[name]
-        tmp = sgmv_shrink(x_3d, self.cache.A[name], table, ranks)
-        out = sgmv_expand(tmp, self.cache.B[name], base_3d, table, ranks, self.cache.scales[name])
+        # layers.py:42-58 of the reference: shrink then expand, issued as one call
+        out = sgmv_shrink_expand(
+            x_3d, self.cache.A[name], self.cache.B[name], base_3d, table, ranks, self.cache.scales[name]
+        )
         return out.reshape(original_shape)
 
     def _check_native(self, x: torch.Tensor) -> None:

@@ -173,6 +173,52 @@ def sgmv_expand(
     return y
 
 
+def sgmv_shrink_expand(
+    x: torch.Tensor,
+    weights_a: torch.Tensor,
+    weights_b: torch.Tensor,
+    y: torch.Tensor,
+    table: SegmentTable,
+    lora_ranks: torch.Tensor,
+    scalings: torch.Tensor,
+    tmp: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """y += scale · (x · A[slot]) · B[slot] in place: :func:`sgmv_shrink` then
+    :func:`sgmv_expand` in one call, the expand overlapping the shrink's end.
+
+    x (B, M, K), weights_a (NS, K, R), weights_b (NS, R, N), y (B, M, N)."""
+    dev = _require_cuda(x, weights_a, weights_b, y, lora_ranks, scalings)
+    B, M, K = x.shape
+    ns, kw, R = weights_a.shape
+    nsb, rw, N = weights_b.shape
+    if kw != K or rw != R or nsb != ns:
+        raise ValueError(f"weight shapes {tuple(weights_a.shape)} / {tuple(weights_b.shape)} do not match x")
+    if (B, M) != (table.num_rows, table.max_seq) or ns != table.num_slots:
+        raise ValueError("segment table does not match the input shape")
+    if tuple(y.shape) != (B, M, N):
+        raise ValueError(f"base_output shape {tuple(y.shape)} != {(B, M, N)}")
+    if not y.is_contiguous():
+        raise ValueError("base_output must be contiguous (it is updated in place)")
+    if tmp is None:
+        tmp = torch.empty((B, M, R), device=dev, dtype=x.dtype)
+    if B == 0 or M == 0:
+        return y
+    xc = x.contiguous()
+    wa = weights_a.contiguous()
+    wb = weights_b.contiguous()
+    if not (xc.dtype == wa.dtype == wb.dtype == y.dtype == tmp.dtype):
+        raise TypeError("x, weights, tmp and base_output must share one dtype")
+    rk = _as(lora_ranks, torch.int32)
+    sc = _as(scalings, torch.float32)
+    _native.call(
+        "plora_sgmv_shrink_expand",
+        xc.data_ptr(), wa.data_ptr(), tmp.data_ptr(), wb.data_ptr(), y.data_ptr(),
+        rk.data_ptr(), sc.data_ptr(), table.slot_start.data_ptr(), table.token_index.data_ptr(),
+        table.num_tokens, K, R, N, ns, dtype_code(xc.dtype), _stream(dev),
+    )
+    return y
+
+
 def sgmv_lora_a_fwd(
     x: torch.Tensor,
     weights: torch.Tensor,

@@ -62,6 +62,13 @@ def test_workspace_size_and_null_checks(native):
     # missing workspace
     st = lib.plora_sgmv_a_fwd(None, None, None, None, None, None, 4, 2, 64, 16, 5, 1, 2, None, 0, None)
     assert st == native.ERR_WORKSPACE
+    # the combined shrink + expand checks its arguments before any CUDA call
+    st = lib.plora_sgmv_shrink_expand(None, None, None, None, None, None, None, None, None,
+                                      8, 64, 16, 64, 5, 2, None)
+    assert st == native.ERR_INVALID_ARGUMENT and "null" in native.last_error()
+    st = lib.plora_sgmv_shrink_expand(None, None, None, None, None, None, None, None, None,
+                                      8, 0, 16, 64, 5, 2, None)
+    assert st == native.ERR_INVALID_ARGUMENT
 
 
 def test_product_path_has_no_cpu_fallback():

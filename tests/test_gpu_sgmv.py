@@ -12,7 +12,7 @@ import torch
 
 from oracle import sgmv_ref
 from polylora_b200.sgmv import (build_segments, sgmv_expand, sgmv_lora_a_fwd, sgmv_lora_b_fwd,
-                                sgmv_shrink)
+                                sgmv_shrink, sgmv_shrink_expand)
 
 pytestmark = pytest.mark.gpu
 
@@ -182,6 +182,28 @@ def test_segment_table_reuse_across_modules(cuda_status_clean):
     assert sgmv_ref.lora_err(got, ref, c["y"], "bfloat16") <= 2e-2
     inact = inactive_mask(cm)
     assert np.array_equal(got[inact], c["y"][inact])
+
+
+@pytest.mark.parametrize("R,rc,dt", [(16, [0, 4, 8, 16], "bfloat16"), (64, [8, 64], "float16"), (32, [8, 32], "bfloat16")])
+def test_combined_entry_matches_separate_calls(R, rc, dt, cuda_status_clean):
+    """plora_sgmv_shrink_expand (expand launched to overlap the shrink's end)
+    gives bit-identical tmp and y to plora_sgmv_shrink + plora_sgmv_expand,
+    repeated back to back on one stream."""
+    c = make_case(50 + R, 600, 1, 1024, 2048, 17, R, rc, dt, base_frac=0.2)
+    d = to_dev(c)
+    table = build_segments(d["wi"], d["seq"], d["ranks"], 1)
+    # rows of inactive tokens are never written: both tmp buffers start at zero
+    tmp_sep = torch.zeros(d["x"].shape[:2] + (R,), device="cuda", dtype=d["x"].dtype)
+    tmp_comb = torch.zeros_like(tmp_sep)
+    y_sep = d["y"].clone()
+    y_comb = d["y"].clone()
+    for _ in range(3):  # back to back: each call must see the previous one's y
+        sgmv_shrink_expand(d["x"], d["A"], d["B"], y_comb, table, d["ranks"], d["scales"], tmp=tmp_comb)
+        sgmv_shrink(d["x"], d["A"], table, d["ranks"], out=tmp_sep)
+        sgmv_expand(tmp_sep, d["B"], y_sep, table, d["ranks"], d["scales"])
+    torch.cuda.synchronize()
+    assert torch.equal(tmp_comb, tmp_sep)
+    assert torch.equal(y_comb, y_sep)
 
 
 def test_full_size_cfg2_sampled_parity_and_determinism(cuda_status_clean):
