@@ -83,6 +83,43 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
                : "r"(addr));
 }
 
+// Round-to-nearest add of two packed pairs of bf16 (BF16) or fp16 values.
+template <bool BF16>
+__device__ __forceinline__ uint32_t add2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (BF16)
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Packs two floats (lo, hi) into a pair of bf16 (BF16) or fp16, round to nearest.
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  uint32_t r;
+  if constexpr (BF16)
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  else
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Four 8x8 matrices of 16-bit pairs from mma fragment layout to shared memory
+// (lane l gives the address of row l & 7 of matrix l >> 3).
+__device__ __forceinline__ void stsm_x4(uint32_t addr, const uint32_t (&r)[4]) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+
+__device__ __forceinline__ void lds_v4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
 // d += a (16x16, row) * b (16x8, col); fp32 accumulate.
 template <bool BF16>
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
@@ -408,8 +445,10 @@ struct ExpandMmaCfg {
   static constexpr int kBoxChunks = kWinCols / 64 < 16 ? kWinCols / 64 : 16;
   static constexpr int kU = RP == 64 ? 2 : 3;            // 32-column blocks per load batch
   static constexpr int kBarrierBytes = 64;
+  static constexpr int kRegroupPitch = 80;  // 64-byte delta rows padded: conflict-free 16-byte access
+  static constexpr int kRegroupBytes = kMmaWarps * 16 * kRegroupPitch;
   // + slot table (3 * num_slots + 1 ints), sized at launch
-  static constexpr int kSmemBytes = 1024 + 2 * kWinBytes + kBarrierBytes;
+  static constexpr int kSmemBytes = 1024 + 2 * kWinBytes + kBarrierBytes + kRegroupBytes;
 };
 
 template <int RP, bool BF16>
@@ -425,7 +464,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kWinBytes);
   uint32_t* released = reinterpret_cast<uint32_t*>(full + 2);  // per buffer, monotonic
   volatile int* abort_flag = reinterpret_cast<volatile int*>(released + 2);
-  int32_t* tab_mem = reinterpret_cast<int32_t*>(smem + 2 * kWinBytes + Cfg::kBarrierBytes);
+  uint8_t* regroup = smem + 2 * kWinBytes + Cfg::kBarrierBytes;  // per-warp 16 x 64 B delta tile
+  int32_t* tab_mem = reinterpret_cast<int32_t*>(regroup + Cfg::kRegroupBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -557,17 +597,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       }
     };
     // y + delta for the 8 columns of a lane: words hold bf16/fp16 pairs
+    // (a correctly rounded pair add equals the fp32 add rounded once: the fp32
+    // sum of two 16-bit floats is exact unless one addend is below half an ulp)
     auto add_store = [&](uint8_t* row, bool v, int col, const uint4& yv, const uint32_t (&d)[4]) {
-      const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
-      uint32_t o[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float lo = E::to_f((uint16_t)(yw[i] & 0xFFFFu)) + E::to_f((uint16_t)(d[i] & 0xFFFFu));
-        const float hi = E::to_f((uint16_t)(yw[i] >> 16)) + E::to_f((uint16_t)(d[i] >> 16));
-        o[i] = (uint32_t)E::from_f(lo) | ((uint32_t)E::from_f(hi) << 16);
-      }
-      if (v) *reinterpret_cast<uint4*>(row + col * 2) = make_uint4(o[0], o[1], o[2], o[3]);
+      const uint4 o = make_uint4(add2<BF16>(yv.x, d[0]), add2<BF16>(yv.y, d[1]), add2<BF16>(yv.z, d[2]),
+                                 add2<BF16>(yv.w, d[3]));
+      if (v) *reinterpret_cast<uint4*>(row + col * 2) = o;
     };
+    // stmatrix: lane l writes row l & 7 of matrix (tile) l >> 3; ld: row g, columns 8t ..
+    const uint32_t rg_base = smem_u32(regroup + warp * 16 * Cfg::kRegroupPitch);
+    const uint32_t rg_st = rg_base + (lane & 7) * Cfg::kRegroupPitch + (lane >> 3) * 16;
+    const uint32_t rg_ld = rg_base + g * Cfg::kRegroupPitch + t * 16;
     auto compute_batch = [&](Batch& B) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
@@ -599,11 +639,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         uint32_t d0[4], d1[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          d0[j] = (uint32_t)E::from_f(scale * acc[j][0]) | ((uint32_t)E::from_f(scale * acc[j][1]) << 16);
-          d1[j] = (uint32_t)E::from_f(scale * acc[j][2]) | ((uint32_t)E::from_f(scale * acc[j][3]) << 16);
+          d0[j] = pack2<BF16>(scale * acc[j][0], scale * acc[j][1]);
+          d1[j] = pack2<BF16>(scale * acc[j][2], scale * acc[j][3]);
         }
-        quad_transpose(d0, t);
-        quad_transpose(d1, t);
+        // the D fragments are 8x8 tiles (rows g / g + 8, columns 8 j ..): stored
+        // as matrices and read back as the lane's 16-byte row piece
+        stsm_x4(rg_st, d0);
+        stsm_x4(rg_st + 8 * Cfg::kRegroupPitch, d1);
+        __syncwarp();
+        lds_v4(rg_ld, d0);
+        lds_v4(rg_ld + 8 * Cfg::kRegroupPitch, d1);
+        __syncwarp();
         const int col = mc.w * W + cwin + 8 * t;
         add_store(y0, v0 && ok, col, B.y0[u], d0);
         add_store(y1, v1 && ok, col, B.y1[u], d1);
