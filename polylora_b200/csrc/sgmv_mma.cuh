@@ -150,6 +150,18 @@ __device__ __forceinline__ uint32_t win_offset(int k, int j) {
   return off + 16u * ((uint32_t)j ^ ((off >> 7) & (RP / 8 - 1)));
 }
 
+// Issues one LoRA-A window: nb 32-row blocks from block blk0 of the 5-D view,
+// 8-block boxes then single blocks (one thread; out of line: the shrink has
+// one release site per unrolled block).
+__device__ __noinline__ void issue_lora_a_window(const CUtensorMap* map8, const CUtensorMap* map1,
+                                                 uint64_t* bar, uint32_t dst, int nb, int blk0,
+                                                 int block_bytes) {
+  mbar_arrive_expect_tx(bar, nb * block_bytes);
+  int q = 0;
+  for (; q + 8 <= nb; q += 8) tma_load_5d_outer(dst + q * block_bytes, map8, bar, blk0 + q);
+  for (; q < nb; ++q) tma_load_5d_outer(dst + q * block_bytes, map1, bar, blk0 + q);
+}
+
 // Sequence of (slot, window) pairs over the CTA's items with rank > 0, in the
 // order every warp consumes them.
 struct WinCursor {
@@ -164,7 +176,10 @@ struct WinCursor {
     valid = true;
     advance(tab);
   }
-  __device__ void advance(const SlotTab& tab) {
+  // out-of-line copy for kernels whose many release sites would otherwise each
+  // carry one (measured faster in the shrink, slower in the expand)
+  __device__ __noinline__ void advance_outlined(const SlotTab& tab) { advance(tab); }
+  __device__ __forceinline__ void advance(const SlotTab& tab) {
     if (slot >= 0 && ++w < nwin) return;
     w = 0;
     int s, cnt;
@@ -213,13 +228,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   const int nwin = (K + W - 1) / W;
   const int kblocks = K >> 5;  // 32-row blocks per slot
   auto issue = [&](const WinCursor& wc, int b) {  // one thread
-    const int nb = min(W, K - wc.w * W) >> 5;
-    mbar_arrive_expect_tx(&full[b], nb * 32 * RP * 2);
-    const int blk0 = wc.slot * kblocks + wc.w * (W >> 5);
-    const uint32_t dst = smem_u32(smem + b * kWinBytes);
-    int q = 0;
-    for (; q + 8 <= nb; q += 8) tma_load_5d_outer(dst + q * 32 * RP * 2, &tmap_a8, &full[b], blk0 + q);
-    for (; q < nb; ++q) tma_load_5d_outer(dst + q * 32 * RP * 2, &tmap_a1, &full[b], blk0 + q);
+    issue_lora_a_window(&tmap_a8, &tmap_a1, &full[b], smem_u32(smem + b * kWinBytes),
+                        min(W, K - wc.w * W) >> 5, wc.slot * kblocks + wc.w * (W >> 5), 32 * RP * 2);
   };
   __syncthreads();  // slot table staged
   WinCursor ic;     // the window this warp would issue after its next release
@@ -233,7 +243,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     prefetch_tmap(&tmap_a1);
     for (int b = 0; b < 2 && ic.valid; ++b) {
       issue(ic, b);
-      ic.advance(tab);
+      ic.advance_outlined(tab);
     }
   } else {
     ic.advance(tab);
