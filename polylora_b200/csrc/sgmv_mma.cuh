@@ -455,7 +455,9 @@ struct ExpandMmaCfg {
   static constexpr int kBoxChunks = kWinCols / 64 < 16 ? kWinCols / 64 : 16;
   static constexpr int kU = RP == 64 ? 2 : 3;            // 32-column blocks per load batch
   static constexpr int kBarrierBytes = 64;
-  static constexpr int kRegroupPitch = 80;  // 64-byte delta rows padded: conflict-free 16-byte access
+  // 64-byte delta rows; 16-byte chunk j of row r sits at chunk j ^ ((r >> 1) & 3), so
+  // both the stmatrix rows and the lanes' 16-byte reads hit 8 distinct bank groups
+  static constexpr int kRegroupPitch = 64;
   static constexpr int kRegroupBytes = kMmaWarps * 16 * kRegroupPitch;
   // + slot table (3 * num_slots + 1 ints), sized at launch
   static constexpr int kSmemBytes = 1024 + 2 * kWinBytes + kBarrierBytes + kRegroupBytes;
@@ -616,8 +618,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     };
     // stmatrix: lane l writes row l & 7 of matrix (tile) l >> 3; ld: row g, columns 8t ..
     const uint32_t rg_base = smem_u32(regroup + warp * 16 * Cfg::kRegroupPitch);
-    const uint32_t rg_st = rg_base + (lane & 7) * Cfg::kRegroupPitch + (lane >> 3) * 16;
-    const uint32_t rg_ld = rg_base + g * Cfg::kRegroupPitch + t * 16;
+    const uint32_t rg_st =
+        rg_base + (lane & 7) * Cfg::kRegroupPitch + 16 * ((lane >> 3) ^ (((lane & 7) >> 1) & 3));
+    const uint32_t rg_ld = rg_base + g * Cfg::kRegroupPitch + 16 * (t ^ ((g >> 1) & 3));
     auto compute_batch = [&](Batch& B) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
