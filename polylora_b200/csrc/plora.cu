@@ -76,7 +76,7 @@ int device_info(DeviceInfo** out) {
                   major, minor);
 #define SET_SMEM(kern, bytes)                                                                  \
   PLORA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,           \
-                                  (int)((bytes) + tab_bytes(kTcMaxSlots))),                     \
+                                  (int)((bytes) + tab_bytes(kFastPathMaxSlots))),                     \
              #kern)
     SET_SMEM((sgmv_shrink_mma_kernel<16, true>), ShrinkMmaCfg<16>::kSmemBytes);
     SET_SMEM((sgmv_shrink_mma_kernel<32, true>), ShrinkMmaCfg<32>::kSmemBytes);
@@ -289,7 +289,7 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
   args.R = (int32_t)R;
   args.stack_num = stack_num;
   const bool tc = dtype != PLORA_DTYPE_F32 && tc_rank_ok(R) && K % 32 == 0 &&
-                  seg.num_slots <= kTcMaxSlots && aligned16(x) &&
+                  seg.num_slots <= kFastPathMaxSlots && aligned16(x) &&
                   aligned16(a) && aligned16(tmp);
   if (tc) {
     CUtensorMap map8, map1;
@@ -347,7 +347,7 @@ int expand_impl(const void* tmp, const void* b, void* y, const int32_t* ranks, c
   args.R = (int32_t)R;
   args.N = (int32_t)N;
   const bool tc = dtype != PLORA_DTYPE_F32 && tc_rank_ok(R) && N % 64 == 0 &&
-                  seg.num_slots <= kTcMaxSlots && aligned16(tmp) &&
+                  seg.num_slots <= kFastPathMaxSlots && aligned16(tmp) &&
                   aligned16(b) && aligned16(y);
   if (tc) {
     CUtensorMap mapn, map1;

@@ -1,25 +1,28 @@
-// SGMV shrink with the activation rows streamed straight into registers.
+// SGMV shrink and expand on the tensor cores with the token rows streamed
+// straight into registers (mma.sync m16n8k16, bf16/fp16 in, fp32 accumulate).
 //
-// The shrink is a gather-and-reduce over HBM: every active token reads its
-// K-wide row of x once, and the rank-R reduction is tiny.  Its speed is set by
-// how many bytes each SM keeps in flight and how few instructions it spends
-// per byte, so x never passes through shared memory: each lane loads 16 bytes
-// (8 consecutive k of one token) and those four registers are, as they are,
-// the B fragments of two m16n8k16 steps of D^T = A^T x^T.  The k order this
-// implies inside a 32-column block (lane quad t owns k = 8t .. 8t + 7) is
-// applied to the LoRA-A rows instead: a 5-D TMA view writes each 32-row block
-// of the slot's weights in the order the ldmatrix.trans fragments read them,
-// so every 8x8 matrix is 8 consecutive swizzled rows (no bank conflicts).
+// Both kernels are gathers over HBM with a tiny rank-R contraction: the shrink
+// reads every active token's K-wide row of x once, the expand reads and
+// rewrites its N-wide row of y once.  Their speed is set by how many bytes each
+// SM keeps in flight and how few instructions and synchronisation points they
+// spend per byte, so the token rows never pass through shared memory: each
+// lane loads 16 bytes (8 consecutive columns of one token row) and those
+// registers feed the mma directly; the expand writes its result back from
+// registers too.  Only the slot's LoRA weights are staged in shared memory, in
+// double-buffered 64 KB windows that TMA lands swizzled so that ldmatrix.trans
+// reads them without bank conflicts.
 //
 // Work split: a CTA takes a contiguous share of the slot-ordered token list,
 // cut into items of <= 128 tokens of one slot.  An item is 16-token tiles x
-// K ranges, one (tile, K range) pair per warp; the per-warp fp32 partial
-// sums are reduced through shared memory at the end of the item.
+// K ranges (shrink) or N ranges (expand), one (tile, range) pair per warp.
+// Window w + 2 of the CTA's window sequence is issued by the last warp to
+// release window w.
 //
-// Reference semantics: src/polylora/sgmv.py:63-138 (_sgmv_lora_a_kernel).
+// Reference semantics: src/polylora/sgmv.py:63-138 (_sgmv_lora_a_kernel) and
+// sgmv.py:178-275 (_sgmv_lora_b_kernel).
 #pragma once
 
-#include "sgmv_tc.cuh"
+#include "sgmv_common.cuh"
 
 namespace plora {
 
@@ -165,7 +168,7 @@ __device__ __noinline__ void issue_lora_a_window(const CUtensorMap* map8, const 
 // Sequence of (slot, window) pairs over the CTA's items with rank > 0, in the
 // order every warp consumes them.
 struct WinCursor {
-  ShrinkItems it;
+  SlotItems it;
   int slot, w, nwin;
   bool valid;
   __device__ void init(const SlotTab& tab, int64_t b, int64_t e, int nw) {
@@ -251,7 +254,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   }
   __syncthreads();
 
-  ShrinkItems items;
+  SlotItems items;
   items.init(tab, begin, end);
   int s, cnt;
   int64_t start;
@@ -521,7 +524,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   }
   __syncthreads();
 
-  ShrinkItems items;
+  SlotItems items;
   items.init(tab, begin, end);
   int s, cnt;
   int64_t start;

@@ -6,7 +6,7 @@
 #pragma once
 
 #include "common.cuh"
-#include "sgmv_tc.cuh"
+#include "sgmv_common.cuh"
 
 namespace plora {
 
