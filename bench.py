@@ -417,6 +417,126 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------- model workloads
+# DeBERTa-v3-large-shaped encoder (random init, bf16), LoRA on
+# query/key/value projections and every `dense` Linear (6 per layer), 32 GPU
+# slots, ranks {4, 8, 16} (a rank-0 adapter is represented by __base__ rows: the
+# adapter store rejects rank 0, as the reference's does), batch 256 x 512
+# right-padded with lengths U[64, 512], 25 % of rows on __base__, uniform
+# popularity.  Rows are sharded over the GPUs (strong scaling of one batch)
+# and the outputs all-gathered.
+CFG3_ROWS, CFG3_SEQ, CFG3_SLOTS = 256, 512, 32
+CFG3_TARGETS = ["query_proj", "key_proj", "value_proj", "dense"]
+
+
+def _deberta_v3_large():
+    from transformers import DebertaV2Config, DebertaV2Model
+
+    cfg = DebertaV2Config(
+        vocab_size=128100, hidden_size=1024, num_hidden_layers=24, num_attention_heads=16,
+        intermediate_size=4096, max_position_embeddings=512, relative_attention=True,
+        position_buckets=256, norm_rel_ebd="layer_norm", share_att_key=True, pos_att_type=["p2c", "c2p"],
+        max_relative_positions=-1, position_biased_input=False, type_vocab_size=0, layer_norm_eps=1e-7,
+        hidden_dropout_prob=0.0, attention_probs_dropout_prob=0.0,
+    )
+    return DebertaV2Model(cfg).eval()
+
+
+def run_model_cfg3(args):
+    import torch
+    import torch.distributed as dist
+
+    from polylora_b200 import PolyLoraConfig, PolyLoraModel
+    from polylora_b200.rowshard import RowParallel
+    from polylora_b200.store import CpuLayerWeights
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.manual_seed(0)
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(dev):
+        base = _deberta_v3_large()
+    torch.set_default_dtype(torch.float32)
+    shapes = {n: (m.in_features, m.out_features) for n, m in base.named_modules()
+              if isinstance(m, torch.nn.Linear) and any(n == t or n.endswith("." + t) for t in CFG3_TARGETS)}
+    model = PolyLoraModel(base, PolyLoraConfig(max_gpu_adapters=CFG3_SLOTS, max_rank=16, target_modules=CFG3_TARGETS))
+    assert set(shapes) == set(model.target_module_names), "target matching differs"
+    g = torch.Generator().manual_seed(1)
+    rng = np.random.default_rng(2)
+    ranks = rng.choice([4, 8, 16], size=CFG3_SLOTS)
+    for a in range(CFG3_SLOTS):
+        r = int(ranks[a])
+        layers = {
+            name: CpuLayerWeights(
+                A=(torch.rand(k, r, generator=g) * 2 - 1) / np.sqrt(k),
+                B=torch.randn(r, n, generator=g) * 0.02,
+                rank=r, scale=2.0,
+            )
+            for name, (k, n) in shapes.items()
+        }
+        model.adapter_store.add_adapter(f"adapter{a}", layers, {"r": r, "lora_alpha": 2 * r})
+    lens = rng.integers(64, CFG3_SEQ + 1, size=CFG3_ROWS)
+    ids = [("__base__" if rng.random() < 0.25 else f"adapter{int(rng.integers(CFG3_SLOTS))}") for _ in range(CFG3_ROWS)]
+    input_ids = torch.randint(0, 128100, (CFG3_ROWS, CFG3_SEQ), generator=g).to(dev)
+    mask = (torch.arange(CFG3_SEQ)[None, :] < torch.from_numpy(lens)[:, None]).long().to(dev)
+    tokens = int(lens.sum())
+
+    lora_fn = RowParallel(lambda adapter_ids, **kw: model(adapter_ids=adapter_ids, **kw).last_hidden_state)
+    base_fn = RowParallel(lambda adapter_ids, **kw: base(**kw).last_hidden_state)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn, steps, warmup):
+        with torch.inference_mode():
+            for _ in range(max(warmup, 3)):
+                fn(ids, input_ids=input_ids, attention_mask=mask)
+            torch.cuda.synchronize()
+            barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                fn(ids, input_ids=input_ids, attention_mask=mask)
+            e1.record()
+            e1.synchronize()
+            barrier()
+        ms = e0.elapsed_time(e1) / steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    gpu_ids = [v for v in visible.split(",") if v.strip().isdigit()]
+    sampler = ClockSampler(int(gpu_ids[local]) if local < len(gpu_ids) else local)
+    sampler.start()
+    ms_lora = timed(lora_fn, args.steps, args.warmup)
+    clocks = sampler.stop()
+    ms_base = timed(base_fn, max(2, args.steps // 2), 2)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": tokens / (ms_lora * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_lora, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {
+                "workload": "BASELINE config 3: DeBERTa-v3-large-shaped encoder (24 layers, hidden 1024, 16 heads, "
+                            "FFN 4096), random init, bf16; LoRA on query/key/value/dense (144 Linears); 32 GPU "
+                            "slots, ranks {4,8,16}, 25% __base__ rows; batch 256 x 512 right-padded, lengths "
+                            "U[64,512]; one forward per step, rows sharded over the GPUs + all-gather",
+                "non_pad_tokens": tokens, "padded_tokens": CFG3_ROWS * CFG3_SEQ,
+            },
+            "padded_tokens_per_s": CFG3_ROWS * CFG3_SEQ / (ms_lora * 1e-3),
+            "base_model_ms_per_step": ms_base,
+            "lora_overhead_frac": ms_lora / ms_base - 1.0,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -424,8 +544,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3"], default="cfg2",
+                    help="cfg2: the SGMV op step (default, the headline line); cfg3: model forward")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.workload == "cfg3":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "config 3 is timed for this library only; "
+                              "the reference arm covers the config-2 op"}), flush=True)
+        else:
+            run_model_cfg3(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
