@@ -481,8 +481,10 @@ def run_model_cfg3(args):
     mask = (torch.arange(CFG3_SEQ)[None, :] < torch.from_numpy(lens)[:, None]).long().to(dev)
     tokens = int(lens.sum())
 
-    lora_fn = RowParallel(lambda adapter_ids, **kw: model(adapter_ids=adapter_ids, **kw).last_hidden_state)
-    base_fn = RowParallel(lambda adapter_ids, **kw: base(**kw).last_hidden_state)
+    # the encoder computes every row at the padded length: balance shards by rows
+    lora_fn = RowParallel(lambda adapter_ids, **kw: model(adapter_ids=adapter_ids, **kw).last_hidden_state,
+                          row_cost=lambda n: 1)
+    base_fn = RowParallel(lambda adapter_ids, **kw: base(**kw).last_hidden_state, row_cost=lambda n: 1)
 
     def barrier():
         if world > 1:
@@ -524,7 +526,7 @@ def run_model_cfg3(args):
                 "workload": "BASELINE config 3: DeBERTa-v3-large-shaped encoder (24 layers, hidden 1024, 16 heads, "
                             "FFN 4096), random init, bf16; LoRA on query/key/value/dense (144 Linears); 32 GPU "
                             "slots, ranks {4,8,16}, 25% __base__ rows; batch 256 x 512 right-padded, lengths "
-                            "U[64,512]; one forward per step, rows sharded over the GPUs + all-gather",
+                            "U[64,512]; one forward per step, rows sharded over the GPUs (equal rows: compute is per padded row) + all-gather",
                 "non_pad_tokens": tokens, "padded_tokens": CFG3_ROWS * CFG3_SEQ,
             },
             "padded_tokens_per_s": CFG3_ROWS * CFG3_SEQ / (ms_lora * 1e-3),

@@ -19,19 +19,26 @@ import torch
 import torch.distributed as dist
 
 
-def partition_rows(seq_lens: Sequence[int], world_size: int) -> list[tuple[int, int]]:
-    """Contiguous row ranges ``[start, end)`` per rank, balanced by tokens.
+def partition_rows(
+    seq_lens: Sequence[int], world_size: int, row_cost: Callable[[int], float] | None = None
+) -> list[tuple[int, int]]:
+    """Contiguous row ranges ``[start, end)`` per rank, balanced by cost.
 
-    Cuts are placed where the running token count crosses k/world_size of the
-    total; every range is non-empty when there are at least ``world_size``
-    rows (otherwise the trailing ranks get empty ranges).  Deterministic, so
-    every rank computes the same partition from the same ``seq_lens``.
+    A row costs ``row_cost(seq_len)``; the default is its valid tokens (at
+    least 1: an empty row still occupies the batch).  A model that computes
+    every row at the padded length (eager attention over the whole padded
+    sequence) costs the same per row: pass ``lambda n: 1`` to balance rows.
+    Cuts are placed where the running cost crosses k/world_size of the total;
+    every range is non-empty when there are at least ``world_size`` rows
+    (otherwise the trailing ranks get empty ranges).  Deterministic, so every
+    rank computes the same partition from the same ``seq_lens``.
     """
     if world_size < 1:
         raise ValueError("world_size must be at least 1")
     lens = [max(int(v), 0) for v in seq_lens]
     rows = len(lens)
-    weights = [max(v, 1) for v in lens]  # empty rows still cost a slot in the batch
+    cost = row_cost if row_cost is not None else (lambda n: max(n, 1))
+    weights = [float(cost(v)) for v in lens]
     total = sum(weights)
     bounds: list[tuple[int, int]] = []
     start = 0
@@ -75,9 +82,11 @@ class RowParallel:
     arguments are passed through.  Returns the full-batch output (all-gathered).
     """
 
-    def __init__(self, fn: Callable[..., torch.Tensor], group=None) -> None:
+    def __init__(self, fn: Callable[..., torch.Tensor], group=None,
+                 row_cost: Callable[[int], float] | None = None) -> None:
         self.fn = fn
         self.group = group
+        self.row_cost = row_cost  # see partition_rows
 
     def __call__(self, adapter_ids: list[str], **batch: Any) -> torch.Tensor:
         world = dist.get_world_size(self.group) if dist.is_initialized() else 1
@@ -89,7 +98,7 @@ class RowParallel:
         else:
             ref = batch.get("input_ids", batch.get("inputs_embeds"))
             seq_lens = [int(ref.shape[1])] * rows
-        bounds = partition_rows(seq_lens, world)
+        bounds = partition_rows(seq_lens, world, self.row_cost)
         start, end = bounds[rank]
         if end == start:  # fewer rows than ranks: run a copy of the last row, drop it
             start, end = rows - 1, rows

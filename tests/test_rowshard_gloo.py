@@ -27,6 +27,16 @@ def test_partition_is_contiguous_covering_and_balanced(lens, world):
         assert max(loads) <= sum(max(v, 1) for v in lens) / world + max(max(v, 1) for v in lens)
 
 
+def test_row_cost_balances_padded_rows():
+    """With a per-row cost of 1 (a model that computes every row at the padded
+    length), shards get equal row counts whatever the valid lengths."""
+    lens = [64] * 48 + [512] * 16  # token balancing would give the short rows' rank 3x the rows
+    b = partition_rows(lens, 4, row_cost=lambda n: 1)
+    assert [e - s for s, e in b] == [16, 16, 16, 16]
+    bt = partition_rows(lens, 4)
+    assert max(e - s for s, e in bt) > 16
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
