@@ -417,6 +417,95 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------- config-2 op sweep
+SWEEP_T = (1, 16, 256, 4096, 16384)
+
+
+def run_sweep(args):
+    """BASELINE config 2 at every T of its sweep: the step (segment table +
+    shrink + expand as one call) as a CUDA graph, timed back to back and with
+    L2 flushed before each step (difference of graphs [flush, step] and [flush])."""
+    import torch
+
+    from polylora_b200.sgmv import build_segments, sgmv_shrink_expand
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    g = torch.Generator(device=dev).manual_seed(1000)
+    ranks_np, _, scales_np = workload(seed=0)
+    ranks = torch.from_numpy(ranks_np).to(dev)
+    scales = torch.from_numpy(scales_np).to(dev)
+    colmask = (torch.arange(MAX_RANK, device=dev)[None, :] < ranks[:, None]).float()
+    A = ((torch.rand(SLOTS, K_IN, MAX_RANK, device=dev, generator=g) * 2 - 1) / 64 * colmask[:, None, :]).to(torch.bfloat16)
+    Bw = (torch.randn(SLOTS, MAX_RANK, N_OUT, device=dev, generator=g) * 0.02 * colmask[:, :, None]).to(torch.bfloat16)
+    flush_w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_r = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    sink = torch.empty((), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    rows = []
+    for T in SWEEP_T:
+        rng = np.random.default_rng(T)
+        wi_np = rng.integers(1, SLOTS, size=T).astype(np.int64)
+        wi_np[rng.random(T) < 0.2] = 0
+        wi = torch.from_numpy(wi_np).to(dev)
+        seq = torch.ones(T, dtype=torch.int32, device=dev)
+        x = torch.randn(T, 1, K_IN, device=dev, generator=g).to(torch.bfloat16)
+        y = torch.randn(T, 1, N_OUT, device=dev, generator=g).to(torch.bfloat16)
+        tmp = torch.empty(T, 1, MAX_RANK, device=dev, dtype=torch.bfloat16)
+
+        def step():
+            table = build_segments(wi, seq, ranks, 1)
+            sgmv_shrink_expand(x, A, Bw, y, table, ranks, scales, tmp=tmp)
+
+        def flush():
+            flush_w.fill_(7)
+            torch.sum(flush_r, dim=0, out=sink)
+
+        def graph_of(fns):
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    for f in fns:
+                        f()
+                torch.cuda.synchronize()
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=stream):
+                    for f in fns:
+                        f()
+                gr.replay()
+            torch.cuda.synchronize()
+            return gr
+
+        def replay_ms(gr, reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                a.record(stream)
+                for _ in range(reps):
+                    gr.replay()
+                b.record(stream)
+            b.synchronize()
+            return a.elapsed_time(b) / reps
+
+        reps = max(args.steps, 20)
+        g_step, g_flush, g_both = graph_of([step]), graph_of([flush]), graph_of([flush, step])
+        warm = replay_ms(g_step, reps)
+        cold = sorted(replay_ms(g_both, reps) - replay_ms(g_flush, reps) for _ in range(3))[1]
+        _, b_s, b_e, _ = algorithmic_bytes(ranks_np, wi_np)
+        rows.append({"T": T, "active_tokens": int((ranks_np[wi_np] > 0).sum()),
+                     "us_per_step_back_to_back": round(warm * 1e3, 2), "us_per_step_l2_flushed": round(cold * 1e3, 2),
+                     "tokens_per_s": T / (warm * 1e-3), "sgmv_gbs_l2_flushed": (b_s + b_e) / (cold * 1e-3) / 1e9})
+        del x, y, tmp
+    big = rows[-1]
+    line = {
+        "metric": METRIC, "value": big["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": 3, "ms_per_step": big["us_per_step_back_to_back"] / 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "BASELINE config 2 op sweep, T in {1,16,256,4096,16384}, K=N=4096, 64 slots, "
+                               "max_rank 16; step = segment table + shrink + expand (one call), CUDA graph"},
+        "sweep": rows,
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ---------------------------------------------------------------- model workloads
 # BASELINE config 3: DeBERTa-v3-large-shaped encoder (random init, bf16), LoRA on
 # query/key/value projections and every `dense` Linear (6 per layer), 32 GPU
@@ -539,6 +628,127 @@ def run_model_cfg3(args):
         dist.destroy_process_group()
 
 
+# Llama-3-8B-shaped decoder (32 layers, hidden 4096, 32 query
+# / 8 KV heads, FFN 14336, vocab 128256), random init, bf16; LoRA on q/k/v/o/
+# gate/up/down (224 Linears); 128 adapters resident in 128 GPU slots, max_rank
+# 64, ranks {8, 16, 32, 64}, Zipf(1.1) popularity.  Two steps: prefill of
+# 64 x 1024 tokens and decode of 256 x 1 token (one forward each, no KV history);
+# rows sharded over the GPUs (strong scaling) and the outputs all-gathered.
+CFG4_ADAPTERS, CFG4_RANK = 128, 64
+CFG4_TARGETS = ["q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"]
+
+
+def _llama3_8b():
+    from transformers import LlamaConfig, LlamaModel
+
+    cfg = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+                      num_attention_heads=32, num_key_value_heads=8, max_position_embeddings=8192,
+                      rope_theta=500000.0, use_cache=False)
+    return LlamaModel(cfg).eval()
+
+
+def run_model_cfg4(args):
+    import torch
+    import torch.distributed as dist
+
+    from polylora_b200 import PolyLoraConfig, PolyLoraModel
+    from polylora_b200.rowshard import RowParallel
+    from polylora_b200.store import CpuLayerWeights
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.manual_seed(0)
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(dev):
+        base = _llama3_8b()
+    torch.set_default_dtype(torch.float32)
+    shapes = {n: (m.in_features, m.out_features) for n, m in base.named_modules()
+              if isinstance(m, torch.nn.Linear) and any(n == t or n.endswith("." + t) for t in CFG4_TARGETS)}
+    model = PolyLoraModel(base, PolyLoraConfig(max_gpu_adapters=CFG4_ADAPTERS, max_rank=CFG4_RANK,
+                                               target_modules=CFG4_TARGETS))
+    # random rank-64 factors per distinct (in, out) shape; an adapter of rank r
+    # uses their first r columns / rows (values do not change the timing)
+    g = torch.Generator().manual_seed(1)
+    src = {}
+    for k, n in set(shapes.values()):
+        src[(k, n)] = ((torch.rand(k, CFG4_RANK, generator=g) * 2 - 1) / np.sqrt(k),
+                       torch.randn(CFG4_RANK, n, generator=g) * 0.02)
+    rng = np.random.default_rng(2)
+    ranks = rng.choice([8, 16, 32, 64], size=CFG4_ADAPTERS)
+    for a in range(CFG4_ADAPTERS):
+        r = int(ranks[a])
+        layers = {name: CpuLayerWeights(A=src[kn][0][:, :r], B=src[kn][1][:r], rank=r, scale=2.0)
+                  for name, kn in shapes.items()}
+        model.adapter_store.add_adapter(f"adapter{a}", layers, {"r": r, "lora_alpha": 2 * r})
+    pop = 1.0 / np.arange(1, CFG4_ADAPTERS + 1) ** 1.1
+    pop /= pop.sum()
+
+    def batch(rows, seq):
+        ids = [f"adapter{int(i)}" for i in rng.choice(CFG4_ADAPTERS, size=rows, p=pop)]
+        input_ids = torch.randint(0, 128256, (rows, seq), generator=g).to(dev)
+        mask = torch.ones(rows, seq, dtype=torch.long, device=dev)
+        return ids, input_ids, mask
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn, ids, input_ids, mask, steps, warmup):
+        with torch.inference_mode():
+            for _ in range(max(warmup, 2)):
+                fn(ids, input_ids=input_ids, attention_mask=mask)
+            torch.cuda.synchronize()
+            barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                fn(ids, input_ids=input_ids, attention_mask=mask)
+            e1.record()
+            e1.synchronize()
+            barrier()
+        ms = e0.elapsed_time(e1) / steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    lora_fn = RowParallel(lambda adapter_ids, **kw: model(adapter_ids=adapter_ids, **kw).last_hidden_state)
+    base_fn = RowParallel(lambda adapter_ids, **kw: base(**kw).last_hidden_state)
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    gpu_ids = [v for v in visible.split(",") if v.strip().isdigit()]
+    sampler = ClockSampler(int(gpu_ids[local]) if local < len(gpu_ids) else local)
+    res = {}
+    sampler.start()
+    for name, rows, seq in (("prefill", 64, 1024), ("decode", 256, 1)):
+        ids, input_ids, mask = batch(rows, seq)
+        ms = timed(lora_fn, ids, input_ids, mask, args.steps, args.warmup)
+        ms_base = timed(base_fn, ids, input_ids, mask, max(2, args.steps // 2), 2)
+        res[name] = {"rows": rows, "seq": seq, "tokens": rows * seq, "distinct_adapters": len(set(ids)),
+                     "ms_per_step": ms, "tokens_per_s": rows * seq / (ms * 1e-3),
+                     "base_model_ms_per_step": ms_base, "lora_overhead_frac": ms / ms_base - 1.0}
+    clocks = sampler.stop()
+    if rank == 0:
+        pre = res["prefill"]
+        line = {
+            "metric": METRIC, "value": pre["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": pre["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": "BASELINE config 4: Llama-3-8B-shaped decoder (32 layers, hidden 4096, 32/8 heads, FFN "
+                            "14336), random init, bf16; LoRA on q/k/v/o/gate/up/down (224 Linears); 128 adapters "
+                            "in 128 GPU slots, max_rank 64, ranks {8,16,32,64}, Zipf(1.1) popularity; value = "
+                            "prefill 64 x 1024 tokens/s; decode 256 x 1 below; rows sharded over the GPUs + "
+                            "all-gather",
+            },
+            "prefill": pre, "decode": res["decode"], "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -546,15 +756,19 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3"], default="cfg2",
+    ap.add_argument("--workload", choices=["cfg2", "cfg2-sweep", "cfg3", "cfg4"], default="cfg2",
                     help="cfg2: the SGMV op step (default, the headline line); cfg3: model forward")
     args = ap.parse_args()
-    if args.workload == "cfg3":
+    if args.workload == "cfg2-sweep" and args.impl != "reference":
+        run_sweep(args)
+    elif args.workload in ("cfg3", "cfg4"):
         if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "config 3 is timed for this library only; "
-                              "the reference arm covers the config-2 op"}), flush=True)
-        else:
+            print(json.dumps({"impl": "reference", "unavailable": f"{args.workload} is timed for this library "
+                              "only; the reference arm covers the config-2 op"}), flush=True)
+        elif args.workload == "cfg3":
             run_model_cfg3(args)
+        else:
+            run_model_cfg4(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
