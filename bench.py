@@ -713,6 +713,44 @@ def run_model_cfg4(args):
             ms = float(t.item())
         return ms
 
+    def time_graphed_decode(model, base, ids, input_ids, steps):
+        """Decode forward replayed as one CUDA graph per call (GraphedForward;
+        unpadded rows, so no mask), beside the base model captured the same way."""
+        from polylora_b200.graphed import GraphedForward
+
+        with torch.inference_mode():
+            graphed = GraphedForward(model, ids, input_ids=input_ids)
+            static_ids = input_ids.clone()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    base(input_ids=static_ids)
+            torch.cuda.current_stream().wait_stream(side)
+            base_graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(base_graph):
+                base(input_ids=static_ids)
+            ref = model(input_ids=input_ids, adapter_ids=ids).last_hidden_state
+            match = bool(torch.equal(graphed(ids, input_ids=input_ids), ref))
+            out = {}
+            for key, fn in (("ms_per_step", lambda: graphed(ids, input_ids=input_ids)),
+                            ("base_model_ms_per_step", base_graph.replay)):
+                for _ in range(3):
+                    fn()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(steps):
+                    fn()
+                e1.record()
+                e1.synchronize()
+                out[key] = e0.elapsed_time(e1) / steps
+            del base_graph, graphed
+        out["tokens_per_s"] = input_ids.numel() / (out["ms_per_step"] * 1e-3)
+        out["lora_overhead_frac"] = out["ms_per_step"] / out["base_model_ms_per_step"] - 1.0
+        out["equals_eager_forward"] = match
+        return out
+
     lora_fn = RowParallel(lambda adapter_ids, **kw: model(adapter_ids=adapter_ids, **kw).last_hidden_state)
     base_fn = RowParallel(lambda adapter_ids, **kw: base(**kw).last_hidden_state)
     visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
@@ -720,16 +758,21 @@ def run_model_cfg4(args):
     sampler = ClockSampler(int(gpu_ids[local]) if local < len(gpu_ids) else local)
     res = {}
     sampler.start()
-    for name, rows, seq in (("prefill", 64, 1024), ("decode", 256, 1)):
+    phases = (("prefill", 64, 1024), ("decode", 256, 1))
+    if args.workload == "cfg4-decode":
+        phases = phases[1:]
+    for name, rows, seq in phases:
         ids, input_ids, mask = batch(rows, seq)
         ms = timed(lora_fn, ids, input_ids, mask, args.steps, args.warmup)
         ms_base = timed(base_fn, ids, input_ids, mask, max(2, args.steps // 2), 2)
         res[name] = {"rows": rows, "seq": seq, "tokens": rows * seq, "distinct_adapters": len(set(ids)),
                      "ms_per_step": ms, "tokens_per_s": rows * seq / (ms * 1e-3),
                      "base_model_ms_per_step": ms_base, "lora_overhead_frac": ms / ms_base - 1.0}
+        if name == "decode" and world == 1:
+            res[name]["graphed"] = time_graphed_decode(model, base, ids, input_ids, args.steps)
     clocks = sampler.stop()
     if rank == 0:
-        pre = res["prefill"]
+        pre = res.get("prefill") or res["decode"]
         line = {
             "metric": METRIC, "value": pre["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": pre["ms_per_step"],
@@ -740,9 +783,11 @@ def run_model_cfg4(args):
                             "14336), random init, bf16; LoRA on q/k/v/o/gate/up/down (224 Linears); 128 adapters "
                             "in 128 GPU slots, max_rank 64, ranks {8,16,32,64}, Zipf(1.1) popularity; value = "
                             "prefill 64 x 1024 tokens/s; decode 256 x 1 below; rows sharded over the GPUs + "
-                            "all-gather",
+                            "all-gather" if "prefill" in res else
+                            "BASELINE config 4 decode leg only: 256 x 1 tokens/s (Llama-3-8B-shaped, 128 adapters, "
+                            "max_rank 64, Zipf(1.1))",
             },
-            "prefill": pre, "decode": res["decode"], "clocks": clocks,
+            **res, "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -756,12 +801,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["cfg2", "cfg2-sweep", "cfg3", "cfg4"], default="cfg2",
+    ap.add_argument("--workload", choices=["cfg2", "cfg2-sweep", "cfg3", "cfg4", "cfg4-decode"], default="cfg2",
                     help="cfg2: the SGMV op step (default, the headline line); cfg3: model forward")
     args = ap.parse_args()
     if args.workload == "cfg2-sweep" and args.impl != "reference":
         run_sweep(args)
-    elif args.workload in ("cfg3", "cfg4"):
+    elif args.workload in ("cfg3", "cfg4", "cfg4-decode"):
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": f"{args.workload} is timed for this library "
                               "only; the reference arm covers the config-2 op"}), flush=True)

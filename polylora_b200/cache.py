@@ -275,8 +275,11 @@ class GpuAdapterCache:
             self._slot_last_use[slot] = event
 
     def wait_ready(self, stream: torch.cuda.Stream | None = None) -> None:
-        """Makes `stream` (default: current) wait for the pending refills."""
-        if self.ready_event is not None:
+        """Makes `stream` (default: current) wait for the pending refills.
+
+        Not during stream capture: a captured forward (``GraphedForward``)
+        orders the refills before each replay, outside the graph."""
+        if self.ready_event is not None and not torch.cuda.is_current_stream_capturing():
             (stream or torch.cuda.current_stream(self.device)).wait_event(self.ready_event)
 
     def synchronize(self) -> None:
