@@ -506,6 +506,131 @@ def run_sweep(args):
     print(json.dumps(line), flush=True)
 
 
+def _graph_timer(stream):
+    """(graph_of, replay_ms): capture callables as one CUDA graph after three
+    eager warm-up passes; mean device time of `reps` back-to-back replays."""
+    import torch
+
+    def graph_of(fns):
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                for f in fns:
+                    f()
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                for f in fns:
+                    f()
+            gr.replay()
+        torch.cuda.synchronize()
+        return gr
+
+    def replay_ms(gr, reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a.record(stream)
+            for _ in range(reps):
+                gr.replay()
+            b.record(stream)
+        b.synchronize()
+        return a.elapsed_time(b) / reps
+
+    return graph_of, replay_ms
+
+
+# BASELINE config 4's decode step at the op level: the seven wrapped Linears of
+# one Llama-3-8B layer (in -> out features), 256 decode tokens over 128 slots of
+# max_rank 64, ranks {8, 16, 32, 64}, Zipf(1.1) adapter popularity.
+CFG4_LINEARS = (("q_proj", 4096, 4096), ("k_proj", 4096, 1024), ("v_proj", 4096, 1024), ("o_proj", 4096, 4096),
+                ("gate_proj", 4096, 14336), ("up_proj", 4096, 14336), ("down_proj", 14336, 4096))
+
+
+def run_cfg4_ops(args):
+    """Shrink, expand and the combined call for each Linear shape of config 4's
+    decode step, under both work splits, with L2 flushed before every launch
+    (difference of graphs [flush, op] and [flush]).  Algorithmic bytes: the
+    LoRA weights of the slots in the batch at their ranks, x / y rows, tmp."""
+    import torch
+
+    from polylora_b200 import _native
+    from polylora_b200.sgmv import build_segments, sgmv_expand, sgmv_shrink, sgmv_shrink_expand
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    ns, R, T = CFG4_ADAPTERS, CFG4_RANK, 256
+    rng = np.random.default_rng(2)
+    ranks_np = rng.choice([8, 16, 32, 64], size=ns).astype(np.int32)
+    pop = 1.0 / np.arange(1, ns + 1) ** 1.1
+    pop /= pop.sum()
+    wi_np = rng.choice(ns, size=T, p=pop).astype(np.int64)
+    used = np.unique(wi_np)
+    ranks = torch.from_numpy(ranks_np).to(dev)
+    scales = torch.full((ns,), 2.0, device=dev)
+    wi = torch.from_numpy(wi_np).to(dev)
+    seq = torch.ones(T, dtype=torch.int32, device=dev)
+    table = build_segments(wi, seq, ranks, 1)
+    g = torch.Generator(device=dev).manual_seed(3)
+    colmask = (torch.arange(R, device=dev)[None, :] < ranks[:, None]).float()
+    flush_w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_r = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    sink = torch.empty((), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    graph_of, replay_ms = _graph_timer(stream)
+
+    def flush():
+        flush_w.fill_(7)
+        torch.sum(flush_r, dim=0, out=sink)
+
+    g_flush = graph_of([flush])
+    reps = max(args.steps, 20)
+    rows = []
+    prev = _native.weight_split_tokens_per_sm()
+    try:
+        linears = [lin for lin in CFG4_LINEARS if args.linear in (None, lin[0])]
+        splits = [sp for sp in (("token_split", 0), ("weight_split", 1 << 40)) if args.split in (None, sp[0])]
+        for name, K, N in linears:
+            A = ((torch.rand(ns, K, R, device=dev, generator=g) * 2 - 1) / 64 * colmask[:, None, :]).to(torch.bfloat16)
+            Bw = (torch.randn(ns, R, N, device=dev, generator=g) * 0.02 * colmask[:, :, None]).to(torch.bfloat16)
+            x = torch.randn(T, 1, K, device=dev, generator=g).to(torch.bfloat16)
+            y = torch.randn(T, 1, N, device=dev, generator=g).to(torch.bfloat16)
+            tmp = torch.empty(T, 1, R, device=dev, dtype=torch.bfloat16)
+            rk_used = int(ranks_np[used].sum())
+            b_shrink = rk_used * K * 2 + T * K * 2 + T * R * 2
+            b_expand = rk_used * N * 2 + T * N * 4 + T * R * 2
+            ops = {
+                "shrink": (lambda: sgmv_shrink(x, A, table, ranks, out=tmp), b_shrink),
+                "expand": (lambda: sgmv_expand(tmp, Bw, y, table, ranks, scales), b_expand),
+                "shrink_expand": (lambda: sgmv_shrink_expand(x, A, Bw, y, table, ranks, scales, tmp=tmp),
+                                  b_shrink + b_expand),
+            }
+            row = {"linear": name, "K": K, "N": N}
+            for split, thr in splits:
+                _native.weight_split_tokens_per_sm(thr)
+                for op, (fn, nbytes) in ops.items():
+                    g_both = graph_of([flush, fn])
+                    us = sorted(replay_ms(g_both, reps) - replay_ms(g_flush, reps) for _ in range(3))[1] * 1e3
+                    row[f"{split}_{op}_us"] = round(us, 2)
+                    row[f"{split}_{op}_gbs"] = round(nbytes / (us * 1e-6) / 1e9, 1)
+                    del g_both
+            rows.append(row)
+            del A, Bw, x, y, tmp
+    finally:
+        _native.weight_split_tokens_per_sm(prev)
+    split_name = splits[-1][0]
+    layer_us = sum(r[f"{split_name}_shrink_expand_us"] for r in rows)
+    line = {
+        "metric": METRIC, "value": T / (layer_us * 1e-6), "unit": "tokens/s", "n_gpus": 1, "steps": reps,
+        "warmup": 3, "ms_per_step": layer_us / 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "BASELINE config 4 decode, op level: the 7 LoRA Linears of one Llama-3-8B layer, "
+                               "256 tokens over 128 slots (max_rank 64, ranks {8,16,32,64}, Zipf(1.1)), "
+                               f"{len(used)} distinct adapters; value = tokens/s through the combined calls "
+                               f"({split_name}) of the Linears listed, L2 flushed before each launch"},
+        "linears": rows,
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ---------------------------------------------------------------- model workloads
 # BASELINE config 3: DeBERTa-v3-large-shaped encoder (random init, bf16), LoRA on
 # query/key/value projections and every `dense` Linear (6 per layer), 32 GPU
@@ -801,11 +926,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["cfg2", "cfg2-sweep", "cfg3", "cfg4", "cfg4-decode"], default="cfg2",
+    ap.add_argument("--workload", choices=["cfg2", "cfg2-sweep", "cfg3", "cfg4", "cfg4-decode", "cfg4-ops"],
+                    default="cfg2",
                     help="cfg2: the SGMV op step (default, the headline line); cfg3: model forward")
+    ap.add_argument("--linear", default=None, help="cfg4-ops: only this Linear (e.g. gate_proj)")
+    ap.add_argument("--split", choices=["token_split", "weight_split"], default=None,
+                    help="cfg4-ops: only this work split")
     args = ap.parse_args()
     if args.workload == "cfg2-sweep" and args.impl != "reference":
         run_sweep(args)
+    elif args.workload == "cfg4-ops" and args.impl != "reference":
+        run_cfg4_ops(args)
     elif args.workload in ("cfg3", "cfg4", "cfg4-decode"):
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": f"{args.workload} is timed for this library "

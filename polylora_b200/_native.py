@@ -80,6 +80,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "plora_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "plora_last_error": (ctypes.c_char_p, []),
     "plora_device_status": (ctypes.c_int, [ctypes.POINTER(_i32), _i32]),
+    "plora_weight_split_tokens_per_sm": (_i64, [_i64]),
     "plora_workspace_size": (_size, [_i64, _i64, _i32]),
     "plora_build_segments": (
         ctypes.c_int,
@@ -192,6 +193,12 @@ def device_status(clear: bool = True) -> int:
     out = _i32(0)
     load().plora_device_status(ctypes.byref(out), 1 if clear else 0)
     return int(out.value)
+
+
+def weight_split_tokens_per_sm(value: int = -1) -> int:
+    """Sets (value >= 0) and returns the previous work-split threshold of the
+    tensor-core kernels, in tokens per SM (see plora_weight_split_tokens_per_sm)."""
+    return int(load().plora_weight_split_tokens_per_sm(value))
 
 
 def workspace_size(num_rows: int, max_seq: int, num_slots: int) -> int:

@@ -134,6 +134,17 @@ __device__ __forceinline__ void griddep_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Coherent (L2) loads for data that the grid before this one in the stream
+// writes.  A programmatically launched kernel may start while that grid still
+// runs; __ldg (a read-only load) may be scheduled above griddep_wait() and
+// then read stale data, while these volatile loads stay after it.
+__device__ __forceinline__ uint32_t ld_cg_u32(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ int32_t ld_cg_i32(const int32_t* p) { return (int32_t)ld_cg_u32(p); }
+
 // 4-D tiled TMA load (box starting at (0, 0, c2, c3)), completing on `bar`.
 __device__ __forceinline__ void tma_load_4d_outer(uint32_t dst, const void* tmap, uint64_t* bar,
                                                   int c2, int c3) {

@@ -13,7 +13,7 @@
 #include "common.cuh"
 #include "segments.cuh"
 #include "sgmv_simt.cuh"
-#include "sgmv_mma.cuh"
+#include "sgmv_grid.cuh"
 
 using namespace plora;
 
@@ -49,8 +49,8 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 constexpr int kMaxDevices = 64;
 
-// Shared-memory bytes of the per-slot table staged by the tensor-core kernels.
-size_t tab_bytes(int32_t ns) { return ((size_t)(3 * ns + 1) * 4 + 15) & ~(size_t)15; }
+// Shared-memory bytes of the per-slot table staged by the token-split kernels.
+size_t tab_bytes(int32_t ns) { return (size_t)slot_tab_bytes(ns); }
 
 struct DeviceInfo {
   int sm_count = 0;
@@ -58,6 +58,16 @@ struct DeviceInfo {
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
+
+// Batches of at most this many tokens per SM run the slot-grid kernels
+// (sgmv_grid.cuh): their slots have few tokens each, so giving every (slot,
+// weight part) a CTA beats giving each CTA a share of the tokens (which makes
+// every CTA stream the whole LoRA weights of each slot it touches).
+std::atomic<int64_t> g_wsplit_tokens_per_sm{16};
+
+bool use_weight_split(int64_t num_tokens, const DeviceInfo* di) {
+  return num_tokens <= g_wsplit_tokens_per_sm.load(std::memory_order_relaxed) * di->sm_count;
+}
 
 int device_info(DeviceInfo** out) {
   int dev = 0;
@@ -76,21 +86,37 @@ int device_info(DeviceInfo** out) {
                   major, minor);
 #define SET_SMEM(kern, bytes)                                                                  \
   PLORA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,           \
-                                  (int)((bytes) + tab_bytes(kFastPathMaxSlots))),                     \
-             #kern)
-    SET_SMEM((sgmv_shrink_mma_kernel<16, true>), ShrinkMmaCfg<16>::kSmemBytes);
-    SET_SMEM((sgmv_shrink_mma_kernel<32, true>), ShrinkMmaCfg<32>::kSmemBytes);
-    SET_SMEM((sgmv_shrink_mma_kernel<64, true>), ShrinkMmaCfg<64>::kSmemBytes);
-    SET_SMEM((sgmv_shrink_mma_kernel<16, false>), ShrinkMmaCfg<16>::kSmemBytes);
-    SET_SMEM((sgmv_shrink_mma_kernel<32, false>), ShrinkMmaCfg<32>::kSmemBytes);
-    SET_SMEM((sgmv_shrink_mma_kernel<64, false>), ShrinkMmaCfg<64>::kSmemBytes);
-    SET_SMEM((sgmv_expand_mma_kernel<16, true>), ExpandMmaCfg<16>::kSmemBytes);
-    SET_SMEM((sgmv_expand_mma_kernel<32, true>), ExpandMmaCfg<32>::kSmemBytes);
-    SET_SMEM((sgmv_expand_mma_kernel<64, true>), ExpandMmaCfg<64>::kSmemBytes);
-    SET_SMEM((sgmv_expand_mma_kernel<16, false>), ExpandMmaCfg<16>::kSmemBytes);
-    SET_SMEM((sgmv_expand_mma_kernel<32, false>), ExpandMmaCfg<32>::kSmemBytes);
-    SET_SMEM((sgmv_expand_mma_kernel<64, false>), ExpandMmaCfg<64>::kSmemBytes);
+                                  (int)((bytes) + tab_bytes(kFastPathMaxSlots))),              \
+             #kern);
+#define SET_SMEM_BOTH(name, RPV, bytes)   \
+  SET_SMEM((name<RPV, true>), bytes)      \
+  SET_SMEM((name<RPV, false>), bytes)
+    SET_SMEM_BOTH(sgmv_shrink_mma_kernel, 16, ShrinkMmaCfg<16>::kSmemBytes)
+    SET_SMEM_BOTH(sgmv_shrink_mma_kernel, 32, ShrinkMmaCfg<32>::kSmemBytes)
+    SET_SMEM_BOTH(sgmv_shrink_mma_kernel, 64, ShrinkMmaCfg<64>::kSmemBytes)
+    SET_SMEM_BOTH(sgmv_expand_mma_kernel, 16, ExpandMmaCfg<16>::kSmemBytes)
+    SET_SMEM_BOTH(sgmv_expand_mma_kernel, 32, ExpandMmaCfg<32>::kSmemBytes)
+    SET_SMEM_BOTH(sgmv_expand_mma_kernel, 64, ExpandMmaCfg<64>::kSmemBytes)
+#undef SET_SMEM_BOTH
 #undef SET_SMEM
+#define SET_GRID(kern, bytes)                                                                  \
+  PLORA_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,           \
+                                  (int)(bytes)),                                               \
+             #kern);
+#define SET_GRID_ALL(RPV)                                                                      \
+  SET_GRID((sgmv_expand_grid_kernel<RPV, true>), ExpandGridCfg<RPV>::kSmemBytes)               \
+  SET_GRID((sgmv_expand_grid_kernel<RPV, false>), ExpandGridCfg<RPV>::kSmemBytes)              \
+  SET_GRID((sgmv_shrink_grid_kernel<RPV, true>), ShrinkGridCfg<RPV>::kSmemBytes)               \
+  SET_GRID((sgmv_shrink_grid_kernel<RPV, false>), ShrinkGridCfg<RPV>::kSmemBytes)              \
+  PLORA_CUDA(cudaFuncSetAttribute((sgmv_shrink_grid_kernel<RPV, true>),                        \
+                                  cudaFuncAttributeNonPortableClusterSizeAllowed, 1), "cluster"); \
+  PLORA_CUDA(cudaFuncSetAttribute((sgmv_shrink_grid_kernel<RPV, false>),                       \
+                                  cudaFuncAttributeNonPortableClusterSizeAllowed, 1), "cluster");
+    SET_GRID_ALL(16)
+    SET_GRID_ALL(32)
+    SET_GRID_ALL(64)
+#undef SET_GRID_ALL
+#undef SET_GRID
     d.attrs_set = true;
   }
   *out = &d;
@@ -257,21 +283,43 @@ bool tc_rank_ok(int64_t R) { return R == 16 || R == 32 || R == 64; }
 // Launches `kernel` with programmatic stream serialisation when `pdl` is set:
 // the kernel may then start while its predecessor in the stream finishes and
 // must call griddep_wait() before reading anything that predecessor writes.
+// With cluster_x > 0 the grid is launched as clusters of cluster_x CTAs along x.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                          cudaStream_t stream, bool pdl, Args&&... args) {
+                          cudaStream_t stream, bool pdl, int cluster_x, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 0) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
+
+// K parts of the grid-split shrink: parts of >= 512 rows (a multiple of 32),
+// at most 16 (the largest cluster).
+void grid_k_parts(int64_t K, int* parts, int* part_rows) {
+  int kp = (int)std::min<int64_t>(16, std::max<int64_t>(1, (K + 511) / 512));
+  const int rows = (int)(((K + kp - 1) / kp + 31) / 32 * 32);
+  *part_rows = rows;
+  *parts = (int)((K + rows - 1) / rows);
+}
+
 
 int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, SegTable seg,
                 int64_t num_tokens, int64_t K, int64_t R, int32_t stack_num, int32_t dtype,
@@ -292,6 +340,27 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
                   seg.num_slots <= kFastPathMaxSlots && aligned16(x) &&
                   aligned16(a) && aligned16(tmp);
   if (tc) {
+    const bool bf = dtype == PLORA_DTYPE_BF16;
+    if (use_weight_split(num_tokens, di)) {  // few tokens per slot: grid split
+      int kp = 0, kp_rows = 0;
+      grid_k_parts(K, &kp, &kp_rows);
+      const dim3 grid((unsigned)kp, (unsigned)seg.num_slots);
+      // the kernel reads its inputs only after griddep_wait(): always launched programmatically
+#define LAUNCH_SHRINK_GRID(RPV)                                                                    \
+  PLORA_CUDA(launch_kernel(bf ? sgmv_shrink_grid_kernel<RPV, true> : sgmv_shrink_grid_kernel<RPV, false>, \
+                           grid, dim3(kGridThreads), ShrinkGridCfg<RPV>::kSmemBytes, stream, true, kp, \
+                           args, kp_rows),                                                         \
+             "launch sgmv_shrink_grid_kernel");
+      if (R == 16) {
+        LAUNCH_SHRINK_GRID(16)
+      } else if (R == 32) {
+        LAUNCH_SHRINK_GRID(32)
+      } else {
+        LAUNCH_SHRINK_GRID(64)
+      }
+#undef LAUNCH_SHRINK_GRID
+      return check_launch("sgmv_shrink_grid_kernel");
+    }
     CUtensorMap map8, map1;
     const CUtensorMapSwizzle swz = R == 16   ? CU_TENSOR_MAP_SWIZZLE_32B
                                    : R == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
@@ -301,14 +370,12 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
         (st = make_map_lora_a_blocks(&map1, a, dtype, (uint64_t)R, (uint64_t)K,
                                      (uint64_t)seg.num_slots, 1, swz)))
       return st;
-    (void)num_tokens;
     const dim3 grid(di->sm_count), block(kMmaThreads);
     const size_t tb = tab_bytes(seg.num_slots);
-    const bool bf = dtype == PLORA_DTYPE_BF16;
     // the kernel reads its inputs only after griddep_wait(): always launched programmatically
 #define LAUNCH_SHRINK(RPV)                                                                         \
   PLORA_CUDA(launch_kernel(bf ? sgmv_shrink_mma_kernel<RPV, true> : sgmv_shrink_mma_kernel<RPV, false>, \
-                           grid, block, ShrinkMmaCfg<RPV>::kSmemBytes + tb, stream, true, map8, map1, args), \
+                           grid, block, ShrinkMmaCfg<RPV>::kSmemBytes + tb, stream, true, 0, map8, map1, args), \
              "launch sgmv_shrink_mma_kernel");
     if (R == 16) {
       LAUNCH_SHRINK(16)
@@ -332,8 +399,8 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
 }
 
 int expand_impl(const void* tmp, const void* b, void* y, const int32_t* ranks, const float* scales,
-                SegTable seg, int64_t R, int64_t N, int32_t dtype, cudaStream_t stream,
-                bool after_shrink = false) {
+                SegTable seg, int64_t num_tokens, int64_t R, int64_t N, int32_t dtype,
+                cudaStream_t stream, bool after_shrink = false) {
   DeviceInfo* di = nullptr;
   int st = device_info(&di);
   if (st) return st;
@@ -350,6 +417,25 @@ int expand_impl(const void* tmp, const void* b, void* y, const int32_t* ranks, c
                   seg.num_slots <= kFastPathMaxSlots && aligned16(tmp) &&
                   aligned16(b) && aligned16(y);
   if (tc) {
+    const bool bf = dtype == PLORA_DTYPE_BF16;
+    if (use_weight_split(num_tokens, di)) {  // few tokens per slot: grid split
+      const dim3 grid((unsigned)((N + kGridCols - 1) / kGridCols), (unsigned)seg.num_slots);
+      // programmatic only right after this library's shrink: tmp is read after griddep_wait()
+#define LAUNCH_EXPAND_GRID(RPV)                                                                    \
+  PLORA_CUDA(launch_kernel(bf ? sgmv_expand_grid_kernel<RPV, true> : sgmv_expand_grid_kernel<RPV, false>, \
+                           grid, dim3(kGridThreads), ExpandGridCfg<RPV>::kSmemBytes, stream,       \
+                           after_shrink, 0, args),                                                 \
+             "launch sgmv_expand_grid_kernel");
+      if (R == 16) {
+        LAUNCH_EXPAND_GRID(16)
+      } else if (R == 32) {
+        LAUNCH_EXPAND_GRID(32)
+      } else {
+        LAUNCH_EXPAND_GRID(64)
+      }
+#undef LAUNCH_EXPAND_GRID
+      return check_launch("sgmv_expand_grid_kernel");
+    }
     CUtensorMap mapn, map1;
     const uint32_t box = R == 16 ? ExpandMmaCfg<16>::kBoxChunks
                          : R == 32 ? ExpandMmaCfg<32>::kBoxChunks
@@ -361,12 +447,11 @@ int expand_impl(const void* tmp, const void* b, void* y, const int32_t* ranks, c
       return st;
     const dim3 grid(di->sm_count), block(kMmaThreads);
     const size_t tb = tab_bytes(seg.num_slots);
-    const bool bf = dtype == PLORA_DTYPE_BF16;
     // programmatic only right after this library's shrink (after_shrink): the kernel reads
     // the segment table, LoRA-B and y before griddep_wait(), tmp after it
 #define LAUNCH_EXPAND(RPV)                                                                         \
   PLORA_CUDA(launch_kernel(bf ? sgmv_expand_mma_kernel<RPV, true> : sgmv_expand_mma_kernel<RPV, false>, \
-                           grid, block, ExpandMmaCfg<RPV>::kSmemBytes + tb, stream, after_shrink, mapn, \
+                           grid, block, ExpandMmaCfg<RPV>::kSmemBytes + tb, stream, after_shrink, 0, mapn, \
                            map1, args),                                                            \
              "launch sgmv_expand_mma_kernel");
     if (R == 16) {
@@ -428,6 +513,10 @@ const char* plora_status_string(int status) {
 }
 
 const char* plora_last_error(void) { return g_last_error.c_str(); }
+
+int64_t plora_weight_split_tokens_per_sm(int64_t value) {
+  return value >= 0 ? g_wsplit_tokens_per_sm.exchange(value) : g_wsplit_tokens_per_sm.load();
+}
 
 int plora_device_status(int32_t* status_out, int32_t clear) {
   int v = 0;
@@ -501,8 +590,8 @@ int plora_sgmv_expand(const void* tmp, const void* lora_b, void* y, const int32_
   if (!tmp || !lora_b || !y || !lora_ranks || !scalings || !slot_start || !token_index)
     return fail(PLORA_ERR_INVALID_ARGUMENT, "null pointer");
   SegTable seg{slot_start, token_index, num_slots};
-  return expand_impl(tmp, lora_b, y, lora_ranks, scalings, seg, max_rank, out_features, dtype,
-                     static_cast<cudaStream_t>(stream));
+  return expand_impl(tmp, lora_b, y, lora_ranks, scalings, seg, num_tokens, max_rank, out_features,
+                     dtype, static_cast<cudaStream_t>(stream));
 }
 
 int plora_sgmv_shrink_expand(const void* x, const void* lora_a, void* tmp, const void* lora_b,
@@ -527,8 +616,8 @@ int plora_sgmv_shrink_expand(const void* x, const void* lora_a, void* tmp, const
   if ((st = shrink_impl(x, lora_a, tmp, lora_ranks, seg, num_tokens, in_features, max_rank, 1,
                         dtype, s)))
     return st;
-  return expand_impl(tmp, lora_b, y, lora_ranks, scalings, seg, max_rank, out_features, dtype, s,
-                     /*after_shrink=*/true);
+  return expand_impl(tmp, lora_b, y, lora_ranks, scalings, seg, num_tokens, max_rank, out_features,
+                     dtype, s, /*after_shrink=*/true);
 }
 
 int plora_sgmv_a_fwd(const void* x, const void* lora_a, void* tmp, const int32_t* seq_lens,

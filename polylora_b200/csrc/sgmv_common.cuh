@@ -3,10 +3,10 @@
 // list.
 //
 // The device segment table (slot_start / token_index, built by segments.cuh)
-// lists the active tokens grouped by slot; every kernel here takes a
-// contiguous share of that list and processes it in items: runs of at most
-// kItemTokens tokens of one slot, so that one slot's LoRA weights serve the
-// whole item.
+// lists the active tokens grouped by slot; the kernels process it in items:
+// runs of at most kItemTokens tokens of one slot, so that one slot's LoRA
+// weights serve the whole item.  The token-split kernels give each CTA a
+// contiguous range of tokens (TokenWork).
 #pragma once
 
 #include "common.cuh"
@@ -57,7 +57,7 @@ __device__ __forceinline__ SlotTab stage_slot_tab(const SegTable& t, const int32
   int32_t* ss = dst;
   int32_t* rk = dst + ns + 1;
   float* sc = reinterpret_cast<float*>(dst + 2 * ns + 1);
-  for (int i = threadIdx.x; i <= ns; i += blockDim.x) ss[i] = __ldg(t.slot_start + i);
+  for (int i = threadIdx.x; i <= ns; i += blockDim.x) ss[i] = ld_cg_i32(t.slot_start + i);
   for (int i = threadIdx.x; i < ns; i += blockDim.x) {
     rk[i] = __ldg(ranks + i);
     sc[i] = scales ? __ldg(scales + i) : 0.f;
@@ -84,6 +84,41 @@ struct SlotItems {
     start = p;
     p += cnt;
     return true;
+  }
+};
+
+// ------------------------------------------------------------------ work split
+// One piece of a CTA's work: tokens [start, start + cnt) of `slot`, weight
+// windows [w_lo, w_hi] (group: always 0 for the token split).
+struct Work {
+  int64_t start;
+  int slot, cnt, w_lo, w_hi, group;
+};
+
+// Token split (batches of many tokens): the CTA's contiguous share [b, e) of
+// the slot-ordered token list, cut into items; every item covers all `nwin`
+// weight windows of its slot.
+struct TokenWork {
+  SlotItems it;
+  int nwin;
+  __device__ void init(const SlotTab& t, int64_t b, int64_t e, int nw) {
+    it.init(t, b, e);
+    nwin = nw;
+  }
+  __device__ __forceinline__ bool next(const SlotTab& t, Work& w) {
+    int s, cnt;
+    int64_t start;
+    while (it.next(t, s, start, cnt))
+      if (t.rk[s] > 0) {
+        w.start = start;
+        w.slot = s;
+        w.cnt = cnt;
+        w.w_lo = 0;
+        w.w_hi = nwin - 1;
+        w.group = 0;
+        return true;
+      }
+    return false;
   }
 };
 

@@ -28,8 +28,10 @@ namespace plora {
 
 constexpr int kMmaWarps = 16;                      // compute warps
 constexpr int kMmaThreads = kMmaWarps * 32;
-constexpr int kWinBytes = 64 * 1024;               // one LoRA weight window
 constexpr int kWinBoxRows = 256;                   // rows per weight TMA box (8 blocks of 32)
+
+constexpr int kWinBufs = 2;           // LoRA weight windows in flight
+constexpr int kWinBytes = 64 * 1024;  // one LoRA weight window
 
 template <int RP>
 struct ShrinkMmaCfg {
@@ -41,7 +43,7 @@ struct ShrinkMmaCfg {
   static constexpr int kPartBytes = kMmaWarps * 16 * RP * 4;    // one 16 x RP fp32 tile per warp
   static constexpr int kBarrierBytes = 64;
   // + slot table (3 * num_slots + 1 ints), sized at launch
-  static constexpr int kSmemBytes = 1024 + 2 * kWinBytes + kPartBytes + kBarrierBytes;
+  static constexpr int kSmemBytes = 1024 + kWinBufs * kWinBytes + kPartBytes + kBarrierBytes;
 };
 
 // 4x4 transpose of 32-bit words across the four lanes of a quad: lane t
@@ -165,16 +167,16 @@ __device__ __noinline__ void issue_lora_a_window(const CUtensorMap* map8, const 
   for (; q < nb; ++q) tma_load_5d_outer(dst + q * block_bytes, map1, bar, blk0 + q);
 }
 
-// Sequence of (slot, window) pairs over the CTA's items with rank > 0, in the
-// order every warp consumes them.
+// Sequence of the weight windows of the CTA's work (slot, group, window), in
+// the order every warp consumes them.
+template <class WorkIt>
 struct WinCursor {
-  SlotItems it;
-  int slot, w, nwin;
+  WorkIt it;
+  int slot, group, w, w_hi;
   bool valid;
-  __device__ void init(const SlotTab& tab, int64_t b, int64_t e, int nw) {
-    it.init(tab, b, e);
-    nwin = nw;
-    slot = -1;
+  __device__ void init(const SlotTab& tab, const WorkIt& src) {
+    it = src;
+    w_hi = -1;
     w = 0;
     valid = true;
     advance(tab);
@@ -183,18 +185,21 @@ struct WinCursor {
   // carry one (measured faster in the shrink, slower in the expand)
   __device__ __noinline__ void advance_outlined(const SlotTab& tab) { advance(tab); }
   __device__ __forceinline__ void advance(const SlotTab& tab) {
-    if (slot >= 0 && ++w < nwin) return;
-    w = 0;
-    int s, cnt;
-    int64_t start;
-    while (it.next(tab, s, start, cnt))
-      if (tab.rk[s] > 0) {
-        slot = s;
-        return;
-      }
+    if (++w <= w_hi) return;
+    Work nx;
+    if (it.next(tab, nx)) {
+      slot = nx.slot;
+      group = nx.group;
+      w = nx.w_lo;
+      w_hi = nx.w_hi;
+      return;
+    }
     valid = false;
   }
 };
+
+// Bytes of the staged slot table (3 * ns + 1 ints, 16-byte aligned).
+__host__ __device__ constexpr int64_t slot_tab_bytes(int64_t ns) { return ((3 * ns + 1) * 4 + 15) & ~15ll; }
 
 // tmp[t, :] = x[t, :] @ A[slot(t)] for the active tokens of the table.
 // 16 warps; an item is 16-token tiles x K ranges, one pair per warp.  The
@@ -204,24 +209,26 @@ template <int RP, bool BF16>
 __global__ void __launch_bounds__(kMmaThreads, 1)
     sgmv_shrink_mma_kernel(const __grid_constant__ CUtensorMap tmap_a8,
                            const __grid_constant__ CUtensorMap tmap_a1, const ShrinkArgs args) {
+  using WorkIt = TokenWork;
   using Cfg = ShrinkMmaCfg<RP>;
   using E = Elem<BF16>;
   constexpr int W = Cfg::kWinRows;
+  constexpr int NB = kWinBufs;
   constexpr int U = Cfg::kU;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  float* part = reinterpret_cast<float*>(smem + 2 * kWinBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kWinBytes + Cfg::kPartBytes);
-  uint32_t* released = reinterpret_cast<uint32_t*>(full + 2);  // per buffer, monotonic
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(released + 2);
+  float* part = reinterpret_cast<float*>(smem + NB * kWinBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NB * kWinBytes + Cfg::kPartBytes);
+  uint32_t* released = reinterpret_cast<uint32_t*>(full + NB);  // per buffer, monotonic
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(released + NB);
   int32_t* tab_mem =
-      reinterpret_cast<int32_t*>(smem + 2 * kWinBytes + Cfg::kPartBytes + Cfg::kBarrierBytes);
+      reinterpret_cast<int32_t*>(smem + NB * kWinBytes + Cfg::kPartBytes + Cfg::kBarrierBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   griddep_wait();    // inputs (segment table, x) come from earlier kernels
   griddep_launch();  // the expand may start on SMs this grid releases
-  const int64_t total = __ldg(args.seg.slot_start + args.seg.num_slots);
+  const int64_t total = ld_cg_i32(args.seg.slot_start + args.seg.num_slots);
   const int64_t begin = total * blockIdx.x / gridDim.x;
   const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
   if (begin >= end) return;  // uniform across the CTA
@@ -230,42 +237,44 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   const int K = args.K;
   const int nwin = (K + W - 1) / W;
   const int kblocks = K >> 5;  // 32-row blocks per slot
-  auto issue = [&](const WinCursor& wc, int b) {  // one thread
+  auto issue = [&](const WinCursor<WorkIt>& wc, int b) {  // one thread
     issue_lora_a_window(&tmap_a8, &tmap_a1, &full[b], smem_u32(smem + b * kWinBytes),
                         min(W, K - wc.w * W) >> 5, wc.slot * kblocks + wc.w * (W >> 5), 32 * RP * 2);
   };
   __syncthreads();  // slot table staged
-  WinCursor ic;     // the window this warp would issue after its next release
-  ic.init(tab, begin, end, nwin);
+  WorkIt work;
+  work.init(tab, begin, end, nwin);
+  WinCursor<WorkIt> ic;  // the window this warp would issue after its next release
+  ic.init(tab, work);
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) mbar_init(&full[i], 1);
-    released[0] = released[1] = 0;
+    for (int i = 0; i < NB; ++i) {
+      mbar_init(&full[i], 1);
+      released[i] = 0;
+    }
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&tmap_a8);
     prefetch_tmap(&tmap_a1);
-    for (int b = 0; b < 2 && ic.valid; ++b) {
+    for (int b = 0; b < NB && ic.valid; ++b) {
       issue(ic, b);
       ic.advance_outlined(tab);
     }
   } else {
-    ic.advance(tab);
-    ic.advance(tab);
+    for (int b = 0; b < NB; ++b) ic.advance(tab);
   }
   __syncthreads();
 
-  SlotItems items;
-  items.init(tab, begin, end);
-  int s, cnt;
-  int64_t start;
   const int g = lane >> 2;  // fragment row group
   const int t = lane & 3;   // lane within the quad
   const uint32_t win_base = smem_u32(smem);
   uint32_t c_base = 0;  // window counter at the start of the item
   bool ok = true;
-  while (items.next(tab, s, start, cnt)) {
+  Work wk;
+  while (work.next(tab, wk)) {
+    const int s = wk.slot;
+    const int64_t start = wk.start;
+    const int cnt = wk.cnt;
     const int rank = tab.rk[s];
-    if (rank <= 0) continue;
     const int tiles = (cnt + 15) >> 4;
     const int KS = max(1, kMmaWarps / tiles);
     const bool active = warp < tiles * KS;
@@ -273,8 +282,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     const int ks = active ? warp - tile * KS : 0;
     const int r0 = tile * 16 + g;
     const bool v0 = active && r0 < cnt, v1 = active && r0 + 8 < cnt;
-    const uint8_t* x0 = args.x + (v0 ? (int64_t)__ldg(args.seg.token_index + start + r0) : 0) * K * 2;
-    const uint8_t* x1 = args.x + (v1 ? (int64_t)__ldg(args.seg.token_index + start + r0 + 8) : 0) * K * 2;
+    const uint8_t* x0 = args.x + (v0 ? (int64_t)ld_cg_i32(args.seg.token_index + start + r0) : 0) * K * 2;
+    const uint8_t* x1 = args.x + (v1 ? (int64_t)ld_cg_i32(args.seg.token_index + start + r0 + 8) : 0) * K * 2;
 
     // this warp's 32-column blocks of window w: [b0, b1); cursors over
     // (window, block) skip windows without blocks
@@ -326,7 +335,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     int cw = -1;  // window of this item the warp currently holds
     // releases the held window; the last of the 16 releasers refills its buffer
     auto release = [&]() {
-      const uint32_t b = (c_base + cw) & 1;
+      const uint32_t b = (c_base + cw) % NB;
       __syncwarp();
       if (lane == 0) {
         __threadfence_block();
@@ -343,7 +352,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         if (cw >= 0) release();
         ++cw;
         const uint32_t c = c_base + cw;
-        if (ok) ok = mbar_wait_warp(&full[c & 1], (c >> 1) & 1, abort_flag);
+        if (ok) ok = mbar_wait_warp(&full[c % NB], (c / NB) & 1, abort_flag);
       }
     };
     auto compute_batch = [&](Batch& B) {
@@ -354,7 +363,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         // B fragments of k16 step s: tokens g (x0) and 8 + g (x1), k = 8t + 4s + {0,1} / {2,3}
         const uint32_t fb0[2][2] = {{B.x0[u].x, B.x0[u].y}, {B.x0[u].z, B.x0[u].w}};
         const uint32_t fb1[2][2] = {{B.x1[u].x, B.x1[u].y}, {B.x1[u].z, B.x1[u].w}};
-        const uint32_t wb = win_base + ((c_base + mc.w) & 1) * kWinBytes;
+        const uint32_t wb = win_base + ((c_base + mc.w) % NB) * kWinBytes;
         const int mi = lane >> 3;
 #pragma unroll
         for (int st = 0; st < 2; ++st) {
@@ -426,7 +435,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         o[i] = (uint32_t)E::from_f(c0 < n_eff ? v[2 * i] : 0.f) |
                ((uint32_t)E::from_f(c0 + 1 < n_eff ? v[2 * i + 1] : 0.f) << 16);
       }
-      const int64_t tok = __ldg(args.seg.token_index + start + row);
+      const int64_t tok = ld_cg_i32(args.seg.token_index + start + row);
       *reinterpret_cast<uint4*>(args.tmp + (tok * args.R + cg * 8) * 2) = make_uint4(o[0], o[1], o[2], o[3]);
     }
     named_barrier(1, kMmaWarps * 32);
@@ -463,28 +472,30 @@ struct ExpandMmaCfg {
   static constexpr int kRegroupPitch = 64;
   static constexpr int kRegroupBytes = kMmaWarps * 16 * kRegroupPitch;
   // + slot table (3 * num_slots + 1 ints), sized at launch
-  static constexpr int kSmemBytes = 1024 + 2 * kWinBytes + kBarrierBytes + kRegroupBytes;
+  static constexpr int kSmemBytes = 1024 + kWinBufs * kWinBytes + kBarrierBytes + kRegroupBytes;
 };
 
 template <int RP, bool BF16>
 __global__ void __launch_bounds__(kMmaThreads, 1)
     sgmv_expand_mma_kernel(const __grid_constant__ CUtensorMap tmap_bn,
                            const __grid_constant__ CUtensorMap tmap_b1, const ExpandArgs args) {
+  using WorkIt = TokenWork;
   using Cfg = ExpandMmaCfg<RP>;
+  constexpr int NB = kWinBufs;
   using E = Elem<BF16>;
   constexpr int W = Cfg::kWinCols;
   constexpr int U = Cfg::kU;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kWinBytes);
-  uint32_t* released = reinterpret_cast<uint32_t*>(full + 2);  // per buffer, monotonic
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(released + 2);
-  uint8_t* regroup = smem + 2 * kWinBytes + Cfg::kBarrierBytes;  // per-warp 16 x 64 B delta tile
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NB * kWinBytes);
+  uint32_t* released = reinterpret_cast<uint32_t*>(full + NB);  // per buffer, monotonic
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(released + NB);
+  uint8_t* regroup = smem + NB * kWinBytes + Cfg::kBarrierBytes;  // per-warp 16 x 64 B delta tile
   int32_t* tab_mem = reinterpret_cast<int32_t*>(regroup + Cfg::kRegroupBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t total = __ldg(args.seg.slot_start + args.seg.num_slots);
+  const int64_t total = ld_cg_i32(args.seg.slot_start + args.seg.num_slots);
   const int64_t begin = total * blockIdx.x / gridDim.x;
   const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
   if (begin >= end) return;  // uniform across the CTA
@@ -492,8 +503,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   const SlotTab tab = stage_slot_tab(args.seg, args.ranks, args.scales, tab_mem);
   const int N = args.N;
   const int nwin = (N + W - 1) / W;
-  const int nchunks = N >> 6;  // 64-column chunks per row
-  auto issue = [&](const WinCursor& wc, int b) {  // one thread
+  auto issue = [&](const WinCursor<WorkIt>& wc, int b) {  // one thread
     const int nc = min(W, N - wc.w * W) >> 6;
     mbar_arrive_expect_tx(&full[b], nc * Cfg::kChunkBytes);
     const int ch0 = wc.w * (W >> 6);
@@ -501,41 +511,44 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     int q = 0;
     for (; q + Cfg::kBoxChunks <= nc; q += Cfg::kBoxChunks)
       tma_load_4d_outer(dst + q * Cfg::kChunkBytes, &tmap_bn, &full[b], ch0 + q, wc.slot);
-    for (; q < nc; ++q) tma_load_4d_outer(dst + q * Cfg::kChunkBytes, &tmap_b1, &full[b], ch0 + q, wc.slot);
+    for (; q < nc; ++q)
+      tma_load_4d_outer(dst + q * Cfg::kChunkBytes, &tmap_b1, &full[b], ch0 + q, wc.slot);
   };
-  (void)nchunks;
   __syncthreads();  // slot table staged
-  WinCursor ic;     // the window this warp would issue after its next release
-  ic.init(tab, begin, end, nwin);
+  WorkIt work;
+  work.init(tab, begin, end, nwin);
+  WinCursor<WorkIt> ic;  // the window this warp would issue after its next release
+  ic.init(tab, work);
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) mbar_init(&full[i], 1);
-    released[0] = released[1] = 0;
+    for (int i = 0; i < NB; ++i) {
+      mbar_init(&full[i], 1);
+      released[i] = 0;
+    }
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&tmap_bn);
     prefetch_tmap(&tmap_b1);
-    for (int b = 0; b < 2 && ic.valid; ++b) {
+    for (int b = 0; b < NB && ic.valid; ++b) {
       issue(ic, b);
       ic.advance(tab);
     }
   } else {
-    ic.advance(tab);
-    ic.advance(tab);
+    for (int b = 0; b < NB; ++b) ic.advance(tab);
   }
   __syncthreads();
 
-  SlotItems items;
-  items.init(tab, begin, end);
-  int s, cnt;
-  int64_t start;
   const int g = lane >> 2;  // fragment row group
   const int t = lane & 3;   // lane within the quad
   const uint32_t win_base = smem_u32(smem);
-  uint32_t c_base = 0;  // window counter at the start of the item
+  uint32_t c_base = 0;  // window counter at the start of the work
   bool ok = true;
-  while (items.next(tab, s, start, cnt)) {
+  Work wk;
+  while (work.next(tab, wk)) {
+    const int s = wk.slot;
+    const int64_t start = wk.start;
+    const int cnt = wk.cnt;
+    const int wlo = wk.w_lo, whi = wk.w_hi;  // this work's windows
     const int rank = tab.rk[s];
-    if (rank <= 0) continue;
     const float scale = tab.sc[s];
     const int tiles = (cnt + 15) >> 4;
     const int CS = max(1, kMmaWarps / tiles);
@@ -544,8 +557,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     const int cs = active ? warp - tile * CS : 0;
     const int r0 = tile * 16 + g;
     const bool v0 = active && r0 < cnt, v1 = active && r0 + 8 < cnt;
-    const int64_t tok0 = v0 ? (int64_t)__ldg(args.seg.token_index + start + r0) : 0;
-    const int64_t tok1 = v1 ? (int64_t)__ldg(args.seg.token_index + start + r0 + 8) : 0;
+    const int64_t tok0 = v0 ? (int64_t)ld_cg_i32(args.seg.token_index + start + r0) : 0;
+    const int64_t tok1 = v1 ? (int64_t)ld_cg_i32(args.seg.token_index + start + r0 + 8) : 0;
     uint8_t* y0 = args.y + tok0 * N * 2;
     uint8_t* y1 = args.y + tok1 * N * 2;
 
@@ -560,13 +573,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       c.end = active ? (cs + 1) * nb / CS : 0;
     };
     auto first = [&](Cur& c) {
-      c.w = 0;
+      c.w = wlo;
       range(c);
-      while (c.blk >= c.end && ++c.w < nwin) range(c);
+      while (c.blk >= c.end && ++c.w <= whi) range(c);
     };
     auto step = [&](Cur& c) {
       if (++c.blk >= c.end)
-        while (++c.w < nwin) {
+        while (++c.w <= whi) {
           range(c);
           if (c.blk < c.end) break;
         }
@@ -581,7 +594,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     auto load_batch = [&](Batch& B) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        if (lc.w < nwin) {
+        if (lc.w <= whi) {
           const int col = lc.w * W + lc.blk * 32 + 8 * t;
           B.y0[u] = v0 ? ld_stream16(y0 + col * 2) : make_uint4(0u, 0u, 0u, 0u);
           B.y1[u] = v1 ? ld_stream16(y1 + col * 2) : make_uint4(0u, 0u, 0u, 0u);
@@ -590,9 +603,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       }
     };
 
-    int cw = -1;  // window of this item the warp currently holds
+    int cw = wlo - 1;  // window of this work the warp currently holds
     auto release = [&]() {
-      const uint32_t b = (c_base + cw) & 1;
+      const uint32_t b = (c_base + cw - wlo) % NB;
       __syncwarp();
       if (lane == 0) {
         __threadfence_block();
@@ -605,10 +618,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     };
     auto hold = [&](int to) {
       while (cw < to) {
-        if (cw >= 0) release();
+        if (cw >= wlo) release();
         ++cw;
-        const uint32_t c = c_base + cw;
-        if (ok) ok = mbar_wait_warp(&full[c & 1], (c >> 1) & 1, abort_flag);
+        const uint32_t c = c_base + cw - wlo;
+        if (ok) ok = mbar_wait_warp(&full[c % NB], (c / NB) & 1, abort_flag);
       }
     };
     // y + delta for the 8 columns of a lane: words hold bf16/fp16 pairs
@@ -627,9 +640,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     auto compute_batch = [&](Batch& B) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        if (mc.w >= nwin) break;
+        if (mc.w > whi) break;
         hold(mc.w);
-        const uint32_t wb = win_base + ((c_base + mc.w) & 1) * kWinBytes;
+        const uint32_t wb = win_base + ((c_base + mc.w - wlo) % NB) * kWinBytes;
         const int cwin = mc.blk * 32;  // block column inside the window
         float acc[4][4];
 #pragma unroll
@@ -685,7 +698,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       const uint8_t* t1 = args.tmp + tok1 * args.R * 2;
       auto ld2 = [&](const uint8_t* row, bool v, int k) -> uint32_t {
         if (!v || k >= kr) return 0u;
-        const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(row + k * 2));
+        const uint32_t w = ld_cg_u32(row + k * 2);
         return k + 1 < kr ? w : (w & 0xFFFFu);
       };
 #pragma unroll
@@ -697,18 +710,18 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       }
     }
     for (;;) {
-      const bool more_b = lc.w < nwin;
+      const bool more_b = lc.w <= whi;
       if (more_b) load_batch(B);
       compute_batch(A);
       if (!more_b) break;
-      const bool more_a = lc.w < nwin;
+      const bool more_a = lc.w <= whi;
       if (more_a) load_batch(A);
       compute_batch(B);
       if (!more_a) break;
     }
-    hold(nwin - 1);  // windows without blocks of this warp are passed through
+    hold(whi);  // windows without blocks of this warp are passed through
     release();
-    c_base += nwin;
+    c_base += whi - wlo + 1;
   }
 }
 

@@ -32,6 +32,19 @@ def test_library_exports_every_declared_symbol(native):
     assert set(declared_functions()) <= set(native._SIGNATURES)
 
 
+def test_weight_split_threshold_round_trips(native):
+    """The work-split threshold is host state: set, read back, restored."""
+    prev = native.weight_split_tokens_per_sm(7)
+    try:
+        assert prev >= 0
+        assert native.weight_split_tokens_per_sm() == 7
+        assert native.weight_split_tokens_per_sm(0) == 7
+        assert native.weight_split_tokens_per_sm(-5) == 0  # negative: query only
+    finally:
+        native.weight_split_tokens_per_sm(prev)
+    assert native.weight_split_tokens_per_sm() == prev
+
+
 def test_version_and_status_strings(native):
     assert "sm_100a" in native.version()
     lib = native.load()

@@ -17,6 +17,17 @@ from polylora_b200.sgmv import (build_segments, sgmv_expand, sgmv_lora_a_fwd, sg
 pytestmark = pytest.mark.gpu
 
 TOL = {"bfloat16": 2e-2, "float16": 2e-2, "float32": 1e-5}
+
+
+@pytest.fixture(params=["token_split", "weight_split"])
+def split_mode(request):
+    """Runs the test under each work split of the tensor-core kernels: every
+    CTA a share of the tokens, or each slot's weights spread over the grid."""
+    from polylora_b200 import _native
+
+    prev = _native.weight_split_tokens_per_sm(0 if request.param == "token_split" else 1 << 40)
+    yield request.param
+    _native.weight_split_tokens_per_sm(prev)
 TORCH = {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}
 
 
@@ -102,7 +113,7 @@ TC_CASES = [
 
 
 @pytest.mark.parametrize("case", TC_CASES, ids=[f"tc{c[0]}" for c in TC_CASES])
-def test_tensor_core_path_matches_oracle(case, cuda_status_clean):
+def test_tensor_core_path_matches_oracle(case, split_mode, cuda_status_clean):
     seed, B, M, K, N, ns, R, rc, dt = case
     run_and_check(make_case(seed, B, M, K, N, ns, R, rc, dt))
 
@@ -123,13 +134,16 @@ def test_cuda_core_path_matches_oracle(case, cuda_status_clean):
     run_and_check(make_case(seed, B, M, K, N, ns, R, rc, dt))
 
 
-def test_stack_num_two(cuda_status_clean):
+def test_stack_num_two(split_mode, cuda_status_clean):
     c = make_case(30, 12, 4, 256, 128, 5, 32, [4, 8, 16], "bfloat16", stack_num=2)
     d = to_dev(c)
     tmp = sgmv_lora_a_fwd(d["x"], d["A"], d["seq"], d["wi"], d["ranks"], 2)
     ref_tmp, written = sgmv_ref.shrink(c["x"], c["A"], c["seq"], c["wi"], c["ranks"], 2, "bfloat16")
     got = tmp.float().cpu().numpy()
     assert sgmv_ref.rel_err(got[written], ref_tmp[written]) <= 2e-2
+    # columns beyond rank * stack_num of active tokens are written as zeros
+    pad = (~inactive_mask(c))[:, :, None] & ~written
+    assert np.all(got[pad] == 0)
 
 
 def test_all_base_rows_are_untouched(cuda_status_clean):
@@ -152,7 +166,7 @@ def test_empty_batch(cuda_status_clean):
 
 
 @pytest.mark.parametrize("case", ["cfg1_rows_f32", "tokens_f32", "odd_rank_f32", "rows_bf16", "tokens_bf16", "rank64_bf16"])
-def test_reference_golden_through_kernels(golden_dir, case, cuda_status_clean):
+def test_reference_golden_through_kernels(golden_dir, case, split_mode, cuda_status_clean):
     g = np.load(golden_dir / "reference_forward.npz")
     get = lambda k: g[f"{case}__{k}"]  # noqa: E731
     dt = str(get("dtype")[0])
@@ -185,7 +199,7 @@ def test_segment_table_reuse_across_modules(cuda_status_clean):
 
 
 @pytest.mark.parametrize("R,rc,dt", [(16, [0, 4, 8, 16], "bfloat16"), (64, [8, 64], "float16"), (32, [8, 32], "bfloat16")])
-def test_combined_entry_matches_separate_calls(R, rc, dt, cuda_status_clean):
+def test_combined_entry_matches_separate_calls(R, rc, dt, split_mode, cuda_status_clean):
     """plora_sgmv_shrink_expand (expand launched to overlap the shrink's end)
     gives bit-identical tmp and y to plora_sgmv_shrink + plora_sgmv_expand,
     repeated back to back on one stream."""
