@@ -144,6 +144,13 @@ __device__ __forceinline__ uint32_t ld_cg_u32(const void* p) {
   return v;
 }
 __device__ __forceinline__ int32_t ld_cg_i32(const int32_t* p) { return (int32_t)ld_cg_u32(p); }
+// The same ordering, cached in L1 as well: for data read by several warps of
+// the CTA after griddep_wait() (the previous grid has completed by then).
+__device__ __forceinline__ uint32_t ld_ca_u32(const void* p) {
+  uint32_t v;
+  asm volatile("ld.global.ca.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
 
 // 4-D tiled TMA load (box starting at (0, 0, c2, c3)), completing on `bar`.
 __device__ __forceinline__ void tma_load_4d_outer(uint32_t dst, const void* tmap, uint64_t* bar,

@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(kGridThreads, 2) sgmv_expand_grid_kernel(const
       const uint8_t* t1 = args.tmp + tok1 * R * 2;
       auto ld2 = [&](const uint8_t* row, bool v, int k) -> uint32_t {
         if (!v || k >= kr) return 0u;
-        const uint32_t w = ld_cg_u32(row + k * 2);
+        const uint32_t w = ld_ca_u32(row + k * 2);
         return k + 1 < kr ? w : (w & 0xFFFFu);
       };
 #pragma unroll
@@ -246,12 +246,13 @@ __global__ void __launch_bounds__(kGridThreads, 2)
     const uint8_t* x1 = args.x + (v1 ? (int64_t)ld_cg_i32(args.seg.token_index + a + g + 8) : 0) * K * 2;
     for (int bb = wb0; bb < wb1; bb += kGridRows / 32) {
       const int nbb = min(kGridRows / 32, wb1 - bb);
-      // rows [32 bb, 32 (bb + nbb)) of the part: row 8 m + 2 cc + e of a block at
-      // position 8 cc + 2 m + e, pieces swizzled as win_offset<RP>
+      // rows [32 bb, 32 (bb + nbb)) of the part: position 8 cc + 2 m + e of a block
+      // holds row 8 m + 2 cc + e, pieces swizzled as win_offset<RP>; consecutive
+      // lanes fill consecutive positions (conflict-free shared-memory writes)
       for (int q = lane; q < nbb * 32 * chunks; q += 32) {
-        const int row = q / chunks, j = q - row * chunks;
-        const int rb = row & 31;
-        const int pos = (row & ~31) + 8 * ((rb >> 1) & 3) + 2 * (rb >> 3) + (rb & 1);
+        const int pos = q / chunks, j = q - pos * chunks;
+        const int pb = pos & 31;
+        const int row = (pos & ~31) + 8 * ((pb >> 1) & 3) + 2 * (pb >> 3) + (pb & 1);
         cp_async16(stage + win_offset<RP>(pos, j), src + ((int64_t)(32 * bb + row) * R + 8 * j) * 2);
       }
       cp_async_commit();

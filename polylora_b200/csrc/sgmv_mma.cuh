@@ -698,7 +698,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       const uint8_t* t1 = args.tmp + tok1 * args.R * 2;
       auto ld2 = [&](const uint8_t* row, bool v, int k) -> uint32_t {
         if (!v || k >= kr) return 0u;
-        const uint32_t w = ld_cg_u32(row + k * 2);
+        const uint32_t w = ld_ca_u32(row + k * 2);
         return k + 1 < kr ? w : (w & 0xFFFFu);
       };
 #pragma unroll
