@@ -919,6 +919,184 @@ def run_model_cfg4(args):
         dist.destroy_process_group()
 
 
+# adapter churn on a DeBERTa-v3-small-shaped encoder (6
+# layers, hidden 768, 12 heads, FFN 3072; bf16, random init), LoRA on
+# query/key/value/dense.  A catalog of 1024 PEFT adapters (ranks {8, 16},
+# alpha 2r) sits on the disk tier, the CPU LRU holds 256 and the GPU 32 slots;
+# each batch is 128 rows x 256 tokens with adapter ids Zipf(0.9) over the
+# catalog, so slots are evicted and refilled (and CPU misses parsed from disk)
+# in every batch.  A batch carries ~88 distinct adapters, more than the 32
+# slots (the reference raises there), so each rank serves its rows as
+# micro-batches of <= 32 distinct adapters.
+CFG5_CATALOG, CFG5_SLOTS, CFG5_CPU, CFG5_ROWS, CFG5_SEQ = 1024, 32, 256, 128, 256
+
+
+def _deberta_v3_small():
+    from transformers import DebertaV2Config, DebertaV2Model
+
+    cfg = DebertaV2Config(
+        vocab_size=128100, hidden_size=768, num_hidden_layers=6, num_attention_heads=12,
+        intermediate_size=3072, max_position_embeddings=512, relative_attention=True,
+        position_buckets=256, norm_rel_ebd="layer_norm", share_att_key=True, pos_att_type=["p2c", "c2p"],
+        max_relative_positions=-1, position_biased_input=False, type_vocab_size=0, layer_norm_eps=1e-7,
+        hidden_dropout_prob=0.0, attention_probs_dropout_prob=0.0,
+    )
+    return DebertaV2Model(cfg).eval()
+
+
+def run_model_cfg5(args):
+    import torch
+    import torch.distributed as dist
+    from safetensors.torch import save_file
+
+    from polylora_b200 import PolyLoraConfig, PolyLoraModel
+    from polylora_b200.rowshard import RowParallel
+    from polylora_b200.store import _entry_dirname
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.manual_seed(0)
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(dev):
+        base = _deberta_v3_small()
+    torch.set_default_dtype(torch.float32)
+    shapes = {n: (m.in_features, m.out_features) for n, m in base.named_modules()
+              if isinstance(m, torch.nn.Linear) and any(n == t or n.endswith("." + t) for t in CFG3_TARGETS)}
+    disk_dir = Path(tempfile.mkdtemp(prefix=f"plora_cfg5_r{rank}_"))
+    model = PolyLoraModel(base, PolyLoraConfig(
+        max_gpu_adapters=CFG5_SLOTS, max_rank=16, target_modules=CFG3_TARGETS,
+        max_cpu_adapters=CFG5_CPU, disk_cache_dir=disk_dir))
+    assert set(shapes) == set(model.target_module_names), "target matching differs"
+    store = model.adapter_store
+    # catalog: PEFT directories written where the disk tier keeps them (no copy);
+    # adapters share random factors per shape (values do not change the timing)
+    g = torch.Generator().manual_seed(1)
+    src = {kn: ((torch.rand(16, kn[0], generator=g) * 2 - 1) / np.sqrt(kn[0]),
+                torch.randn(kn[1], 16, generator=g) * 0.02) for kn in set(shapes.values())}
+    rng = np.random.default_rng(5)
+    ranks = rng.choice([8, 16], size=CFG5_CATALOG)
+    t_setup = time.perf_counter()
+    for a in range(CFG5_CATALOG):
+        aid, r = f"adapter{a}", int(ranks[a])
+        path = disk_dir / _entry_dirname(aid)
+        path.mkdir(parents=True, exist_ok=True)
+        (path / "adapter_config.json").write_text(json.dumps(
+            {"peft_type": "LORA", "r": r, "lora_alpha": 2 * r, "lora_dropout": 0.0,
+             "target_modules": CFG3_TARGETS}))
+        sd = {}
+        for name, kn in shapes.items():
+            sd[f"base_model.model.{name}.lora_A.weight"] = src[kn][0][:r].to(torch.bfloat16).contiguous()
+            sd[f"base_model.model.{name}.lora_B.weight"] = src[kn][1][:, :r].to(torch.bfloat16).contiguous()
+        save_file(sd, str(path / "adapter_model.safetensors"))
+        store.disk_cache.add_adapter(aid, path)
+    t_setup = time.perf_counter() - t_setup
+    disk_loads = [0]
+    load_from_disk = store._load_adapter_from_disk_cache
+
+    def counting_load(aid):
+        disk_loads[0] += 1
+        return load_from_disk(aid)
+
+    store._load_adapter_from_disk_cache = counting_load
+    pop = 1.0 / np.arange(1, CFG5_CATALOG + 1) ** 0.9
+    pop /= pop.sum()
+
+    def make_batch():
+        ids = [f"adapter{int(i)}" for i in rng.choice(CFG5_CATALOG, size=CFG5_ROWS, p=pop)]
+        input_ids = torch.randint(0, 128100, (CFG5_ROWS, CFG5_SEQ), generator=g).to(dev)
+        return ids, input_ids
+
+    micro_batches = [0]
+
+    def serve(adapter_ids, input_ids):
+        """This rank's rows as micro-batches of <= 32 distinct adapters (in order of first use)."""
+        out = torch.empty(input_ids.shape + (768,), device=dev, dtype=torch.bfloat16)
+        order = list(dict.fromkeys(adapter_ids))
+        for i in range(0, len(order), CFG5_SLOTS):
+            group = set(order[i:i + CFG5_SLOTS])
+            rows = [j for j, a in enumerate(adapter_ids) if a in group]
+            idx = torch.tensor(rows, device=dev)
+            res = model(input_ids=input_ids.index_select(0, idx), adapter_ids=[adapter_ids[j] for j in rows])
+            out.index_copy_(0, idx, res.last_hidden_state)
+            micro_batches[0] += 1
+        return out
+
+    lora_fn = RowParallel(lambda adapter_ids, input_ids: serve(adapter_ids, input_ids), row_cost=lambda n: 1)
+
+    def step(ids, x):
+        return lora_fn(ids, input_ids=x)
+    batches = [make_batch() for _ in range(max(args.warmup, 3) + args.steps)]
+    cache = model.adapter_cache
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    gpu_ids = [v for v in visible.split(",") if v.strip().isdigit()]
+    sampler = ClockSampler(int(gpu_ids[local]) if local < len(gpu_ids) else local)
+    with torch.inference_mode():
+        for ids, x in batches[: max(args.warmup, 3)]:
+            step(ids, x)
+        torch.cuda.synchronize()
+        barrier()
+        stats0, loads0, mb0 = dict(cache.stats), disk_loads[0], micro_batches[0]
+        sampler.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for ids, x in batches[max(args.warmup, 3):]:
+            step(ids, x)
+        e1.record()
+        e1.synchronize()
+        clocks = sampler.stop()
+        barrier()
+        ms = e0.elapsed_time(e1) / args.steps
+        # the same batches through the base model alone
+        torch.cuda.synchronize()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record()
+        for ids, x in batches[max(args.warmup, 3):]:
+            n = x.shape[0]
+            lo, hi = n * rank // world, n * (rank + 1) // world
+            base(input_ids=x[lo:hi])
+        b1.record()
+        b1.synchronize()
+        ms_base = b0.elapsed_time(b1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms, ms_base], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_base = float(t[0]), float(t[1])
+    delta = {k: cache.stats[k] - stats0[k] for k in cache.stats}
+    shutil.rmtree(disk_dir, ignore_errors=True)
+    if rank == 0:
+        tokens = CFG5_ROWS * CFG5_SEQ
+        line = {
+            "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {
+                "workload": "BASELINE config 5: adapter churn, DeBERTa-v3-small-shaped encoder (6 layers, hidden "
+                            "768, 12 heads, FFN 3072), bf16, random init; LoRA on query/key/value/dense (36 "
+                            "Linears); 1024-adapter PEFT catalog (ranks {8,16}) on the disk tier, CPU LRU 256, "
+                            "32 GPU slots; batches 128 x 256 tokens, adapter ids Zipf(0.9); one batch per step "
+                            "(rank 0's stats), rows sharded over the GPUs, micro-batches of <= 32 distinct adapters",
+            },
+            "per_step_rank0": {
+                "micro_batches": (micro_batches[0] - mb0) / args.steps,
+                "gpu_slot_misses": delta["misses"] / args.steps, "gpu_slot_hits": delta["hits"] / args.steps,
+                "evictions": delta["evictions"] / args.steps,
+                "refill_h2d_MB": delta["h2d_bytes"] / args.steps / 1e6,
+                "disk_loads": (disk_loads[0] - loads0) / args.steps,
+            },
+            "catalog_setup_s": t_setup,
+            "base_model_ms_per_step": ms_base, "lora_overhead_frac": ms / ms_base - 1.0,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -926,7 +1104,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["cfg2", "cfg2-sweep", "cfg3", "cfg4", "cfg4-decode", "cfg4-ops"],
+    ap.add_argument("--workload", choices=["cfg2", "cfg2-sweep", "cfg3", "cfg4", "cfg4-decode", "cfg4-ops", "cfg5"],
                     default="cfg2",
                     help="cfg2: the SGMV op step (default, the headline line); cfg3: model forward")
     ap.add_argument("--linear", default=None, help="cfg4-ops: only this Linear (e.g. gate_proj)")
@@ -937,12 +1115,14 @@ def main():
         run_sweep(args)
     elif args.workload == "cfg4-ops" and args.impl != "reference":
         run_cfg4_ops(args)
-    elif args.workload in ("cfg3", "cfg4", "cfg4-decode"):
+    elif args.workload in ("cfg3", "cfg4", "cfg4-decode", "cfg5"):
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": f"{args.workload} is timed for this library "
                               "only; the reference arm covers the config-2 op"}), flush=True)
         elif args.workload == "cfg3":
             run_model_cfg3(args)
+        elif args.workload == "cfg5":
+            run_model_cfg5(args)
         else:
             run_model_cfg4(args)
     elif args.impl == "reference":

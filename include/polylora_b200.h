@@ -192,7 +192,9 @@ int plora_sgmv_shrink_expand(const void* x, const void* lora_a, void* tmp, const
  *   staging      device buffer of at least image_bytes
  * Image layout: num_modules records of plora_slot_record, then the data
  * blocks they point at (byte offsets from the image start):
- *   A block (in_features x rank) row-major, B block (rank x out_features).
+ *   A block (rank x in_features) row-major and B block (out_features x rank)
+ *   row-major: the factors as PEFT stores them (lora_A.weight, lora_B.weight);
+ *   the fill writes them transposed into the slot layouts.
  * ------------------------------------------------------------------------- */
 typedef struct plora_slot_module {
   void* lora_a;     /* (num_slots, in_features, max_rank) */

@@ -119,8 +119,11 @@ __global__ void __launch_bounds__(kSimtThreads) sgmv_expand_simt_kernel(const Ex
 }
 
 // Slot refill: every module's slot region rewritten from the staged adapter
-// image (zero padding past the adapter's rank, rank/scale scalars).  Mirrors
-// src/polylora/cache.py:108-115 (zero on evict) and 119-150 (load).
+// image (zero padding past the adapter's rank, rank/scale scalars).  The image
+// holds each module's factors as PEFT stores them (A rank x in, B out x rank),
+// so the host does no transposes; this kernel writes them transposed into the
+// slot layouts (K x R, R x N).  Mirrors src/polylora/cache.py:108-115 (zero on
+// evict) and 119-150 (load, which transposes on the host).
 template <typename T>
 __global__ void __launch_bounds__(256) slot_fill_kernel(const plora_slot_module* __restrict__ mods,
                                                          int32_t num_modules, int32_t slot,
@@ -142,11 +145,11 @@ __global__ void __launch_bounds__(256) slot_fill_kernel(const plora_slot_module*
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nA + nB; i += stride) {
     if (i < nA) {
       const int64_t k = i / R, j = i - k * R;
-      A[i] = (j < r) ? srcA[k * r + j] : zero;
+      A[i] = (j < r) ? srcA[j * K + k] : zero;
     } else {
       const int64_t i2 = i - nA;
-      const int64_t j = i2 / N;
-      B[i2] = (j < r) ? srcB[i2] : zero;
+      const int64_t j = i2 / N, n = i2 - j * N;
+      B[i2] = (j < r) ? srcB[n * r + j] : zero;
     }
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) {

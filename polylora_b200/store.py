@@ -72,6 +72,7 @@ class DiskAdapterCache:
         self.max_adapters = max_adapters
         self.cache_dir.mkdir(parents=True, exist_ok=True)
         self.entries: OrderedDict[str, DiskAdapterEntry] = OrderedDict()
+        self._json_blocks: dict[str, str] = {}  # adapter_id -> its manifest entry, serialised
         self._load_manifest()
         self._evict_if_needed()
 
@@ -102,6 +103,7 @@ class DiskAdapterCache:
                 shutil.rmtree(target)
             shutil.copytree(source, target)
         self.entries[adapter_id] = DiskAdapterEntry(adapter_id, target, peft_adapter_name)
+        self._json_blocks.pop(adapter_id, None)
         self.entries.move_to_end(adapter_id)
         self._evict_if_needed(exclude={adapter_id})
         self._write_manifest()
@@ -119,15 +121,25 @@ class DiskAdapterCache:
                     adapter_id, path, str(item.get("peft_adapter_name", "default"))
                 )
 
+    def _json_block(self, e: DiskAdapterEntry) -> str:
+        block = self._json_blocks.get(e.adapter_id)
+        if block is None:
+            fields = {"adapter_id": e.adapter_id, "path": e.path.name, "peft_adapter_name": e.peft_adapter_name}
+            body = ",\n".join(f"      {json.dumps(k)}: {json.dumps(fields[k])}" for k in sorted(fields))
+            block = "    {\n" + body + "\n    }"
+            self._json_blocks[e.adapter_id] = block
+        return block
+
     def _write_manifest(self) -> None:
-        payload = {
-            "adapters": [
-                {"adapter_id": e.adapter_id, "path": e.path.name, "peft_adapter_name": e.peft_adapter_name}
-                for e in self.entries.values()
-            ]
-        }
-        with self.manifest_path.open("w", encoding="utf-8") as handle:
-            json.dump(payload, handle, indent=2, sort_keys=True)
+        """The LRU order, written on every change as the reference does
+        (store.py:60-63, 101-114): the bytes of ``json.dump(..., indent=2,
+        sort_keys=True)``, assembled from cached per-entry blocks so that a
+        touch of a large catalog costs a string join, not a re-serialisation."""
+        if self.entries:
+            text = '{\n  "adapters": [\n' + ",\n".join(self._json_block(e) for e in self.entries.values()) + "\n  ]\n}"
+        else:
+            text = '{\n  "adapters": []\n}'
+        self.manifest_path.write_text(text, encoding="utf-8")
 
     def _evict_if_needed(self, exclude: set[str] | None = None) -> None:
         if self.max_adapters is None:
@@ -139,6 +151,7 @@ class DiskAdapterCache:
             if victim is None:
                 raise RuntimeError("No evictable disk LoRA adapter is available")
             entry = self.entries.pop(victim)
+            self._json_blocks.pop(victim, None)
             if entry.path.exists():
                 shutil.rmtree(entry.path)
             evicted = True
@@ -155,16 +168,6 @@ def _validate_adapter_dir(adapter_path: Path) -> None:
         raise FileNotFoundError(f"PEFT adapter config not found: {config}")
     if not (adapter_path / "adapter_model.safetensors").exists() and not (adapter_path / "adapter_model.bin").exists():
         raise FileNotFoundError(f"No PEFT adapter weights found in {adapter_path}")
-
-
-def _pin_if_possible(tensor: torch.Tensor) -> torch.Tensor:
-    """Page-locks host tensors when a CUDA device exists (store.py:151-157)."""
-    if torch.cuda.is_available():
-        try:
-            return tensor.pin_memory()
-        except RuntimeError:
-            return tensor
-    return tensor
 
 
 def _matches_module_name(module_name: str, allowed: list[str]) -> bool:
@@ -187,6 +190,31 @@ def _state_dict_lora_module_names(state_dict: dict[str, torch.Tensor]) -> set[st
 def _find_lora_key(state_dict: dict[str, torch.Tensor], module_name: str, side: str, peft_adapter_name: str) -> str | None:
     suffixes = (f"{module_name}.{side}.{peft_adapter_name}.weight", f"{module_name}.{side}.weight")
     return next((k for k in state_dict if k.endswith(suffixes)), None)
+
+
+def _lora_key_index(state_dict: dict[str, torch.Tensor], module_names: list[str],
+                    peft_adapter_name: str) -> dict[tuple[str, str], str]:
+    """(module, side) -> the key :func:`_find_lora_key` returns, in one pass.
+
+    A key ``<prefix>.<side>[.<name>].weight`` matches every module whose name is
+    a string suffix of ``<prefix>``; each key is filed under all such module
+    names, and the first key in ``state_dict`` order wins, as in the scan."""
+    wanted = set(module_names)
+    index: dict[tuple[str, str], str] = {}
+    for key in state_dict:
+        for side in ("lora_A", "lora_B"):
+            prefix = None
+            for suffix in (f".{side}.{peft_adapter_name}.weight", f".{side}.weight"):
+                if key.endswith(suffix):
+                    prefix = key[: -len(suffix)]
+                    break
+            if prefix is None:
+                continue
+            for i in range(len(prefix)):
+                tail = prefix[i:]
+                if tail in wanted and (tail, side) not in index:
+                    index[(tail, side)] = key
+    return index
 
 
 class CpuAdapterStore:
@@ -267,10 +295,11 @@ class CpuAdapterStore:
         config: dict[str, Any] | None = None,
     ) -> None:
         self._validate_lora_keys_within_modules(adapter_id, state_dict, module_names)
+        index = _lora_key_index(state_dict, module_names, peft_adapter_name)
         layers: dict[str, CpuLayerWeights] = {}
         for module_name in module_names:
-            key_a = _find_lora_key(state_dict, module_name, "lora_A", peft_adapter_name)
-            key_b = _find_lora_key(state_dict, module_name, "lora_B", peft_adapter_name)
+            key_a = index.get((module_name, "lora_A"))
+            key_b = index.get((module_name, "lora_B"))
             if key_a is None and key_b is None:
                 continue  # module absent: a rank-0 no-op for this adapter
             if key_a is None or key_b is None:
@@ -282,9 +311,11 @@ class CpuAdapterStore:
                 raise ValueError(f"Adapter {adapter_id!r} has non-positive rank for {module_name!r}")
             if int(lora_b.shape[1]) != rank:
                 raise ValueError(f"LoRA A/B rank mismatch for adapter {adapter_id!r}, module {module_name!r}")
+            # (in, r) and (r, out) as transposed views: the one copy is the packed slot
+            # image (slot_image), the only thing sent to the GPU, which is pinned
             layers[module_name] = CpuLayerWeights(
-                A=_pin_if_possible(lora_a.t().contiguous()),
-                B=_pin_if_possible(lora_b.t().contiguous()),
+                A=lora_a.t(),
+                B=lora_b.t(),
                 rank=rank,
                 scale=float(lora_alpha) / rank,
             )
@@ -413,8 +444,10 @@ class CpuAdapterStore:
         """Packed pinned image of an adapter for ``plora_slot_fill``.
 
         Layout: one ``plora_slot_record`` per module in ``module_names`` order
-        (absent modules have rank 0), then the A (in, r) and B (r, out) blocks
-        in ``dtype``, each 256-byte aligned.  Returns the uint8 image and the
+        (absent modules have rank 0), then the A block (r, in) and the B block
+        (out, r) in ``dtype`` -- the factors as PEFT stores them, so that an
+        adapter loaded from PEFT needs no transposes on the host (the fill
+        kernel transposes) -- each 256-byte aligned.  Returns the uint8 image and the
         per-module ranks.  Cached until the adapter leaves this tier.
         """
         key = (adapter_id, dtype, tuple(module_names))
@@ -432,23 +465,22 @@ class CpuAdapterStore:
             if w is None:
                 ranks.append(0)
                 continue
-            a = w.A.to(dtype).contiguous()
-            b = w.B.to(dtype).contiguous()
+            a_t, b_t = w.A.t(), w.B.t()  # (r, in), (out, r): contiguous for PEFT-loaded adapters
             records[i].a_offset = offset
-            blocks.append((offset, a))
-            offset = _align(offset + a.numel() * esize)
+            blocks.append((offset, a_t))
+            offset = _align(offset + a_t.numel() * esize)
             records[i].b_offset = offset
-            blocks.append((offset, b))
-            offset = _align(offset + b.numel() * esize)
+            blocks.append((offset, b_t))
+            offset = _align(offset + b_t.numel() * esize)
             records[i].rank = int(w.rank)
             records[i].scale = float(w.scale)
             ranks.append(int(w.rank))
-        image = torch.zeros(offset, dtype=torch.uint8)
+        # page-locked from the start when a CUDA device exists (torch's pinned block cache)
+        image = torch.zeros(offset, dtype=torch.uint8, pin_memory=torch.cuda.is_available())
         header = bytes(records)
         image[: len(header)] = torch.frombuffer(bytearray(header), dtype=torch.uint8)
-        for off, t in blocks:
-            image[off : off + t.numel() * esize] = t.reshape(-1).view(torch.uint8)
-        image = _pin_if_possible(image)
+        for off, t in blocks:  # one converting copy per block
+            image[off : off + t.numel() * esize].view(dtype).view(t.shape).copy_(t)
         self._images[key] = (image, ranks)
         return image, ranks
 

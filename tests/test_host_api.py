@@ -90,6 +90,25 @@ def test_disk_manifest_matches_reference_bytes(tmp_path, golden_dir):
     assert list(again.entries) == ["gamma", "b/eta"]
 
 
+def test_manifest_bytes_equal_json_dump_for_any_ids(tmp_path):
+    """The manifest is assembled from cached per-entry blocks; its bytes must be
+    those of json.dump(indent=2, sort_keys=True) of the LRU order, whatever the
+    ids hold (quotes, backslashes, non-ASCII) and after touches and evictions."""
+    cache = DiskAdapterCache(tmp_path / "cache", max_adapters=4)
+    ids = ['plain', 'qu"ote', "back\\slash", "ünïcode/ß", "tab\tid", "x" * 40]
+    for i, a in enumerate(ids):
+        cache.add_adapter(a, _adapter_dir(tmp_path / f"src{i}"), "default" if i % 2 else "named")
+        if i >= 2:
+            cache.get(ids[1]) if ids[1] in cache else None
+
+        payload = {"adapters": [{"adapter_id": e.adapter_id, "path": e.path.name,
+                                 "peft_adapter_name": e.peft_adapter_name} for e in cache.entries.values()]}
+        assert cache.manifest_path.read_text(encoding="utf-8") == json.dumps(payload, indent=2, sort_keys=True)
+    empty = DiskAdapterCache(tmp_path / "empty")
+    empty._write_manifest()
+    assert empty.manifest_path.read_text() == json.dumps({"adapters": []}, indent=2, sort_keys=True)
+
+
 def test_disk_cache_evicts_oldest_directory(tmp_path):
     cache = DiskAdapterCache(tmp_path / "c", max_adapters=2)
     srcs = {a: _adapter_dir(tmp_path / f"s_{a}") for a in "abc"}
@@ -178,6 +197,23 @@ def test_rank_above_max_rank_is_rejected():
     assert cache.slot_to_adapter[1] is None
 
 
+def test_lora_key_index_matches_the_scan():
+    """The one-pass key index returns what the per-module suffix scan returns,
+    including modules that are string suffixes of others and named adapters."""
+    from polylora_b200.store import _find_lora_key, _lora_key_index
+
+    mods = ["layer.1.dense", "encoder.layer.1.dense", "layer.11.dense", "q", "attn.q", "missing"]
+    keys = ["base_model.model.encoder.layer.11.dense.lora_A.weight", "base_model.model.encoder.layer.1.dense.lora_A.weight",
+            "base_model.model.encoder.layer.1.dense.lora_B.default.weight", "x.attn.q.lora_A.other.weight",
+            "x.attn.q.lora_A.weight", "x.attn.q.lora_B.weight", "encoder.layer.11.dense.lora_B.weight", "unrelated.weight"]
+    sd = {k: torch.zeros(1) for k in keys}
+    for name in ("default", "other"):
+        index = _lora_key_index(sd, mods, name)
+        for m in mods:
+            for side in ("lora_A", "lora_B"):
+                assert index.get((m, side)) == _find_lora_key(sd, m, side, name), (name, m, side)
+
+
 def test_slot_image_layout():
     from polylora_b200._native import SlotRecord
 
@@ -189,9 +225,10 @@ def test_slot_image_layout():
     assert ranks == [0, 2]
     recs = (SlotRecord * 2).from_buffer_copy(image[:48].numpy().tobytes())
     assert recs[0].rank == 0 and recs[1].rank == 2 and recs[1].scale == 0.5
-    got_a = image[recs[1].a_offset: recs[1].a_offset + 24].view(torch.bfloat16).float().reshape(6, 2)
-    got_b = image[recs[1].b_offset: recs[1].b_offset + 20].view(torch.bfloat16).float().reshape(2, 5)
-    assert torch.equal(got_a, a) and torch.equal(got_b, b)
+    # blocks as PEFT stores them: A (r, in), B (out, r)
+    got_a = image[recs[1].a_offset: recs[1].a_offset + 24].view(torch.bfloat16).float().reshape(2, 6)
+    got_b = image[recs[1].b_offset: recs[1].b_offset + 20].view(torch.bfloat16).float().reshape(5, 2)
+    assert torch.equal(got_a, a.t()) and torch.equal(got_b, b.t())
     assert recs[1].a_offset % 256 == 0 and recs[1].b_offset % 256 == 0
 
 
