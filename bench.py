@@ -1025,7 +1025,8 @@ def run_model_cfg5(args):
 
     def step(ids, x):
         return lora_fn(ids, input_ids=x)
-    batches = [make_batch() for _ in range(max(args.warmup, 3) + args.steps)]
+    nw = max(args.warmup, 3)
+    batches = [make_batch() for _ in range(2 * (nw + args.steps))]
     cache = model.adapter_cache
 
     def barrier():
@@ -1035,27 +1036,42 @@ def run_model_cfg5(args):
     visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
     gpu_ids = [v for v in visible.split(",") if v.strip().isdigit()]
     sampler = ClockSampler(int(gpu_ids[local]) if local < len(gpu_ids) else local)
-    with torch.inference_mode():
-        for ids, x in batches[: max(args.warmup, 3)]:
+    def run_pass(seq, prefetch):
+        """Warm-up then timed batches; with `prefetch`, each step first queues the
+        next batch's adapters for the CPU tier's prefetch thread (this rank's rows)."""
+        def my_ids(ids):
+            lo, hi = len(ids) * rank // world, len(ids) * (rank + 1) // world
+            return ids[lo:hi]
+
+        for i, (ids, x) in enumerate(seq[:nw]):
+            if prefetch and i + 1 < len(seq):
+                model.prefetch(my_ids(seq[i + 1][0]))
             step(ids, x)
         torch.cuda.synchronize()
         barrier()
-        stats0, loads0, mb0 = dict(cache.stats), disk_loads[0], micro_batches[0]
-        sampler.start()
+        st0, ld0, mbs0 = dict(cache.stats), disk_loads[0], micro_batches[0]
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for ids, x in batches[max(args.warmup, 3):]:
+        for i, (ids, x) in enumerate(seq[nw:], start=nw):
+            if prefetch and i + 1 < len(seq):
+                model.prefetch(my_ids(seq[i + 1][0]))
             step(ids, x)
         e1.record()
         e1.synchronize()
-        clocks = sampler.stop()
+        store.wait_prefetches()
         barrier()
-        ms = e0.elapsed_time(e1) / args.steps
+        return e0.elapsed_time(e1) / args.steps, st0, ld0, mbs0
+
+    with torch.inference_mode():
+        ms_nopf, _, _, _ = run_pass(batches[: nw + args.steps], prefetch=False)
+        sampler.start()
+        ms, stats0, loads0, mb0 = run_pass(batches[nw + args.steps:], prefetch=True)
+        clocks = sampler.stop()
         # the same batches through the base model alone
         torch.cuda.synchronize()
         b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         b0.record()
-        for ids, x in batches[max(args.warmup, 3):]:
+        for ids, x in batches[-args.steps:]:
             n = x.shape[0]
             lo, hi = n * rank // world, n * (rank + 1) // world
             base(input_ids=x[lo:hi])
@@ -1063,9 +1079,9 @@ def run_model_cfg5(args):
         b1.synchronize()
         ms_base = b0.elapsed_time(b1) / args.steps
     if world > 1:
-        t = torch.tensor([ms, ms_base], device=dev, dtype=torch.float64)
+        t = torch.tensor([ms, ms_base, ms_nopf], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, ms_base = float(t[0]), float(t[1])
+        ms, ms_base, ms_nopf = float(t[0]), float(t[1]), float(t[2])
     delta = {k: cache.stats[k] - stats0[k] for k in cache.stats}
     shutil.rmtree(disk_dir, ignore_errors=True)
     if rank == 0:
@@ -1079,8 +1095,11 @@ def run_model_cfg5(args):
                             "768, 12 heads, FFN 3072), bf16, random init; LoRA on query/key/value/dense (36 "
                             "Linears); 1024-adapter PEFT catalog (ranks {8,16}) on the disk tier, CPU LRU 256, "
                             "32 GPU slots; batches 128 x 256 tokens, adapter ids Zipf(0.9); one batch per step "
-                            "(rank 0's stats), rows sharded over the GPUs, micro-batches of <= 32 distinct adapters",
+                            "(rank 0's stats), rows sharded over the GPUs, micro-batches of <= 32 distinct adapters; "
+                            "value with the next batch's adapters prefetched from disk on the CPU tier's thread",
             },
+            "ms_per_step_without_prefetch": ms_nopf,
+            "tokens_per_s_without_prefetch": CFG5_ROWS * CFG5_SEQ / (ms_nopf * 1e-3),
             "per_step_rank0": {
                 "micro_batches": (micro_batches[0] - mb0) / args.steps,
                 "gpu_slot_misses": delta["misses"] / args.steps, "gpu_slot_hits": delta["hits"] / args.steps,

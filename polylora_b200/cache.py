@@ -19,6 +19,8 @@ absent modules set to 0), which covers the reference's zero-on-evict.
 
 from __future__ import annotations
 
+import contextlib
+
 from collections import OrderedDict
 from dataclasses import dataclass
 
@@ -64,6 +66,7 @@ class GpuAdapterCache:
         self._slot_last_use: dict[int, torch.cuda.Event] = {}
         self.ready_event: torch.cuda.Event | None = None
         self._allocate(self.device, self.dtype)
+        self._publish_image_spec()
 
     # ------------------------------------------------------------------ storage
     def _allocate(self, device: torch.device, dtype: torch.dtype, src: "GpuAdapterCache | None" = None) -> None:
@@ -116,9 +119,17 @@ class GpuAdapterCache:
         self._allocate(device, dtype, src=self)
         self.device = device
         self.dtype = dtype
+        self._publish_image_spec()
         self._staging = None
         self._slot_last_use.clear()
         self.ready_event = None
+
+    def _publish_image_spec(self) -> None:
+        """Tells the CPU tier the layout of this cache's slot images (CUDA only)."""
+        setter = getattr(self.store, "set_image_spec", None)
+        if setter is not None:
+            cuda = self.device.type == "cuda"
+            setter(self.module_names if cuda else None, self.dtype if cuda else None)
 
     # ------------------------------------------------------------------ slot policy
     def ensure_resident(self, adapter_ids: list[str]) -> torch.Tensor:
@@ -171,20 +182,25 @@ class GpuAdapterCache:
                 raise ValueError(f"LoRA B shape mismatch for adapter {adapter_id!r}, module {name!r}")
 
     def _load_adapter_into_slot(self, adapter_id: str, slot: int) -> None:
-        adapter = self.store.get(adapter_id)
-        try:
-            self._validate(adapter_id, adapter)
-        except ValueError:
-            self._clear_slot(slot)
-            raise
-        if self.device.type == "cuda":
-            self._fill_slot_native(adapter_id, slot)
-        else:
-            self._fill_slot_host(adapter, slot)
-        self.adapter_to_slot[adapter_id] = slot
-        self.slot_to_adapter[slot] = adapter_id
-        self._touch(adapter_id)
-        self._sync_cpu_eviction_exclusions()
+        # one critical section against the CPU tier's prefetch workers: the
+        # adapter stays in the tier and its image's slab is not reused until
+        # the copy reading it has been recorded (note_image_use)
+        lock = getattr(self.store, "locked", None)
+        with lock() if lock is not None else contextlib.nullcontext():
+            adapter = self.store.get(adapter_id)
+            try:
+                self._validate(adapter_id, adapter)
+            except ValueError:
+                self._clear_slot(slot)
+                raise
+            if self.device.type == "cuda":
+                self._fill_slot_native(adapter_id, slot)
+            else:
+                self._fill_slot_host(adapter, slot)
+            self.adapter_to_slot[adapter_id] = slot
+            self.slot_to_adapter[slot] = adapter_id
+            self._touch(adapter_id)
+            self._sync_cpu_eviction_exclusions()
 
     def _touch(self, adapter_id: str) -> None:
         if adapter_id == self.config.base_adapter_id:
@@ -227,6 +243,7 @@ class GpuAdapterCache:
         event.record(stream)
         self.ready_event = event
         self.stats["h2d_bytes"] += nbytes
+        self.store.note_image_use(adapter_id, self.module_names, self.dtype, event)
         self._inflight = [(e, t) for e, t in self._inflight if not e.query()]
         self._inflight.append((event, image))
 

@@ -24,6 +24,9 @@ class PolyLoraConfig:
     base_adapter_id: str = "__base__"
     enforce_right_padding: bool = True
     use_triton_kernels: bool = True
+    # threads of the CPU tier's disk prefetch (PolyLoraModel.prefetch); None: 1.
+    # No counterpart in the reference.
+    prefetch_workers: int | None = None
 
     def __post_init__(self) -> None:
         checks = (

@@ -40,6 +40,7 @@ class PolyLoraModel(nn.Module):
             config.max_cpu_adapters,
             disk_cache=disk_cache,
             module_names=self.target_module_names,
+            prefetch_workers=config.prefetch_workers,
         )
         self.adapter_store.set_module_names(self.target_module_names)
         device, dtype = self._infer_device_dtype(base_model)
@@ -49,6 +50,14 @@ class PolyLoraModel(nn.Module):
     @property
     def target_module_names(self) -> list[str]:
         return [spec.name for spec in self.module_specs]
+
+    def prefetch(self, adapter_ids: list[str]):
+        """Starts loading, on worker threads, the adapters of a queued batch that
+        are only on the disk tier, with their slot images in this model's cache
+        dtype, so that the batch's forward finds them in the CPU tier.  Returns
+        the futures of the loads started.  No counterpart in the reference."""
+        cache = self.adapter_cache
+        return self.adapter_store.prefetch(adapter_ids, image_dtype=cache.dtype, module_names=cache.module_names)
 
     def add_adapter_from_peft_model(self, adapter_id: str, peft_model: nn.Module, peft_adapter_name: str | None = None) -> None:
         self.adapter_store.add_adapter_from_peft_model(

@@ -7,20 +7,25 @@ API-compatible with the reference's ``src/polylora/store.py``:
   ``{"adapters": [{"adapter_id", "path", "peft_adapter_name"}]}`` written with
   ``indent=2, sort_keys=True``, same directory naming) so existing caches load.
 * :class:`CpuAdapterStore` — store.py:160-436.  LRU of per-module
-  ``(A^T, B^T, rank, alpha/rank)`` in pinned memory, PEFT validation with the
-  same exception types and messages, eviction that skips GPU-resident
-  adapters.
+  ``(A^T, B^T, rank, alpha/rank)``, PEFT validation with the same exception
+  types and messages, eviction that skips GPU-resident adapters.
 
 Added for the GPU tier: :meth:`CpuAdapterStore.slot_image` packs every module
 of an adapter into one pinned buffer laid out for ``plora_slot_fill`` so a
-GPU slot refill is a single host-to-device copy plus one scatter kernel.
+GPU slot refill is a single host-to-device copy plus one scatter kernel (the
+per-module tensors themselves stay in pageable memory).
+:meth:`CpuAdapterStore.prefetch` parses disk adapters and builds their images
+on worker threads ahead of use (prefetch from queued batches); the LRU and the
+disk tier are guarded by one lock.
 """
 
 from __future__ import annotations
 
 import json
 import shutil
+import threading
 from collections import OrderedDict
+from concurrent.futures import Future, ThreadPoolExecutor
 from dataclasses import dataclass
 from hashlib import sha256
 from pathlib import Path
@@ -217,6 +222,45 @@ def _lora_key_index(state_dict: dict[str, torch.Tensor], module_names: list[str]
     return index
 
 
+class PinnedSlabPool:
+    """Page-locked slabs of one size for slot images.
+
+    One large pinned arena is carved into slabs, so that building an image
+    costs no page-locking call.  A released slab is reused only once the GPU
+    copy that last read it (:meth:`note_use`) has completed."""
+
+    def __init__(self, slab_bytes: int, slabs_per_arena: int = 32) -> None:
+        self.slab_bytes = slab_bytes
+        self.slabs_per_arena = slabs_per_arena
+        self.arenas: list[torch.Tensor] = []
+        self.free: list[torch.Tensor] = []
+        self.retired: list[tuple[torch.Tensor, Any]] = []  # (slab, event of its last copy)
+        self.last_use: dict[int, Any] = {}                 # slab data_ptr -> event
+
+    def acquire(self) -> torch.Tensor:
+        if not self.free and self.retired:
+            still = []
+            for slab, ev in self.retired:
+                (self.free.append(slab) if ev.query() else still.append((slab, ev)))
+            self.retired = still
+        if not self.free:
+            arena = torch.empty(self.slabs_per_arena * self.slab_bytes, dtype=torch.uint8, pin_memory=True)
+            self.arenas.append(arena)
+            self.free.extend(arena[i * self.slab_bytes:(i + 1) * self.slab_bytes]
+                             for i in range(self.slabs_per_arena))
+        return self.free.pop()
+
+    def note_use(self, slab: torch.Tensor, event: Any) -> None:
+        self.last_use[slab.data_ptr()] = event
+
+    def release(self, slab: torch.Tensor) -> None:
+        ev = self.last_use.pop(slab.data_ptr(), None)
+        if ev is None or ev.query():
+            self.free.append(slab)
+        else:
+            self.retired.append((slab, ev))
+
+
 class CpuAdapterStore:
     """LRU of adapters in host memory, refilled from the disk tier on a miss."""
 
@@ -226,6 +270,7 @@ class CpuAdapterStore:
         max_adapters: int | None = None,
         disk_cache: DiskAdapterCache | None = None,
         module_names: list[str] | None = None,
+        prefetch_workers: int | None = None,
     ) -> None:
         if max_adapters is not None and max_adapters < 1:
             raise ValueError("max_adapters must be at least 1")
@@ -236,6 +281,18 @@ class CpuAdapterStore:
         self.adapters: OrderedDict[str, CpuAdapter] = OrderedDict()
         self.eviction_exclusions: set[str] = set()
         self._images: dict[tuple, tuple[torch.Tensor, list]] = {}
+        self._slabs: dict[tuple, tuple[PinnedSlabPool, torch.Tensor]] = {}  # image key -> its slab
+        self._pools: dict[int, PinnedSlabPool] = {}  # slab size class -> pool
+        # (module_names, dtype) of the GPU cache's slot images, set by the cache:
+        # disk loads then place safetensors bytes straight into the image
+        self._image_spec: tuple[tuple[str, ...], torch.dtype] | None = None
+        # guards adapters / _images / _loading / the disk tier (reentrant: get -> load -> add)
+        self._lock = threading.RLock()
+        self._loading: dict[str, Future] = {}  # adapter id -> in-flight prefetch
+        # one worker by default: parsing holds the GIL for most of its time, so the
+        # gain is overlap with the serving thread, not parallel parsing
+        self.prefetch_workers = prefetch_workers or 1
+        self._pool: ThreadPoolExecutor | None = None
 
     # ------------------------------------------------------------------ LRU
     def __contains__(self, adapter_id: str) -> bool:
@@ -246,19 +303,114 @@ class CpuAdapterStore:
     def get(self, adapter_id: str) -> CpuAdapter:
         if adapter_id == self.base_adapter_id:
             raise KeyError(f"Base adapter {adapter_id!r} has no LoRA weights")
-        if adapter_id not in self.adapters:
-            if self.disk_cache is None or adapter_id not in self.disk_cache:
-                raise KeyError(f"Unknown LoRA adapter id: {adapter_id}")
-            self._load_adapter_from_disk_cache(adapter_id)
-        self.touch(adapter_id)
-        return self.adapters[adapter_id]
+        pending = self._loading.get(adapter_id)
+        if pending is not None and not self._lock._is_owned():
+            # a prefetch is loading it: wait (its error is raised here).  A caller
+            # holding the lock must not wait (the worker needs the lock to insert):
+            # it loads synchronously below and the worker discards its copy.
+            pending.result()
+        with self._lock:
+            if adapter_id not in self.adapters:
+                if self.disk_cache is None or adapter_id not in self.disk_cache:
+                    raise KeyError(f"Unknown LoRA adapter id: {adapter_id}")
+                self._load_adapter_from_disk_cache(adapter_id)
+            self.touch(adapter_id)
+            return self.adapters[adapter_id]
 
     def touch(self, adapter_id: str) -> None:
-        if adapter_id in self.adapters:
-            self.adapters.move_to_end(adapter_id)
+        with self._lock:
+            if adapter_id in self.adapters:
+                self.adapters.move_to_end(adapter_id)
 
     def set_eviction_exclusions(self, adapter_ids: set[str]) -> None:
-        self.eviction_exclusions = {a for a in adapter_ids if a != self.base_adapter_id}
+        with self._lock:
+            self.eviction_exclusions = {a for a in adapter_ids if a != self.base_adapter_id}
+
+    def set_image_spec(self, module_names: list[str] | None, dtype: torch.dtype | None) -> None:
+        """Module order and dtype of the GPU cache's slot images (None: no GPU
+        cache).  With a spec, an adapter read from a safetensors file whose LoRA
+        tensors already have that dtype is loaded by copying the file's bytes
+        into its slot image, the per-module weights being views of the image."""
+        with self._lock:
+            self._image_spec = (tuple(module_names), dtype) if module_names is not None and dtype is not None else None
+
+    def locked(self):
+        """The tier's lock, for a caller that must keep an adapter (and its
+        image's slab) in place across several calls, e.g. a GPU slot refill
+        while prefetch workers insert and evict."""
+        return self._lock
+
+    # ------------------------------------------------------------------ prefetch
+    def wait_prefetches(self) -> None:
+        """Waits for every prefetch started so far (errors are left to get())."""
+        for fut in list(self._loading.values()):
+            try:
+                fut.result()
+            except Exception:  # noqa: BLE001 - surfaced again by get()
+                pass
+
+    def prefetch(self, adapter_ids, image_dtype: torch.dtype | None = None,
+                 module_names: list[str] | None = None) -> list[Future]:
+        """Starts loading the listed adapters that are only on the disk tier.
+
+        Worker threads parse each adapter (and, with ``image_dtype``, build its
+        pinned slot image for ``module_names``) and insert it into the LRU, so
+        that a later :meth:`get` / :meth:`slot_image` finds it resident; a
+        :meth:`get` of an adapter still loading waits for it.  Returns the
+        futures of the loads started (errors surface there and in :meth:`get`).
+        No counterpart in the reference, which loads on first use."""
+        started: list[Future] = []
+        with self._lock:
+            for aid in dict.fromkeys(adapter_ids):
+                if (aid == self.base_adapter_id or aid in self.adapters or aid in self._loading
+                        or self.disk_cache is None or aid not in self.disk_cache):
+                    continue
+                if self._pool is None:
+                    self._pool = ThreadPoolExecutor(self.prefetch_workers, thread_name_prefix="plora-prefetch")
+                fut = self._pool.submit(self._prefetch_one, aid, image_dtype, module_names)
+                self._loading[aid] = fut
+                started.append(fut)
+        return started
+
+    def _prefetch_one(self, adapter_id: str, image_dtype: torch.dtype | None,
+                      module_names: list[str] | None) -> None:
+        try:
+            with self._lock:
+                if adapter_id in self.adapters:
+                    return
+                if self.module_names is None:
+                    raise RuntimeError("module_names must be configured before loading adapters from disk cache")
+                entry = self.disk_cache.get(adapter_id)
+                names = list(self.module_names)
+            fast = self._load_direct(adapter_id, Path(entry.path), names, entry.peft_adapter_name)
+            if fast is not None:
+                with self._lock:
+                    if adapter_id not in self.adapters:  # a synchronous load may have won the race
+                        self._insert_loaded(adapter_id, *fast)
+                    elif fast[3] is not None:
+                        fast[3][0].release(fast[3][1])
+                return
+            config, state_dict = self._read_peft_dir(Path(entry.path))  # outside the lock: file I/O, parsing
+            layers = self._layers_from_peft_state_dict(adapter_id, state_dict, names, float(config["lora_alpha"]),
+                                                       entry.peft_adapter_name)
+            adapter = CpuAdapter(adapter_id, config, layers)
+            image = slab = None
+            if image_dtype is not None and module_names is not None:
+                slab = self._acquire_slab(_slot_image_bytes(adapter, module_names, image_dtype))
+                image = _build_slot_image(adapter, module_names, image_dtype, slab)
+            with self._lock:
+                if adapter_id not in self.adapters:  # a synchronous load may have won the race
+                    self.add_adapter(adapter_id, layers, config)
+                    if image is not None:
+                        key = (adapter_id, image_dtype, tuple(module_names))
+                        self._images[key] = image
+                        if slab is not None:
+                            self._slabs[key] = slab
+                elif slab is not None:
+                    slab[0].release(slab[1])
+        finally:
+            with self._lock:
+                self._loading.pop(adapter_id, None)
 
     def set_module_names(self, module_names: list[str]) -> None:
         self.module_names = list(module_names)
@@ -268,10 +420,11 @@ class CpuAdapterStore:
             raise ValueError(f"{self.base_adapter_id!r} is reserved for base-only rows")
         if not layers:
             raise ValueError("Adapter must contain at least one target layer")
-        self._drop_images(adapter_id)
-        self.adapters[adapter_id] = CpuAdapter(adapter_id, config or {}, layers)
-        self.adapters.move_to_end(adapter_id)
-        self._evict_if_needed(exclude={adapter_id})
+        with self._lock:
+            self._drop_images(adapter_id)
+            self.adapters[adapter_id] = CpuAdapter(adapter_id, config or {}, layers)
+            self.adapters.move_to_end(adapter_id)
+            self._evict_if_needed(exclude={adapter_id})
 
     def _evict_if_needed(self, exclude: set[str] | None = None) -> None:
         if self.max_adapters is None:
@@ -294,8 +447,23 @@ class CpuAdapterStore:
         peft_adapter_name: str = "default",
         config: dict[str, Any] | None = None,
     ) -> None:
+        layers = self._layers_from_peft_state_dict(adapter_id, state_dict, module_names, lora_alpha, peft_adapter_name)
+        self.add_adapter(adapter_id, layers, config)
+
+    def _layers_from_peft_state_dict(
+        self,
+        adapter_id: str,
+        state_dict: dict[str, torch.Tensor],
+        module_names: list[str],
+        lora_alpha: float,
+        peft_adapter_name: str = "default",
+        index: dict[tuple[str, str], str] | None = None,
+    ) -> dict[str, CpuLayerWeights]:
+        """Per-module weights of a PEFT state dict (store.py:260-291); no state
+        changes.  ``index``: the state dict's :func:`_lora_key_index`, if built."""
         self._validate_lora_keys_within_modules(adapter_id, state_dict, module_names)
-        index = _lora_key_index(state_dict, module_names, peft_adapter_name)
+        if index is None:
+            index = _lora_key_index(state_dict, module_names, peft_adapter_name)
         layers: dict[str, CpuLayerWeights] = {}
         for module_name in module_names:
             key_a = index.get((module_name, "lora_A"))
@@ -319,7 +487,7 @@ class CpuAdapterStore:
                 rank=rank,
                 scale=float(lora_alpha) / rank,
             )
-        self.add_adapter(adapter_id, layers, config)
+        return layers
 
     def add_adapter_from_peft_model(
         self,
@@ -349,9 +517,10 @@ class CpuAdapterStore:
         module_names: list[str],
         peft_adapter_name: str = "default",
     ) -> None:
-        if self.disk_cache is not None:
-            adapter_path = self.disk_cache.add_adapter(adapter_id, adapter_path, peft_adapter_name)
-        self._load_adapter_from_disk_path(adapter_id, adapter_path, module_names, peft_adapter_name)
+        with self._lock:
+            if self.disk_cache is not None:
+                adapter_path = self.disk_cache.add_adapter(adapter_id, adapter_path, peft_adapter_name)
+            self._load_adapter_from_disk_path(adapter_id, adapter_path, module_names, peft_adapter_name)
 
     def _load_adapter_from_disk_cache(self, adapter_id: str) -> None:
         if self.disk_cache is None:
@@ -359,7 +528,82 @@ class CpuAdapterStore:
         if self.module_names is None:
             raise RuntimeError("module_names must be configured before loading adapters from disk cache")
         entry = self.disk_cache.get(adapter_id)
+        fast = self._load_direct(adapter_id, Path(entry.path), list(self.module_names), entry.peft_adapter_name)
+        if fast is not None:
+            self._insert_loaded(adapter_id, *fast)
+            return
         self._load_adapter_from_disk_path(adapter_id, entry.path, self.module_names, entry.peft_adapter_name)
+
+    def _insert_loaded(self, adapter_id, config, layers, image, slab, key) -> None:
+        with self._lock:
+            self.add_adapter(adapter_id, layers, config)
+            self._images[key] = image
+            if slab is not None:
+                self._slabs[key] = slab
+
+    def _load_direct(self, adapter_id: str, path: Path, names: list[str], peft_adapter_name: str):
+        """Loads an adapter by placing its safetensors bytes in its slot image.
+
+        Applies when the GPU cache's image spec is set, matches ``names`` and
+        the file's LoRA tensors are of the image dtype; returns None otherwise
+        (the caller takes the general path).  Validation and errors are those
+        of the general path: the per-module weights are built by
+        :meth:`_layers_from_peft_state_dict` from views of the filled image."""
+        spec = self._image_spec
+        st_path = path / "adapter_model.safetensors"
+        if spec is None or tuple(names) != spec[0] or not st_path.exists():
+            return None
+        dtype = spec[1]
+        code = {torch.bfloat16: "BF16", torch.float16: "F16", torch.float32: "F32"}.get(dtype)
+        config, _ = self._read_peft_dir_config(path)
+        header, data = _read_safetensors(st_path)
+        keys = dict.fromkeys(header)
+        index = _lora_key_index(keys, names, peft_adapter_name)
+        used = set(index.values())
+        if code is None or any(header[k].get("dtype") != code for k in used):
+            return None
+        esize = torch.empty((), dtype=dtype).element_size()
+        records = (SlotRecord * len(names))()
+        places: list[tuple[str, int]] = []  # (key, image offset)
+        offset = _align(len(names) * _ctypes_sizeof(SlotRecord))
+        alpha = float(config["lora_alpha"])
+        for i, name in enumerate(names):
+            ka, kb = index.get((name, "lora_A")), index.get((name, "lora_B"))
+            if ka is None or kb is None or len(header[ka]["shape"]) != 2 or len(header[kb]["shape"]) != 2:
+                continue  # absent, or malformed: left to the general checks below
+            ra = int(header[ka]["shape"][0])
+            records[i].a_offset = offset
+            places.append((ka, offset))
+            offset = _align(offset + _numel(header[ka]["shape"]) * esize)
+            records[i].b_offset = offset
+            places.append((kb, offset))
+            offset = _align(offset + _numel(header[kb]["shape"]) * esize)
+            records[i].rank = ra
+            records[i].scale = alpha / ra if ra > 0 else 0.0
+        slab = self._acquire_slab(offset)
+        image = slab[1][:offset] if slab is not None else torch.zeros(offset, dtype=torch.uint8)
+        try:
+            image.zero_()
+            raw = image.numpy()
+            header_bytes = bytes(records)
+            raw[: len(header_bytes)] = memoryview(header_bytes)
+            views: dict[str, Any] = dict.fromkeys(header)
+            for key, off in places:
+                b0, b1 = header[key]["data_offsets"]
+                raw[off : off + (b1 - b0)] = data[b0:b1]
+                views[key] = image[off : off + (b1 - b0)].view(dtype).view(*header[key]["shape"])
+            for key in used:  # malformed entries: the general checks see their real shapes
+                if views[key] is None:
+                    b0, b1 = header[key]["data_offsets"]
+                    views[key] = torch.frombuffer(bytearray(data[b0:b1]), dtype=dtype).view(*header[key]["shape"])
+            layers = self._layers_from_peft_state_dict(adapter_id, views, names, alpha, peft_adapter_name, index)
+            ranks = [records[i].rank for i in range(len(names))]
+        except BaseException:
+            if slab is not None:
+                slab[0].release(slab[1])
+            raise
+        key = (adapter_id, dtype, tuple(names))
+        return config, layers, (image, ranks), slab, key
 
     def _load_adapter_from_disk_path(
         self,
@@ -368,20 +612,28 @@ class CpuAdapterStore:
         module_names: list[str],
         peft_adapter_name: str = "default",
     ) -> None:
-        adapter_path = Path(adapter_path)
-        config_path = adapter_path / "adapter_config.json"
-        if not config_path.exists():
-            raise FileNotFoundError(f"PEFT adapter config not found: {config_path}")
-        config = json.loads(config_path.read_text(encoding="utf-8"))
-        self._validate_peft_config_dict(config)
+        config, state_dict = self._read_peft_dir(Path(adapter_path))
         self.add_adapter_from_peft_state_dict(
             adapter_id=adapter_id,
-            state_dict=self._load_peft_state_dict(adapter_path),
+            state_dict=state_dict,
             module_names=module_names,
             lora_alpha=float(config["lora_alpha"]),
             peft_adapter_name=peft_adapter_name,
             config=config,
         )
+
+    def _read_peft_dir(self, adapter_path: Path) -> tuple[dict[str, Any], dict[str, torch.Tensor]]:
+        """Validated adapter_config.json and the weights of a PEFT directory."""
+        config, _ = self._read_peft_dir_config(adapter_path)
+        return config, self._load_peft_state_dict(adapter_path)
+
+    def _read_peft_dir_config(self, adapter_path: Path) -> tuple[dict[str, Any], None]:
+        config_path = adapter_path / "adapter_config.json"
+        if not config_path.exists():
+            raise FileNotFoundError(f"PEFT adapter config not found: {config_path}")
+        config = json.loads(config_path.read_text(encoding="utf-8"))
+        self._validate_peft_config_dict(config)
+        return config, None
 
     _find_lora_key = staticmethod(_find_lora_key)
     _state_dict_lora_module_names = staticmethod(_state_dict_lora_module_names)
@@ -447,46 +699,114 @@ class CpuAdapterStore:
         (absent modules have rank 0), then the A block (r, in) and the B block
         (out, r) in ``dtype`` -- the factors as PEFT stores them, so that an
         adapter loaded from PEFT needs no transposes on the host (the fill
-        kernel transposes) -- each 256-byte aligned.  Returns the uint8 image and the
-        per-module ranks.  Cached until the adapter leaves this tier.
+        kernel transposes) -- each 256-byte aligned.  Returns the uint8 image
+        and the per-module ranks.  Cached until the adapter leaves this tier.
         """
         key = (adapter_id, dtype, tuple(module_names))
-        cached = self._images.get(key)
-        if cached is not None:
+        with self._lock:
+            cached = self._images.get(key)
+            if cached is None:
+                adapter = self.adapters[adapter_id]
+                slab = self._acquire_slab(_slot_image_bytes(adapter, module_names, dtype))
+                cached = _build_slot_image(adapter, module_names, dtype, slab)
+                self._images[key] = cached
+                if slab is not None:
+                    self._slabs[key] = slab
             return cached
-        adapter = self.adapters[adapter_id]
-        esize = torch.empty((), dtype=dtype).element_size()
-        records = (SlotRecord * len(module_names))()
-        blocks: list[tuple[int, torch.Tensor]] = []
-        offset = _align(len(module_names) * _ctypes_sizeof(SlotRecord))
-        ranks: list[int] = []
-        for i, name in enumerate(module_names):
-            w = adapter.layers.get(name)
-            if w is None:
-                ranks.append(0)
-                continue
-            a_t, b_t = w.A.t(), w.B.t()  # (r, in), (out, r): contiguous for PEFT-loaded adapters
-            records[i].a_offset = offset
-            blocks.append((offset, a_t))
-            offset = _align(offset + a_t.numel() * esize)
-            records[i].b_offset = offset
-            blocks.append((offset, b_t))
-            offset = _align(offset + b_t.numel() * esize)
-            records[i].rank = int(w.rank)
-            records[i].scale = float(w.scale)
-            ranks.append(int(w.rank))
-        # page-locked from the start when a CUDA device exists (torch's pinned block cache)
-        image = torch.zeros(offset, dtype=torch.uint8, pin_memory=torch.cuda.is_available())
-        header = bytes(records)
-        image[: len(header)] = torch.frombuffer(bytearray(header), dtype=torch.uint8)
-        for off, t in blocks:  # one converting copy per block
-            image[off : off + t.numel() * esize].view(dtype).view(t.shape).copy_(t)
-        self._images[key] = (image, ranks)
-        return image, ranks
+
+    def note_image_use(self, adapter_id: str, module_names: list[str], dtype: torch.dtype, event: Any) -> None:
+        """Records the event of a GPU copy that reads this image: its slab is not
+        reused (after the adapter leaves the tier) before the event completes."""
+        with self._lock:
+            slab = self._slabs.get((adapter_id, dtype, tuple(module_names)))
+            if slab is not None:
+                slab[0].note_use(slab[1], event)
+
+    def _acquire_slab(self, nbytes: int) -> tuple[PinnedSlabPool, torch.Tensor] | None:
+        """A pinned slab of at least ``nbytes`` (None without a CUDA device)."""
+        if not torch.cuda.is_available():
+            return None
+        size = _align(nbytes, 1 << 18)  # 256 KB size classes
+        with self._lock:
+            pool = self._pools.get(size)
+            if pool is None:
+                pool = self._pools[size] = PinnedSlabPool(size)
+            return pool, pool.acquire()
 
     def _drop_images(self, adapter_id: str) -> None:
         for key in [k for k in self._images if k[0] == adapter_id]:
             del self._images[key]
+            slab = self._slabs.pop(key, None)
+            if slab is not None:
+                slab[0].release(slab[1])
+
+
+def _slot_image_bytes(adapter: CpuAdapter, module_names: list[str], dtype: torch.dtype) -> int:
+    esize = torch.empty((), dtype=dtype).element_size()
+    offset = _align(len(module_names) * _ctypes_sizeof(SlotRecord))
+    for name in module_names:
+        w = adapter.layers.get(name)
+        if w is not None:
+            offset = _align(offset + w.A.numel() * esize)
+            offset = _align(offset + w.B.numel() * esize)
+    return offset
+
+
+def _build_slot_image(adapter: CpuAdapter, module_names: list[str], dtype: torch.dtype,
+                      slab: tuple[PinnedSlabPool, torch.Tensor] | None = None) -> tuple[torch.Tensor, list]:
+    """The packed image of :meth:`CpuAdapterStore.slot_image`, in ``slab`` (a
+    pinned pool slab) when given; no state changes."""
+    esize = torch.empty((), dtype=dtype).element_size()
+    records = (SlotRecord * len(module_names))()
+    blocks: list[tuple[int, torch.Tensor]] = []
+    offset = _align(len(module_names) * _ctypes_sizeof(SlotRecord))
+    ranks: list[int] = []
+    for i, name in enumerate(module_names):
+        w = adapter.layers.get(name)
+        if w is None:
+            ranks.append(0)
+            continue
+        a_t, b_t = w.A.t(), w.B.t()  # (r, in), (out, r): contiguous for PEFT-loaded adapters
+        records[i].a_offset = offset
+        blocks.append((offset, a_t))
+        offset = _align(offset + a_t.numel() * esize)
+        records[i].b_offset = offset
+        blocks.append((offset, b_t))
+        offset = _align(offset + b_t.numel() * esize)
+        records[i].rank = int(w.rank)
+        records[i].scale = float(w.scale)
+        ranks.append(int(w.rank))
+    if slab is not None:
+        image = slab[1][:offset]
+        image.zero_()
+    else:
+        image = torch.zeros(offset, dtype=torch.uint8)
+    header = bytes(records)
+    image[: len(header)] = torch.frombuffer(bytearray(header), dtype=torch.uint8)
+    for off, t in blocks:  # one converting copy per block
+        image[off : off + t.numel() * esize].view(dtype).view(t.shape).copy_(t)
+    return image, ranks
+
+
+def _numel(shape) -> int:
+    n = 1
+    for d in shape:
+        n *= int(d)
+    return n
+
+
+def _read_safetensors(path: Path):
+    """The JSON header (without ``__metadata__``) and the data section of a
+    safetensors file (8-byte little-endian header length, header, data)."""
+    import numpy as np
+
+    with open(path, "rb") as f:
+        n = int.from_bytes(f.read(8), "little")
+        header = json.loads(f.read(n))
+    # mapped, not read: each tensor's bytes are copied once, into the slot image
+    data = np.memmap(path, dtype=np.uint8, mode="r", offset=8 + n)
+    header.pop("__metadata__", None)
+    return header, data
 
 
 def _align(n: int, a: int = 256) -> int:

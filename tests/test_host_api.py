@@ -243,3 +243,175 @@ def test_context_var_and_right_padding():
     with pytest.raises(ValueError, match="right-padded"):
         bad = torch.tensor([[0, 1, 1]])
         assert_right_padded(bad, bad.sum(-1))
+
+
+# ---------------------------------------------------------------- prefetch (CPU tier)
+def _peft_dir(path: Path, mods, r, seed):
+    from safetensors.torch import save_file
+
+    g = torch.Generator().manual_seed(seed)
+    path.mkdir(parents=True)
+    (path / "adapter_config.json").write_text(json.dumps({"peft_type": "LORA", "lora_alpha": 2 * r, "r": r}))
+    sd = {}
+    for m, (k, n) in mods.items():
+        sd[f"base_model.model.{m}.lora_A.weight"] = torch.randn(r, k, generator=g)
+        sd[f"base_model.model.{m}.lora_B.weight"] = torch.randn(n, r, generator=g)
+    save_file(sd, str(path / "adapter_model.safetensors"))
+    return path
+
+
+def _disk_store(tmp_path, n=4, **kw):
+    mods = {"enc.q": (6, 4), "enc.dense": (4, 8)}
+    disk = DiskAdapterCache(tmp_path / "disk")
+    for i in range(n):
+        disk.add_adapter(f"ad{i}", _peft_dir(tmp_path / f"src{i}", mods, 2 + i % 2, i))
+    return CpuAdapterStore(disk_cache=disk, module_names=list(mods), **kw), list(mods)
+
+
+def test_prefetch_loads_the_same_weights_as_a_synchronous_get(tmp_path):
+    store, mods = _disk_store(tmp_path)
+    ref, _ = _disk_store(tmp_path / "ref")
+    futs = store.prefetch(["ad1", "ad2", "__base__", "unknown", "ad1"], image_dtype=torch.bfloat16, module_names=mods)
+    assert len(futs) == 2
+    for f in futs:
+        f.result(timeout=30)
+    assert {"ad1", "ad2"} <= set(store.adapters) and "ad0" not in store.adapters
+    for aid in ("ad1", "ad2"):
+        got, want = store.get(aid), ref.get(aid)
+        for m in mods:
+            assert torch.equal(got.layers[m].A, want.layers[m].A) and torch.equal(got.layers[m].B, want.layers[m].B)
+            assert got.layers[m].scale == want.layers[m].scale
+        # the image was built by the worker and is what slot_image returns
+        key = (aid, torch.bfloat16, tuple(mods))
+        assert key in store._images
+        image, ranks = store.slot_image(aid, mods, torch.bfloat16)
+        assert torch.equal(image, ref.slot_image(aid, mods, torch.bfloat16)[0]) and ranks == [got.layers[m].rank for m in mods]
+    assert store.prefetch(["ad1"]) == []  # resident: nothing to start
+
+
+def test_get_waits_for_an_inflight_prefetch_instead_of_loading_twice(tmp_path, monkeypatch):
+    import threading
+    import time
+
+    store, mods = _disk_store(tmp_path)
+    calls, gate = [], threading.Event()
+    orig = store._read_peft_dir
+
+    def slow_read(path):
+        calls.append(path)
+        gate.wait(5)
+        return orig(path)
+
+    monkeypatch.setattr(store, "_read_peft_dir", slow_read)
+    (fut,) = store.prefetch(["ad3"])
+    time.sleep(0.05)
+    threading.Timer(0.2, gate.set).start()
+    adapter = store.get("ad3")  # blocks until the worker has inserted it
+    assert fut.done() and adapter is store.adapters["ad3"] and len(calls) == 1
+
+
+def test_prefetch_errors_reach_the_future_and_get(tmp_path):
+    store, mods = _disk_store(tmp_path, n=1)
+    bad = tmp_path / "bad"
+    bad.mkdir()
+    (bad / "adapter_config.json").write_text(json.dumps({"peft_type": "LORA", "lora_alpha": 2, "r": 2, "use_dora": True}))
+    torch.save({}, bad / "adapter_model.bin")
+    store.disk_cache.add_adapter("bad", bad)
+    (fut,) = store.prefetch(["bad"])
+    with pytest.raises(ValueError, match="DoRA"):
+        fut.result(timeout=30)
+    with pytest.raises(ValueError, match="DoRA"):
+        store.get("bad")
+
+
+def test_get_under_the_tier_lock_does_not_wait_for_a_prefetch(tmp_path, monkeypatch):
+    """A GPU refill holds the tier's lock around get(); a prefetch of the same
+    adapter in flight must not deadlock it (the worker needs the lock)."""
+    import threading
+
+    store, mods = _disk_store(tmp_path)
+    gate = threading.Event()
+    orig = store._read_peft_dir
+
+    def gated_read(path):
+        gate.wait(5)
+        return orig(path)
+
+    monkeypatch.setattr(store, "_read_peft_dir", gated_read)
+    (fut,) = store.prefetch(["ad2"])
+    result = {}
+
+    def refill():
+        with store.locked():
+            monkeypatch.setattr(store, "_read_peft_dir", orig)  # the synchronous load is not gated
+            result["adapter"] = store.get("ad2")
+        gate.set()
+
+    t = threading.Thread(target=refill)
+    t.start()
+    t.join(timeout=20)
+    gate.set()
+    assert not t.is_alive(), "get() under the lock waited for the prefetch"
+    fut.result(timeout=20)
+    assert store.adapters["ad2"] is result["adapter"]  # the worker discarded its copy
+
+
+def _peft_dir_dtype(path: Path, mods, r, seed, dtype, tamper=None):
+    from safetensors.torch import save_file
+
+    g = torch.Generator().manual_seed(seed)
+    path.mkdir(parents=True)
+    (path / "adapter_config.json").write_text(json.dumps({"peft_type": "LORA", "lora_alpha": 2 * r, "r": r}))
+    sd = {}
+    for m, (k, n) in mods.items():
+        sd[f"base_model.model.{m}.lora_A.weight"] = torch.randn(r, k, generator=g).to(dtype)
+        sd[f"base_model.model.{m}.lora_B.weight"] = torch.randn(n, r, generator=g).to(dtype)
+    if tamper:
+        tamper(sd)
+    save_file(sd, str(path / "adapter_model.safetensors"))
+    return path
+
+
+@pytest.mark.parametrize("file_dtype", [torch.bfloat16, torch.float32])
+def test_direct_safetensors_load_equals_the_general_path(tmp_path, file_dtype):
+    mods = {"enc.q": (6, 4), "enc.dense": (4, 8), "enc.absent": (3, 3)}
+    names = list(mods)
+    disk = DiskAdapterCache(tmp_path / "disk")
+    for i in range(3):
+        disk.add_adapter(f"ad{i}", _peft_dir_dtype(tmp_path / f"s{i}", {m: mods[m] for m in names[:2]}, 2 + i, i, file_dtype))
+    fast = CpuAdapterStore(disk_cache=disk, module_names=names)
+    fast.set_image_spec(names, torch.bfloat16)
+    slow = CpuAdapterStore(disk_cache=disk, module_names=names)
+    for i in range(3):
+        aid = f"ad{i}"
+        a, b = fast.get(aid), slow.get(aid)
+        # with bf16 files the image is written while loading (no second build)
+        assert ((aid, torch.bfloat16, tuple(names)) in fast._images) == (file_dtype == torch.bfloat16)
+        assert a.layers.keys() == b.layers.keys() and "enc.absent" not in a.layers
+        for m in a.layers:
+            la, lb = a.layers[m], b.layers[m]
+            assert la.rank == lb.rank and la.scale == lb.scale and la.A.dtype == lb.A.dtype == file_dtype
+            assert torch.equal(la.A, lb.A) and torch.equal(la.B, lb.B)
+            assert tuple(la.A.shape) == (mods[m][0], la.rank) and tuple(la.B.shape) == (la.rank, mods[m][1])
+        img_a, ranks_a = fast.slot_image(aid, names, torch.bfloat16)
+        img_b, ranks_b = slow.slot_image(aid, names, torch.bfloat16)
+        assert ranks_a == ranks_b and torch.equal(img_a, img_b)
+
+
+@pytest.mark.parametrize("tamper,msg", [
+    (lambda sd: sd.update({"base_model.model.enc.q.lora_B.weight": torch.zeros(4, 3, dtype=torch.bfloat16)}), "rank mismatch"),
+    (lambda sd: sd.pop("base_model.model.enc.dense.lora_B.weight"), "incomplete LoRA weights"),
+    (lambda sd: sd.update({"base_model.model.other.lora_A.weight": torch.zeros(2, 2, dtype=torch.bfloat16)}),
+     "outside the configured module set"),
+])
+def test_direct_load_raises_the_general_paths_errors(tmp_path, tamper, msg):
+    mods = {"enc.q": (6, 4), "enc.dense": (4, 8)}
+    disk = DiskAdapterCache(tmp_path / "disk")
+    disk.add_adapter("bad", _peft_dir_dtype(tmp_path / "s", mods, 2, 0, torch.bfloat16, tamper))
+    for spec in (True, False):
+        store = CpuAdapterStore(disk_cache=disk, module_names=list(mods))
+        if spec:
+            store.set_image_spec(list(mods), torch.bfloat16)
+        with pytest.raises(ValueError, match=msg):
+            store.get("bad")
+        assert "bad" not in store.adapters
