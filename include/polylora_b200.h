@@ -65,11 +65,12 @@ int plora_device_status(int32_t* status_out, int32_t clear);
 
 /* Work-split threshold of the tensor-core shrink / expand, in tokens per SM:
  * calls whose num_tokens is at most this times the SM count spread each
- * slot's LoRA weights over the grid (weight split, for batches of few tokens
- * per adapter such as decode); larger calls give each CTA a share of the
- * tokens.  Default 16.  With value >= 0 sets it (0: never split weights);
- * returns the previous value.  Process-wide; results do not depend on it
- * beyond fp32 summation order.  No counterpart in the reference. */
+ * slot's LoRA weights over the grid (the slot-grid kernels: one CTA per slot
+ * and weight part, for batches of few tokens per adapter such as decode);
+ * larger calls give each CTA a share of the tokens.  Default 16.  With
+ * value >= 0 sets it (0: always the token split); returns the previous value.
+ * Process-wide; results do not depend on it beyond fp32 summation order.
+ * No counterpart in the reference. */
 int64_t plora_weight_split_tokens_per_sm(int64_t value);
 
 /* Workspace bytes needed by plora_build_segments, plora_sgmv_a_fwd and

@@ -137,24 +137,6 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// 3-D tiled map over a contiguous (d2, d1, d0) 16-bit tensor.
-[[maybe_unused]] int make_map_3d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, uint64_t d1,
-                uint64_t d2, uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz) {
-  auto enc = tensor_map_encoder();
-  if (!enc) return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  const cuuint64_t dims[3] = {d0, d1, d2};
-  const cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
-  const cuuint32_t box[3] = {b0, b1, 1};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  const CUtensorMapDataType dt = dtype == PLORA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return PLORA_OK;
-}
-
 // LoRA-A (num_slots, K, R) viewed as 5-D (R, e:2, m:4, cc:4, block) with
 // row k = 32 block + 8 m + 2 cc + e, so that a box lands each 32-row block
 // in (cc, m, e) order: shared-memory row position 8 cc + 2 m + e.  Slots are
@@ -196,24 +178,6 @@ int make_map_lora_b_chunks(CUtensorMap* map, const void* base, int dtype, uint64
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled (LoRA-B chunks) failed (%d)", (int)r);
-  return PLORA_OK;
-}
-
-// 2-D tiled map over a contiguous (d1, d0) 16-bit tensor.
-[[maybe_unused]] int make_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t d0, uint64_t d1,
-                uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz) {
-  auto enc = tensor_map_encoder();
-  if (!enc) return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  const cuuint64_t dims[2] = {d0, d1};
-  const cuuint64_t strides[1] = {d0 * 2};
-  const cuuint32_t box[2] = {b0, b1};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUtensorMapDataType dt = dtype == PLORA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(PLORA_ERR_CUDA, "cuTensorMapEncodeTiled(2d) failed (%d)", (int)r);
   return PLORA_OK;
 }
 

@@ -89,10 +89,10 @@ struct SlotItems {
 
 // ------------------------------------------------------------------ work split
 // One piece of a CTA's work: tokens [start, start + cnt) of `slot`, weight
-// windows [w_lo, w_hi] (group: always 0 for the token split).
+// windows [w_lo, w_hi].
 struct Work {
   int64_t start;
-  int slot, cnt, w_lo, w_hi, group;
+  int slot, cnt, w_lo, w_hi;
 };
 
 // Token split (batches of many tokens): the CTA's contiguous share [b, e) of
@@ -115,7 +115,6 @@ struct TokenWork {
         w.cnt = cnt;
         w.w_lo = 0;
         w.w_hi = nwin - 1;
-        w.group = 0;
         return true;
       }
     return false;

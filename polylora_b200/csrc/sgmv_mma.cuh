@@ -167,12 +167,12 @@ __device__ __noinline__ void issue_lora_a_window(const CUtensorMap* map8, const 
   for (; q < nb; ++q) tma_load_5d_outer(dst + q * block_bytes, map1, bar, blk0 + q);
 }
 
-// Sequence of the weight windows of the CTA's work (slot, group, window), in
+// Sequence of the weight windows of the CTA's work (slot, window), in
 // the order every warp consumes them.
 template <class WorkIt>
 struct WinCursor {
   WorkIt it;
-  int slot, group, w, w_hi;
+  int slot, w, w_hi;
   bool valid;
   __device__ void init(const SlotTab& tab, const WorkIt& src) {
     it = src;
@@ -189,7 +189,6 @@ struct WinCursor {
     Work nx;
     if (it.next(tab, nx)) {
       slot = nx.slot;
-      group = nx.group;
       w = nx.w_lo;
       w_hi = nx.w_hi;
       return;
