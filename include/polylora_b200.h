@@ -217,6 +217,24 @@ int plora_slot_fill(const plora_slot_module* modules, int32_t num_modules, int32
                     int32_t num_slots, int64_t max_rank, int32_t dtype, const void* host_image,
                     size_t image_bytes, void* staging, size_t staging_bytes, void* stream);
 
+/* Host only: packs the LoRA factors of a PEFT adapter's safetensors file
+ * (`path`) for `modules` into a slot image in plora_slot_fill's layout
+ * (records, then A (rank x in) and B (out x rank) blocks, 256-byte aligned;
+ * scale = lora_alpha / rank; absent modules rank 0).  A module's weight is the
+ * first key, in file order, ending in "<module>.lora_A.<adapter_name>.weight"
+ * or "<module>.lora_A.weight" (lora_B likewise), as in the reference's loader
+ * (src/polylora/store.py).  Writes *image_bytes (also when the image is too
+ * small: PLORA_ERR_WORKSPACE, nothing written) and dims[3 * i .. 3 * i + 2] =
+ * rank, in_features, out_features of module i.  Handles the common case only:
+ * PLORA_ERR_UNSUPPORTED when a LoRA tensor is missing, malformed, not of
+ * `dtype`, of inconsistent rank, duplicated, or outside `modules` (the
+ * Python loader then takes the file and raises the reference's errors);
+ * PLORA_ERR_INVALID_ARGUMENT when the file cannot be opened or read.  No
+ * counterpart in the reference (its loader is Python). */
+int plora_peft_pack(const char* path, const char* const* modules, int32_t num_modules,
+                    const char* adapter_name, int32_t dtype, double lora_alpha, void* image,
+                    size_t capacity, size_t* image_bytes, int64_t* dims);
+
 #ifdef __cplusplus
 }
 #endif

@@ -81,6 +81,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "plora_last_error": (ctypes.c_char_p, []),
     "plora_device_status": (ctypes.c_int, [ctypes.POINTER(_i32), _i32]),
     "plora_weight_split_tokens_per_sm": (_i64, [_i64]),
+    "plora_peft_pack": (
+        ctypes.c_int,
+        [ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p), _i32, ctypes.c_char_p, _i32, ctypes.c_double,
+         _c_void_p, _size, ctypes.POINTER(_size), ctypes.POINTER(_i64)],
+    ),
     "plora_workspace_size": (_size, [_i64, _i64, _i32]),
     "plora_build_segments": (
         ctypes.c_int,

@@ -14,6 +14,7 @@
 #include "segments.cuh"
 #include "sgmv_simt.cuh"
 #include "sgmv_grid.cuh"
+#include "peft_pack.h"
 
 using namespace plora;
 

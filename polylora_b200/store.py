@@ -21,6 +21,7 @@ disk tier are guarded by one lock.
 
 from __future__ import annotations
 
+import ctypes
 import json
 import shutil
 import threading
@@ -286,6 +287,8 @@ class CpuAdapterStore:
         # (module_names, dtype) of the GPU cache's slot images, set by the cache:
         # disk loads then place safetensors bytes straight into the image
         self._image_spec: tuple[tuple[str, ...], torch.dtype] | None = None
+        self._c_names: dict[tuple[str, ...], Any] = {}   # module names as a C string array
+        self._pack_bytes: dict[tuple[str, ...], int] = {}  # largest packed image seen (slab sizing)
         # guards adapters / _images / _loading / the disk tier (reentrant: get -> load -> add)
         self._lock = threading.RLock()
         self._loading: dict[str, Future] = {}  # adapter id -> in-flight prefetch
@@ -542,67 +545,76 @@ class CpuAdapterStore:
                 self._slabs[key] = slab
 
     def _load_direct(self, adapter_id: str, path: Path, names: list[str], peft_adapter_name: str):
-        """Loads an adapter by placing its safetensors bytes in its slot image.
+        """Loads an adapter by packing its safetensors file straight into its slot image.
 
-        Applies when the GPU cache's image spec is set, matches ``names`` and
-        the file's LoRA tensors are of the image dtype; returns None otherwise
-        (the caller takes the general path).  Validation and errors are those
-        of the general path: the per-module weights are built by
-        :meth:`_layers_from_peft_state_dict` from views of the filled image."""
+        Applies when the GPU cache's image spec is set and matches ``names``:
+        the native packer (``plora_peft_pack``, no interpreter lock) fills a
+        pinned slab, and the per-module weights are views of that image.  Returns
+        None when the packer declines the file (a tensor of another dtype,
+        missing, malformed, of inconsistent rank or outside the modules); the
+        caller then takes the general path, which raises the reference's errors."""
         spec = self._image_spec
         st_path = path / "adapter_model.safetensors"
         if spec is None or tuple(names) != spec[0] or not st_path.exists():
             return None
         dtype = spec[1]
-        code = {torch.bfloat16: "BF16", torch.float16: "F16", torch.float32: "F32"}.get(dtype)
-        config, _ = self._read_peft_dir_config(path)
-        header, data = _read_safetensors(st_path)
-        keys = dict.fromkeys(header)
-        index = _lora_key_index(keys, names, peft_adapter_name)
-        used = set(index.values())
-        if code is None or any(header[k].get("dtype") != code for k in used):
+        code = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}.get(dtype)
+        if code is None:
             return None
-        esize = torch.empty((), dtype=dtype).element_size()
-        records = (SlotRecord * len(names))()
-        places: list[tuple[str, int]] = []  # (key, image offset)
-        offset = _align(len(names) * _ctypes_sizeof(SlotRecord))
+        config, _ = self._read_peft_dir_config(path)
         alpha = float(config["lora_alpha"])
-        for i, name in enumerate(names):
-            ka, kb = index.get((name, "lora_A")), index.get((name, "lora_B"))
-            if ka is None or kb is None or len(header[ka]["shape"]) != 2 or len(header[kb]["shape"]) != 2:
-                continue  # absent, or malformed: left to the general checks below
-            ra = int(header[ka]["shape"][0])
-            records[i].a_offset = offset
-            places.append((ka, offset))
-            offset = _align(offset + _numel(header[ka]["shape"]) * esize)
-            records[i].b_offset = offset
-            places.append((kb, offset))
-            offset = _align(offset + _numel(header[kb]["shape"]) * esize)
-            records[i].rank = ra
-            records[i].scale = alpha / ra if ra > 0 else 0.0
-        slab = self._acquire_slab(offset)
-        image = slab[1][:offset] if slab is not None else torch.zeros(offset, dtype=torch.uint8)
         try:
-            image.zero_()
-            raw = image.numpy()
-            header_bytes = bytes(records)
-            raw[: len(header_bytes)] = memoryview(header_bytes)
-            views: dict[str, Any] = dict.fromkeys(header)
-            for key, off in places:
-                b0, b1 = header[key]["data_offsets"]
-                raw[off : off + (b1 - b0)] = data[b0:b1]
-                views[key] = image[off : off + (b1 - b0)].view(dtype).view(*header[key]["shape"])
-            for key in used:  # malformed entries: the general checks see their real shapes
-                if views[key] is None:
-                    b0, b1 = header[key]["data_offsets"]
-                    views[key] = torch.frombuffer(bytearray(data[b0:b1]), dtype=dtype).view(*header[key]["shape"])
-            layers = self._layers_from_peft_state_dict(adapter_id, views, names, alpha, peft_adapter_name, index)
-            ranks = [records[i].rank for i in range(len(names))]
-        except BaseException:
+            from . import _native
+
+            lib = _native.load()
+        except Exception:  # noqa: BLE001 - no library: the general path still works
+            return None
+        key_names = tuple(names)
+        c_names = self._c_names.get(key_names)
+        if c_names is None:
+            c_names = self._c_names[key_names] = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
+        n = len(names)
+        dims = (ctypes.c_int64 * (3 * n))()
+        nbytes = ctypes.c_size_t(0)
+        need = self._pack_bytes.get(key_names, 1 << 20)
+        for _ in range(2):
+            slab = self._acquire_slab(need)
+            buf = slab[1] if slab is not None else torch.empty(need, dtype=torch.uint8)
+            status = lib.plora_peft_pack(str(st_path).encode(), c_names, n, peft_adapter_name.encode(), code, alpha,
+                                         buf.data_ptr(), buf.numel(), ctypes.byref(nbytes), dims)
+            if status == 0:
+                break
             if slab is not None:
                 slab[0].release(slab[1])
-            raise
-        key = (adapter_id, dtype, tuple(names))
+            if status != 4:  # anything but "image too small": the general path decides
+                return None
+            need = int(nbytes.value)
+        else:
+            return None
+        size = int(nbytes.value)
+        with self._lock:
+            self._pack_bytes[key_names] = max(size, self._pack_bytes.get(key_names, 0))
+        image = buf[:size]
+        typed = image.view(dtype)
+        base = typed.storage_offset()
+        esize = typed.element_size()
+        recs = (SlotRecord * n).from_buffer_copy(image[: n * ctypes.sizeof(SlotRecord)].numpy().tobytes())
+        layers: dict[str, CpuLayerWeights] = {}
+        ranks: list[int] = []
+        for i, name in enumerate(names):
+            r, k_in, n_out = int(dims[3 * i]), int(dims[3 * i + 1]), int(dims[3 * i + 2])
+            ranks.append(r)
+            if r == 0:
+                continue
+            # (in, r) and (r, out): transposed views of the image's (r, in) and (out, r) blocks
+            a = torch.as_strided(typed, (k_in, r), (1, k_in), base + recs[i].a_offset // esize)
+            b = torch.as_strided(typed, (r, n_out), (1, r), base + recs[i].b_offset // esize)
+            layers[name] = CpuLayerWeights(A=a, B=b, rank=r, scale=alpha / r)
+        if not layers:  # the general path raises the reference's error for this
+            if slab is not None:
+                slab[0].release(slab[1])
+            return None
+        key = (adapter_id, dtype, key_names)
         return config, layers, (image, ranks), slab, key
 
     def _load_adapter_from_disk_path(
@@ -786,27 +798,6 @@ def _build_slot_image(adapter: CpuAdapter, module_names: list[str], dtype: torch
     for off, t in blocks:  # one converting copy per block
         image[off : off + t.numel() * esize].view(dtype).view(t.shape).copy_(t)
     return image, ranks
-
-
-def _numel(shape) -> int:
-    n = 1
-    for d in shape:
-        n *= int(d)
-    return n
-
-
-def _read_safetensors(path: Path):
-    """The JSON header (without ``__metadata__``) and the data section of a
-    safetensors file (8-byte little-endian header length, header, data)."""
-    import numpy as np
-
-    with open(path, "rb") as f:
-        n = int.from_bytes(f.read(8), "little")
-        header = json.loads(f.read(n))
-    # mapped, not read: each tensor's bytes are copied once, into the slot image
-    data = np.memmap(path, dtype=np.uint8, mode="r", offset=8 + n)
-    header.pop("__metadata__", None)
-    return header, data
 
 
 def _align(n: int, a: int = 256) -> int:

@@ -415,3 +415,41 @@ def test_direct_load_raises_the_general_paths_errors(tmp_path, tamper, msg):
         with pytest.raises(ValueError, match=msg):
             store.get("bad")
         assert "bad" not in store.adapters
+
+
+def test_native_packer_follows_the_reference_key_rules(tmp_path):
+    """Module names that are string suffixes of others, adapter-named keys,
+    __metadata__ and unrelated tensors: the packed load equals the general one."""
+    from safetensors.torch import save_file
+
+    mods = {"layer.1.dense": (4, 6), "encoder.layer.1.dense": (4, 6), "layer.11.dense": (5, 3), "q": (3, 3),
+            "attn.q": (3, 3)}
+    g = torch.Generator().manual_seed(7)
+    t = lambda *s: torch.randn(*s, generator=g).to(torch.bfloat16)  # noqa: E731
+    sd = {
+        "base_model.model.encoder.layer.11.dense.lora_A.weight": t(2, 5),
+        "base_model.model.encoder.layer.11.dense.lora_B.weight": t(3, 2),
+        "base_model.model.encoder.layer.1.dense.lora_A.default.weight": t(3, 4),
+        "base_model.model.encoder.layer.1.dense.lora_B.default.weight": t(6, 3),
+        "x.attn.q.lora_A.weight": t(2, 3),
+        "x.attn.q.lora_B.weight": t(3, 2),
+        "x.attn.q.lora_A.other.weight": t(4, 3),
+        "unrelated.weight": t(2, 2),
+    }
+    path = tmp_path / "src"
+    path.mkdir()
+    (path / "adapter_config.json").write_text(json.dumps({"peft_type": "LORA", "lora_alpha": 8, "r": 2}))
+    save_file(sd, str(path / "adapter_model.safetensors"), metadata={"format": "pt", "note": 'é "q" \\ x'})
+    names = list(mods)
+    disk = DiskAdapterCache(tmp_path / "disk")
+    disk.add_adapter("a", path)
+    fast = CpuAdapterStore(disk_cache=disk, module_names=names)
+    fast.set_image_spec(names, torch.bfloat16)
+    slow = CpuAdapterStore(disk_cache=disk, module_names=names)
+    a, b = fast.get("a"), slow.get("a")
+    assert ("a", torch.bfloat16, tuple(names)) in fast._images  # packed natively
+    assert a.layers.keys() == b.layers.keys()
+    for m in a.layers:
+        assert torch.equal(a.layers[m].A, b.layers[m].A) and torch.equal(a.layers[m].B, b.layers[m].B)
+        assert a.layers[m].rank == b.layers[m].rank and a.layers[m].scale == b.layers[m].scale
+    assert torch.equal(fast.slot_image("a", names, torch.bfloat16)[0], slow.slot_image("a", names, torch.bfloat16)[0])
