@@ -525,6 +525,102 @@ def run_sweep(args):
     print(json.dumps(line), flush=True)
 
 
+def run_triton_compare(args):
+    """The reference's own GPU path on this B200: its Triton `sgmv_lora_a_fwd` +
+    `sgmv_lora_b_fwd` (src/polylora/sgmv.py:141-175, 278-328, unmodified, from
+    the pip install under baseline/_ref) beside this library's operators of the
+    same signatures, eager, on the config-2 sweep inputs.  Each step is the
+    pair of calls as `layers.py:42-58` makes them (the reference's host syncs
+    included); times are CUDA events over back-to-back steps, and with L2
+    flushed before every step (loop [flush, step] minus loop [flush])."""
+    import torch
+
+    from polylora_b200.sgmv import sgmv_lora_a_fwd, sgmv_lora_b_fwd
+
+    ref_dir = ROOT / "baseline" / "_ref"
+    try:
+        sys.path.insert(0, str(ref_dir))
+        from polylora.sgmv import sgmv_lora_a_fwd as ref_a, sgmv_lora_b_fwd as ref_b
+    except Exception as exc:  # noqa: BLE001 - reported, not fatal
+        print(json.dumps({"workload": "cfg2-triton", "unavailable": f"reference not importable from {ref_dir.name}: "
+                          f"{type(exc).__name__}: {exc}"}), flush=True)
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    g = torch.Generator(device=dev).manual_seed(1000)
+    ranks_np, _, scales_np = workload(seed=0)
+    ranks = torch.from_numpy(ranks_np).to(dev)
+    scales = torch.from_numpy(scales_np).to(dev)
+    colmask = (torch.arange(MAX_RANK, device=dev)[None, :] < ranks[:, None]).float()
+    A = ((torch.rand(SLOTS, K_IN, MAX_RANK, device=dev, generator=g) * 2 - 1) / 64 * colmask[:, None, :]).to(torch.bfloat16)
+    Bw = (torch.randn(SLOTS, MAX_RANK, N_OUT, device=dev, generator=g) * 0.02 * colmask[:, :, None]).to(torch.bfloat16)
+    flush_w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_r = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    sink = torch.empty((), dtype=torch.float32, device=dev)
+
+    def flush():
+        flush_w.fill_(7)
+        torch.sum(flush_r, dim=0, out=sink)
+
+    def loop_ms(fns, reps):
+        for _ in range(3):
+            for f in fns:
+                f()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            for f in fns:
+                f()
+        b.record()
+        b.synchronize()
+        return a.elapsed_time(b) / reps
+
+    rows = []
+    reps = max(args.steps, 20)
+    for T in SWEEP_T:
+        rng = np.random.default_rng(T)
+        wi_np = rng.integers(1, SLOTS, size=T).astype(np.int64)
+        wi_np[rng.random(T) < 0.2] = 0
+        wi = torch.from_numpy(wi_np).to(dev)
+        seq = torch.ones(T, dtype=torch.int32, device=dev)
+        x = torch.randn(T, 1, K_IN, device=dev, generator=g).to(torch.bfloat16)
+        y0 = torch.randn(T, 1, N_OUT, device=dev, generator=g).to(torch.bfloat16)
+        y = y0.clone()
+
+        def ours():
+            sgmv_lora_b_fwd(sgmv_lora_a_fwd(x, A, seq, wi, ranks), Bw, seq, wi, ranks, scales, y)
+
+        def theirs():
+            ref_b(ref_a(x, A, seq, wi, ranks), Bw, seq, wi, ranks, scales, y)
+
+        # agreement on fresh outputs: max |difference| over the largest LoRA delta
+        y_o, y_r = y0.clone(), y0.clone()
+        sgmv_lora_b_fwd(sgmv_lora_a_fwd(x, A, seq, wi, ranks), Bw, seq, wi, ranks, scales, y_o)
+        ref_b(ref_a(x, A, seq, wi, ranks), Bw, seq, wi, ranks, scales, y_r)
+        torch.cuda.synchronize()
+        delta = (y_r.float() - y0.float()).abs().max().item()
+        diff = (y_o.float() - y_r.float()).abs().max().item()
+        row = {"T": T, "active_tokens": int((ranks_np[wi_np] > 0).sum()),
+               "max_abs_diff_over_max_delta": diff / delta if delta else diff}
+        t_flush = loop_ms([flush], reps)
+        for name, fn in (("triton_reference", theirs), ("ours", ours)):
+            warm = loop_ms([fn], reps)
+            cold = loop_ms([flush, fn], reps) - t_flush
+            row[name] = {"us_back_to_back": round(warm * 1e3, 2), "us_l2_flushed": round(cold * 1e3, 2),
+                         "tokens_per_s": T / (warm * 1e-3)}
+        row["speedup_back_to_back"] = row["triton_reference"]["us_back_to_back"] / row["ours"]["us_back_to_back"]
+        row["speedup_l2_flushed"] = row["triton_reference"]["us_l2_flushed"] / row["ours"]["us_l2_flushed"]
+        rows.append(row)
+        del x, y, y0, y_o, y_r
+    import triton
+
+    print(json.dumps({"workload": "cfg2-triton", "n_gpus": 1, "dtype": "bf16", "data": "synthetic",
+                      "config": "BASELINE config 2 op sweep (K=N=4096, 64 slots + __base__, max_rank 16, ranks "
+                                "U{0,4,8,16}, 20% base rows); step = sgmv_lora_a_fwd + sgmv_lora_b_fwd, eager",
+                      "triton": triton.__version__, "sweep": rows}), flush=True)
+
+
 def _graph_timer(stream):
     """(graph_of, replay_ms): capture callables as one CUDA graph after three
     eager warm-up passes; mean device time of `reps` back-to-back replays."""
@@ -1142,7 +1238,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["cfg2", "cfg2-sweep", "cfg3", "cfg4", "cfg4-decode", "cfg4-ops", "cfg5"],
+    ap.add_argument("--workload", choices=["cfg2", "cfg2-sweep", "cfg2-triton", "cfg3", "cfg4", "cfg4-decode",
+                                           "cfg4-ops", "cfg5"],
                     default="cfg2",
                     help="cfg2: the SGMV op step (default, the headline line); cfg3: model forward")
     ap.add_argument("--linear", default=None, help="cfg4-ops: only this Linear (e.g. gate_proj)")
@@ -1151,6 +1248,8 @@ def main():
     args = ap.parse_args()
     if args.workload == "cfg2-sweep" and args.impl != "reference":
         run_sweep(args)
+    elif args.workload == "cfg2-triton" and args.impl != "reference":
+        run_triton_compare(args)
     elif args.workload == "cfg4-ops" and args.impl != "reference":
         run_cfg4_ops(args)
     elif args.workload in ("cfg3", "cfg4", "cfg4-decode", "cfg5"):
