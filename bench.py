@@ -1080,7 +1080,7 @@ def run_model_cfg5(args):
     disk_dir = Path(tempfile.mkdtemp(prefix=f"plora_cfg5_r{rank}_"))
     model = PolyLoraModel(base, PolyLoraConfig(
         max_gpu_adapters=CFG5_SLOTS, max_rank=16, target_modules=CFG3_TARGETS,
-        max_cpu_adapters=CFG5_CPU, disk_cache_dir=disk_dir))
+        max_cpu_adapters=CFG5_CPU, disk_cache_dir=disk_dir, prefetch_workers=args.prefetch_workers))
     assert set(shapes) == set(model.target_module_names), "target matching differs"
     store = model.adapter_store
     # catalog: PEFT directories written where the disk tier keeps them (no copy);
@@ -1211,7 +1211,8 @@ def run_model_cfg5(args):
                             "Linears); 1024-adapter PEFT catalog (ranks {8,16}) on the disk tier, CPU LRU 256, "
                             "32 GPU slots; batches 128 x 256 tokens, adapter ids Zipf(0.9); one batch per step "
                             "(rank 0's stats), rows sharded over the GPUs, micro-batches of <= 32 distinct adapters; "
-                            "value with the next batch's adapters prefetched from disk on the CPU tier's thread",
+                            f"value with the next batch's adapters prefetched from disk on the CPU tier's "
+                            f"{args.prefetch_workers} worker thread(s)",
             },
             "ms_per_step_without_prefetch": ms_nopf,
             "tokens_per_s_without_prefetch": CFG5_ROWS * CFG5_SEQ / (ms_nopf * 1e-3),
@@ -1242,6 +1243,8 @@ def main():
                                            "cfg4-ops", "cfg5"],
                     default="cfg2",
                     help="cfg2: the SGMV op step (default, the headline line); cfg3: model forward")
+    ap.add_argument("--prefetch-workers", type=int, default=1,
+                    help="cfg5: worker threads of the CPU tier's prefetch of queued batches")
     ap.add_argument("--linear", default=None, help="cfg4-ops: only this Linear (e.g. gate_proj)")
     ap.add_argument("--split", choices=["token_split", "weight_split"], default=None,
                     help="cfg4-ops: only this work split")

@@ -228,7 +228,8 @@ class PinnedSlabPool:
 
     One large pinned arena is carved into slabs, so that building an image
     costs no page-locking call.  A released slab is reused only once the GPU
-    copy that last read it (:meth:`note_use`) has completed."""
+    copy that last read it (:meth:`note_use`) has completed.  Safe to use from
+    several threads (prefetch workers release slabs outside the store's lock)."""
 
     def __init__(self, slab_bytes: int, slabs_per_arena: int = 32) -> None:
         self.slab_bytes = slab_bytes
@@ -237,29 +238,33 @@ class PinnedSlabPool:
         self.free: list[torch.Tensor] = []
         self.retired: list[tuple[torch.Tensor, Any]] = []  # (slab, event of its last copy)
         self.last_use: dict[int, Any] = {}                 # slab data_ptr -> event
+        self._mutex = threading.Lock()
 
     def acquire(self) -> torch.Tensor:
-        if not self.free and self.retired:
-            still = []
-            for slab, ev in self.retired:
-                (self.free.append(slab) if ev.query() else still.append((slab, ev)))
-            self.retired = still
-        if not self.free:
-            arena = torch.empty(self.slabs_per_arena * self.slab_bytes, dtype=torch.uint8, pin_memory=True)
-            self.arenas.append(arena)
-            self.free.extend(arena[i * self.slab_bytes:(i + 1) * self.slab_bytes]
-                             for i in range(self.slabs_per_arena))
-        return self.free.pop()
+        with self._mutex:
+            if not self.free and self.retired:
+                still = []
+                for slab, ev in self.retired:
+                    (self.free.append(slab) if ev.query() else still.append((slab, ev)))
+                self.retired = still
+            if not self.free:
+                arena = torch.empty(self.slabs_per_arena * self.slab_bytes, dtype=torch.uint8, pin_memory=True)
+                self.arenas.append(arena)
+                self.free.extend(arena[i * self.slab_bytes:(i + 1) * self.slab_bytes]
+                                 for i in range(self.slabs_per_arena))
+            return self.free.pop()
 
     def note_use(self, slab: torch.Tensor, event: Any) -> None:
-        self.last_use[slab.data_ptr()] = event
+        with self._mutex:
+            self.last_use[slab.data_ptr()] = event
 
     def release(self, slab: torch.Tensor) -> None:
-        ev = self.last_use.pop(slab.data_ptr(), None)
-        if ev is None or ev.query():
-            self.free.append(slab)
-        else:
-            self.retired.append((slab, ev))
+        with self._mutex:
+            ev = self.last_use.pop(slab.data_ptr(), None)
+            if ev is None or ev.query():
+                self.free.append(slab)
+            else:
+                self.retired.append((slab, ev))
 
 
 class CpuAdapterStore:

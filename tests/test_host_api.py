@@ -268,24 +268,37 @@ def _disk_store(tmp_path, n=4, **kw):
     return CpuAdapterStore(disk_cache=disk, module_names=list(mods), **kw), list(mods)
 
 
-def test_prefetch_loads_the_same_weights_as_a_synchronous_get(tmp_path):
-    store, mods = _disk_store(tmp_path)
-    ref, _ = _disk_store(tmp_path / "ref")
-    futs = store.prefetch(["ad1", "ad2", "__base__", "unknown", "ad1"], image_dtype=torch.bfloat16, module_names=mods)
-    assert len(futs) == 2
+@pytest.mark.parametrize("workers", [1, 4])
+@pytest.mark.parametrize("direct", [False, True], ids=["general", "native_packer"])
+def test_prefetch_loads_the_same_weights_as_a_synchronous_get(tmp_path, workers, direct):
+    """One or several workers, through the Python parser or the native packer
+    (image spec published), while the main thread reads other adapters."""
+    store, mods = _disk_store(tmp_path, n=6, prefetch_workers=workers)
+    ref, _ = _disk_store(tmp_path / "ref", n=6)
+    dt = torch.float32 if direct else torch.bfloat16  # the files hold fp32: the packer takes fp32 images only
+    if direct:
+        store.set_image_spec(mods, dt)
+    wanted = ["ad1", "ad2", "ad3", "ad4", "ad5"]
+    futs = store.prefetch(wanted[:2] + ["__base__", "unknown", "ad1"] + wanted[2:],
+                          image_dtype=dt, module_names=mods)
+    assert len(futs) == 5
+    store.get("ad0")  # a synchronous load while the workers run
     for f in futs:
         f.result(timeout=30)
-    assert {"ad1", "ad2"} <= set(store.adapters) and "ad0" not in store.adapters
-    for aid in ("ad1", "ad2"):
+    assert set(wanted) <= set(store.adapters)
+    for aid in wanted:
         got, want = store.get(aid), ref.get(aid)
         for m in mods:
             assert torch.equal(got.layers[m].A, want.layers[m].A) and torch.equal(got.layers[m].B, want.layers[m].B)
             assert got.layers[m].scale == want.layers[m].scale
         # the image was built by the worker and is what slot_image returns
-        key = (aid, torch.bfloat16, tuple(mods))
+        key = (aid, dt, tuple(mods))
         assert key in store._images
-        image, ranks = store.slot_image(aid, mods, torch.bfloat16)
-        assert torch.equal(image, ref.slot_image(aid, mods, torch.bfloat16)[0]) and ranks == [got.layers[m].rank for m in mods]
+        image, ranks = store.slot_image(aid, mods, dt)
+        assert torch.equal(image, ref.slot_image(aid, mods, dt)[0]) and ranks == [got.layers[m].rank for m in mods]
+        # the native packer's weights are views of the packed image
+        shares = got.layers[mods[0]].A.untyped_storage().data_ptr() == image.untyped_storage().data_ptr()
+        assert shares == direct
     assert store.prefetch(["ad1"]) == []  # resident: nothing to start
 
 
