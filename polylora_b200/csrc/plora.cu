@@ -227,6 +227,11 @@ int build_segments(const int64_t* wi, const int32_t* seq_lens, const int32_t* ra
   const size_t need = seg_workspace_bytes(num_rows, num_slots);
   if (!ws || ws_bytes < need)
     return fail(PLORA_ERR_WORKSPACE, "segment workspace %zu < %zu bytes", ws_bytes, need);
+  if (num_rows <= kSegSmallRows && num_slots <= kSegSmallSlots && num_rows * max_seq <= kSegSmallTokens) {
+    seg_small_kernel<<<1, 1024, 0, stream>>>(wi, seq_lens, ranks, (int32_t)num_rows, max_seq, num_slots,
+                                             slot_start, token_index);
+    return check_launch("seg_small_kernel");
+  }
   SegWorkspace w = seg_workspace_carve(ws, num_rows, num_slots);
   const int64_t blocks = (num_rows + kSegRowsPerBlock - 1) / kSegRowsPerBlock;
   if (blocks > INT32_MAX) return fail(PLORA_ERR_UNSUPPORTED, "too many rows");

@@ -184,6 +184,111 @@ __global__ void __launch_bounds__(256) seg_place_kernel(int64_t num_rows, int64_
   for (int64_t m = lane; m < l; m += 32) token_index[dst + m] = (int32_t)(tok0 + m);
 }
 
+// One-launch builder for small batches (decode steps): one block of 1024
+// threads, one thread per row, the same table as the three passes above.
+//   1. key / len per row exactly as seg_count_kernel;
+//   2. per warp, the same-slot prefix of lower lanes (__match_any_sync group +
+//      shuffle scan); the group's last lane writes the warp's token count of
+//      that slot into cnt[warp][slot] (one group per slot per warp: no races);
+//   3. per slot (thread s), cnt[.][s] becomes the exclusive prefix over warps,
+//      i.e. over lower rows, and the slot total goes into a block scan over
+//      slots that gives slot_start;
+//   4. a row's first position is slot_start[slot] + cnt[warp][slot] + prefix;
+//      one warp per row then writes the row's token ids.
+// Rows <= kSegSmallRows, slots <= kSegSmallSlots and tokens <= kSegSmallTokens
+// (a single SM writes every token id).  Needs no workspace.
+constexpr int kSegSmallRows = 1024;
+constexpr int kSegSmallSlots = 256;
+constexpr int64_t kSegSmallTokens = 16384;
+
+__global__ void __launch_bounds__(1024) seg_small_kernel(
+    const int64_t* __restrict__ weight_indices, const int32_t* __restrict__ seq_lens,
+    const int32_t* __restrict__ lora_ranks, int32_t num_rows, int64_t max_seq, int32_t num_slots,
+    int32_t* __restrict__ slot_start, int32_t* __restrict__ token_index) {
+  __shared__ int32_t cnt[32][kSegSmallSlots];  // per-warp per-slot counts, then offsets
+  __shared__ int32_t start[kSegSmallSlots];
+  __shared__ int32_t row_dst[kSegSmallRows];   // first token position of a row, -1 when inactive
+  __shared__ int32_t warp_sums[32];
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  const int warp = t >> 5;
+  for (int i = t; i < 32 * kSegSmallSlots; i += blockDim.x) (&cnt[0][0])[i] = 0;
+
+  int key = -1;
+  int len = 0;
+  if (t < num_rows) {
+    const int64_t slot = weight_indices[t];
+    if (slot < 0 || slot >= num_slots) {
+      raise_status(PLORA_DEV_SLOT_RANGE);
+    } else {
+      const int32_t rank = lora_ranks[slot];
+      int64_t l = seq_lens[t];
+      l = l < 0 ? 0 : (l > max_seq ? max_seq : l);
+      if (rank > 0 && l > 0) {
+        key = (int)slot;
+        len = (int)l;
+      }
+    }
+  }
+  const unsigned peers = __match_any_sync(0xffffffffu, key);
+  int prefix = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int lj = __shfl_sync(0xffffffffu, len, j);
+    if (j < lane && ((peers >> j) & 1u)) prefix += lj;
+  }
+  const bool group_last = (31 - __clz(peers)) == lane;
+  __syncthreads();  // cnt zeroed
+  if (key >= 0 && group_last) cnt[warp][key] = prefix + len;
+  __syncthreads();
+
+  int total = 0;
+  if (t < num_slots) {
+#pragma unroll 8
+    for (int w = 0; w < 32; ++w) {
+      const int v = cnt[w][t];
+      cnt[w][t] = total;
+      total += v;
+    }
+  }
+  int incl = total;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += u;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int v = warp_sums[lane];
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, v, d);
+      if (lane >= d) v += u;
+    }
+    warp_sums[lane] = v;  // inclusive over warps
+  }
+  __syncthreads();
+  if (t < num_slots) {
+    const int excl = (warp > 0 ? warp_sums[warp - 1] : 0) + incl - total;
+    start[t] = excl;
+    slot_start[t] = excl;
+  }
+  if (t == 0) slot_start[num_slots] = warp_sums[31];
+  __syncthreads();
+  if (t < num_rows) row_dst[t] = key >= 0 ? start[key] + cnt[warp][key] + prefix : -1;
+  __syncthreads();
+
+  for (int r = warp; r < num_rows; r += 32) {
+    const int dst = row_dst[r];
+    if (dst < 0) continue;
+    int64_t l = seq_lens[r];
+    l = l < 0 ? 0 : (l > max_seq ? max_seq : l);
+    const int64_t tok0 = (int64_t)r * max_seq;
+    for (int64_t m = lane; m < l; m += 32) token_index[dst + m] = (int32_t)(tok0 + m);
+  }
+}
+
 // Flat tile schedule of the reference (sgmv.py:29-61), one block with carry:
 //   num_n_tiles[b] = cdiv(n_eff[b], block_n)
 //   tiles[b]       = (seq_len == 0 || n_eff == 0) ? 0 : cdiv(seq_len, block_m) * num_n_tiles[b]

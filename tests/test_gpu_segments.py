@@ -30,6 +30,12 @@ CASES = [
     (37, 5, 2, 0.5, [16]),
     (255, 3, 17, 0.3, [0, 16]),
     (257, 3, 17, 0.3, [0, 16]),
+    # the one-launch builder's limits (rows <= 1024, slots <= 256, tokens <= 16384) and just past each
+    (1024, 16, 256, 0.2, [0, 4, 8, 16]),
+    (1000, 16, 200, 0.1, [0, 8]),
+    (1024, 17, 65, 0.2, [0, 4, 8, 16]),
+    (1025, 1, 65, 0.2, [0, 4, 8, 16]),
+    (1024, 1, 257, 0.2, [0, 4, 8, 16]),
 ]
 
 
