@@ -206,6 +206,37 @@ def test_cpu_miss_reloads_adapter_from_disk_cache(tmp_path, cuda_status_clean):
     torch.testing.assert_close(actual, _closed_form_model(copy.deepcopy(base), [ad], sample), atol=1e-5, rtol=1e-5)
 
 
+def test_three_disk_adapters_batched_equal_per_row(tmp_path, cuda_status_clean):
+    """Three PEFT adapters saved as adapter_model.bin (ranks 2/3/4, alpha
+    4/9/8, as the reference's disk test): a right-padded mixed batch equals
+    each row run alone with its adapter, and the closed form, at 1e-5."""
+    base = _tiny_deberta(11).cuda()
+    modules = _linear_modules(base, TARGETS)
+    model = PolyLoraModel(copy.deepcopy(base), PolyLoraConfig(target_modules=TARGETS, max_gpu_adapters=3,
+                                                               max_rank=4)).eval()
+    spec = {"a": (2, 4.0), "b": (3, 9.0), "c": (4, 8.0)}
+    sds = {a: _random_adapter(modules, r, 40 + i) for i, (a, (r, _)) in enumerate(spec.items())}
+    for a, (r, alpha) in spec.items():
+        model.load_adapter_from_disk(a, str(_write_adapter(tmp_path / a, sds[a], r, alpha, "bin")))
+    ids = torch.randint(1, 97, (5, 9), generator=torch.Generator().manual_seed(3))
+    mask = torch.ones(5, 9, dtype=torch.long)
+    mask[1, 6:] = 0
+    mask[3, 2:] = 0
+    rows = ["c", "a", "b", "__base__", "a"]
+    sample = dict(input_ids=ids.cuda(), attention_mask=mask.cuda())
+    with torch.inference_mode():
+        out = model(**sample, adapter_ids=rows).last_hidden_state
+        for i, a in enumerate(rows):
+            one = model(input_ids=ids[i:i + 1].cuda(), attention_mask=mask[i:i + 1].cuda(),
+                        adapter_ids=[a]).last_hidden_state
+            valid = mask[i].bool().cuda()
+            torch.testing.assert_close(out[i][valid], one[0][valid], atol=1e-5, rtol=1e-5)
+    ads = {a: _layers_from_sd({k: t.cuda() for k, t in sds[a].items()}, spec[a][1]) for a in spec}
+    expected = _closed_form_model(copy.deepcopy(base), [ads.get(r) for r in rows], sample)
+    valid = mask.bool().cuda()
+    torch.testing.assert_close(out[valid], expected[valid], atol=1e-5, rtol=1e-5)
+
+
 def test_bf16_model_matches_closed_form(cuda_status_clean):
     """bf16 weights take the tensor-core kernels (max_rank 16)."""
     base = _tiny_deberta(9).cuda().to(torch.bfloat16)
