@@ -367,9 +367,12 @@ extern "C" int plora_peft_pack(const char* path, const char* const* modules, int
   }
   // check what the packing uses, lay out the image
   auto usable = [&](const TensorInfo& t) {
-    if (t.dtype != code || t.shape.size() != 2 || t.shape[0] < 0 || t.shape[1] < 0) return false;
+    if (t.dtype != code || t.shape.size() != 2) return false;
+    // dims below 2^31, so that their product cannot overflow (the header is untrusted input)
+    if (t.shape[0] < 0 || t.shape[1] < 0 || t.shape[0] > INT32_MAX || t.shape[1] > INT32_MAX) return false;
     if (t.begin < 0 || t.end < t.begin || t.end > data_len) return false;
-    return t.end - t.begin == t.shape[0] * t.shape[1] * esize;
+    const int64_t n = t.shape[0] * t.shape[1];
+    return n <= (t.end - t.begin) / esize && n * esize == t.end - t.begin;
   };
   int64_t offset = align256((int64_t)num_modules * (int64_t)sizeof(plora_slot_record));
   std::vector<plora_slot_record> recs((size_t)num_modules);

@@ -466,3 +466,44 @@ def test_native_packer_follows_the_reference_key_rules(tmp_path):
         assert torch.equal(a.layers[m].A, b.layers[m].A) and torch.equal(a.layers[m].B, b.layers[m].B)
         assert a.layers[m].rank == b.layers[m].rank and a.layers[m].scale == b.layers[m].scale
     assert torch.equal(fast.slot_image("a", names, torch.bfloat16)[0], slow.slot_image("a", names, torch.bfloat16)[0])
+
+
+def _raw_safetensors(path: Path, header: bytes, data: bytes = b"", declared_len: int | None = None) -> Path:
+    n = len(header) if declared_len is None else declared_len
+    path.write_bytes(n.to_bytes(8, "little") + header + data)
+    return path
+
+
+def test_native_packer_declines_hostile_headers(tmp_path):
+    """The packer reads untrusted files: shapes whose byte count overflows,
+    over-deep JSON, a header longer than the file and offsets past the data are
+    declined (PLORA_ERR_UNSUPPORTED) with nothing written."""
+    import ctypes
+
+    from polylora_b200 import _native
+
+    lib = _native.load()
+    mods = (ctypes.c_char_p * 1)(b"enc.q")
+    dims = (ctypes.c_int64 * 3)()
+    nbytes = ctypes.c_size_t(0)
+    image = torch.full((4096,), 0xAB, dtype=torch.uint8)
+
+    def pack(path):
+        return lib.plora_peft_pack(str(path).encode(), mods, 1, b"default", 2, 8.0, image.data_ptr(), image.numel(),
+                                   ctypes.byref(nbytes), dims)
+
+    huge = 1 << 62  # 2^62 x 4 bf16 elements: the byte count wraps to 0 in 64 bits
+    overflow = {"base_model.model.enc.q.lora_A.weight": {"dtype": "BF16", "shape": [huge, 4], "data_offsets": [0, 0]},
+                "base_model.model.enc.q.lora_B.weight": {"dtype": "BF16", "shape": [4, huge], "data_offsets": [0, 0]}}
+    past_end = {"base_model.model.enc.q.lora_A.weight": {"dtype": "BF16", "shape": [2, 4], "data_offsets": [0, 16]},
+                "base_model.model.enc.q.lora_B.weight": {"dtype": "BF16", "shape": [4, 2], "data_offsets": [16, 4096]}}
+    cases = {
+        "overflow": _raw_safetensors(tmp_path / "o.safetensors", json.dumps(overflow).encode()),
+        "deep": _raw_safetensors(tmp_path / "d.safetensors", b"[" * 200 + b"]" * 200),
+        "long_header": _raw_safetensors(tmp_path / "h.safetensors", b'{"a": 1}', declared_len=1 << 20),
+        "past_end": _raw_safetensors(tmp_path / "p.safetensors", json.dumps(past_end).encode(), bytes(32)),
+    }
+    for name, path in cases.items():
+        assert pack(path) == _native.ERR_UNSUPPORTED, name
+        assert bool((image == 0xAB).all()), f"{name}: image written"
+    assert pack(tmp_path / "missing.safetensors") == _native.ERR_INVALID_ARGUMENT
