@@ -48,6 +48,7 @@ extern "C" {
 #define PLORA_DEV_WAIT_TIMEOUT 1 /* a bounded pipeline wait expired; kernel returned early */
 #define PLORA_DEV_SLOT_RANGE 2   /* a weight index outside [0, num_slots) was skipped      */
 #define PLORA_DEV_RANK_RANGE 4   /* a rank outside [0, max_rank] was clamped               */
+#define PLORA_DEV_IMAGE_RANGE 8  /* a slot-image record pointed outside the image: rank 0  */
 
 /* Library version string. */
 const char* plora_version(void);
@@ -196,6 +197,9 @@ int plora_sgmv_shrink_expand(const void* x, const void* lora_a, void* tmp, const
  *   A block (rank x in_features) row-major and B block (out_features x rank)
  *   row-major: the factors as PEFT stores them (lora_A.weight, lora_B.weight);
  *   the fill writes them transposed into the slot layouts.
+ * A record of nonzero rank whose blocks are not inside [0, image_bytes), or
+ * not aligned to the element size, is not read: that module is filled as
+ * rank 0 and the device status gets PLORA_DEV_IMAGE_RANGE.
  * ------------------------------------------------------------------------- */
 typedef struct plora_slot_module {
   void* lora_a;     /* (num_slots, in_features, max_rank) */

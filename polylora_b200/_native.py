@@ -27,6 +27,7 @@ ERR_DEVICE = 5
 DEV_WAIT_TIMEOUT = 1
 DEV_SLOT_RANGE = 2
 DEV_RANK_RANGE = 4
+DEV_IMAGE_RANGE = 8
 
 NOALLOC_SCRATCH_BYTES = 8 << 20  # PLORA_NOALLOC_SCRATCH_BYTES
 

@@ -653,12 +653,13 @@ int plora_slot_fill(const plora_slot_module* modules, int32_t num_modules, int32
              "slot image copy");
   const dim3 grid(64, (unsigned)num_modules), block(256);
   const uint8_t* img = static_cast<const uint8_t*>(staging);
+  const int64_t nbytes = (int64_t)image_bytes;
   if (elem_size(dtype) == 4)
-    slot_fill_kernel<float><<<grid, block, 0, s>>>(modules, num_modules, slot, max_rank, img);
+    slot_fill_kernel<float><<<grid, block, 0, s>>>(modules, num_modules, slot, max_rank, img, nbytes);
   else if (dtype == PLORA_DTYPE_BF16)
-    slot_fill_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(modules, num_modules, slot, max_rank, img);
+    slot_fill_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(modules, num_modules, slot, max_rank, img, nbytes);
   else
-    slot_fill_kernel<__half><<<grid, block, 0, s>>>(modules, num_modules, slot, max_rank, img);
+    slot_fill_kernel<__half><<<grid, block, 0, s>>>(modules, num_modules, slot, max_rank, img, nbytes);
   return check_launch("slot_fill_kernel");
 }
 

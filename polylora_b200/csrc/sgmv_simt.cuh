@@ -123,11 +123,15 @@ __global__ void __launch_bounds__(kSimtThreads) sgmv_expand_simt_kernel(const Ex
 // holds each module's factors as PEFT stores them (A rank x in, B out x rank),
 // so the host does no transposes; this kernel writes them transposed into the
 // slot layouts (K x R, R x N).  Mirrors src/polylora/cache.py:108-115 (zero on
-// evict) and 119-150 (load, which transposes on the host).
+// evict) and 119-150 (load, which transposes on the host).  A record whose A or
+// B block does not lie inside the image's `image_bytes` (or is not aligned to
+// the element size) is not read: the module is filled as rank 0 and
+// PLORA_DEV_IMAGE_RANGE is raised.
 template <typename T>
 __global__ void __launch_bounds__(256) slot_fill_kernel(const plora_slot_module* __restrict__ mods,
                                                          int32_t num_modules, int32_t slot,
-                                                         int64_t R, const uint8_t* __restrict__ image) {
+                                                         int64_t R, const uint8_t* __restrict__ image,
+                                                         int64_t image_bytes) {
   const int m = blockIdx.y;
   if (m >= num_modules) return;
   const plora_slot_module mod = mods[m];
@@ -135,6 +139,17 @@ __global__ void __launch_bounds__(256) slot_fill_kernel(const plora_slot_module*
   int64_t r = rec.rank;
   r = r < 0 ? 0 : (r > R ? R : r);
   const int64_t K = mod.in_features, N = mod.out_features;
+  if (r > 0) {
+    const int64_t esz = (int64_t)sizeof(T);
+    const bool inside = rec.a_offset >= 0 && rec.b_offset >= 0 && rec.a_offset % esz == 0 &&
+                        rec.b_offset % esz == 0 && rec.a_offset <= image_bytes &&
+                        rec.b_offset <= image_bytes && r * K * esz <= image_bytes - rec.a_offset &&
+                        r * N * esz <= image_bytes - rec.b_offset;
+    if (!inside) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) raise_status(PLORA_DEV_IMAGE_RANGE);
+      r = 0;
+    }
+  }
   const int64_t nA = K * R, nB = R * N;
   T* A = reinterpret_cast<T*>(mod.lora_a) + (int64_t)slot * nA;
   T* B = reinterpret_cast<T*>(mod.lora_b) + (int64_t)slot * nB;
