@@ -94,3 +94,22 @@ def test_product_path_has_no_cpu_fallback():
     with pytest.raises(RuntimeError, match="CUDA"):
         sgmv_lora_a_fwd(x, w, torch.ones(2, dtype=torch.int32), torch.zeros(2, dtype=torch.int64),
                         torch.zeros(3, dtype=torch.int32))
+
+
+def test_segment_and_slot_fill_limits_rejected_before_cuda(native):
+    """Size limits and slot-fill arguments are checked on the host, before any
+    CUDA call (the non-null pointers below are never dereferenced)."""
+    lib = native.load()
+    dummy = 0x1000
+    # more slots than the segment kernels take
+    st = lib.plora_build_segments(dummy, dummy, dummy, 4, 1, 5000, dummy, dummy, dummy, 1 << 20, None)
+    assert st == native.ERR_UNSUPPORTED and "num_slots" in native.last_error()
+    # token ids must fit in int32
+    st = lib.plora_build_segments(dummy, dummy, dummy, 1 << 20, 1 << 12, 65, dummy, dummy, dummy, 1 << 20, None)
+    assert st == native.ERR_UNSUPPORTED and "int32" in native.last_error()
+    # slot fill: slot outside the cache, image smaller than its records, staging too small
+    fill = lambda slot, image_bytes, staging_bytes: lib.plora_slot_fill(  # noqa: E731
+        dummy, 2, slot, 4, 16, native.DTYPE_BF16, dummy, image_bytes, dummy, staging_bytes, None)
+    assert fill(4, 4096, 4096) == native.ERR_INVALID_ARGUMENT
+    assert fill(1, 47, 4096) == native.ERR_INVALID_ARGUMENT and "records" in native.last_error()
+    assert fill(1, 4096, 4095) == native.ERR_WORKSPACE
