@@ -90,6 +90,9 @@ size_t plora_workspace_size(int64_t num_rows, int64_t max_seq, int32_t num_slots
  *   token_index (num_rows * max_seq,) int32: active token ids (row*max_seq+m)
  *               ordered by (slot, row, m); entries past the total are unused.
  * A token is active when its slot's rank in `lora_ranks` is > 0.
+ * Batches of at most 1024 rows, 256 slots and 16384 tokens are built by one
+ * kernel, larger ones by three; the table is the same either way, and the
+ * workspace must be passed in both cases.
  * ------------------------------------------------------------------------- */
 int plora_build_segments(const int64_t* weight_indices, const int32_t* seq_lens,
                          const int32_t* lora_ranks, int64_t num_rows, int64_t max_seq,
