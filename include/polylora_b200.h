@@ -228,13 +228,16 @@ int plora_slot_fill(const plora_slot_module* modules, int32_t num_modules, int32
  * (`path`) for `modules` into a slot image in plora_slot_fill's layout
  * (records, then A (rank x in) and B (out x rank) blocks, 256-byte aligned;
  * scale = lora_alpha / rank; absent modules rank 0).  A module's weight is the
- * first key, in file order, ending in "<module>.lora_A.<adapter_name>.weight"
+ * first key, in data-offset order (as safetensors' load_file returns them),
+ * ending in "<module>.lora_A.<adapter_name>.weight"
  * or "<module>.lora_A.weight" (lora_B likewise), as in the reference's loader
  * (src/polylora/store.py).  Writes *image_bytes (also when the image is too
  * small: PLORA_ERR_WORKSPACE, nothing written) and dims[3 * i .. 3 * i + 2] =
  * rank, in_features, out_features of module i.  Handles the common case only:
  * PLORA_ERR_UNSUPPORTED when a LoRA tensor is missing, malformed, not of
- * `dtype`, of inconsistent rank, duplicated, or outside `modules` (the
+ * `dtype`, of inconsistent rank, duplicated, or outside `modules`, and when
+ * any tensor fails the safetensors format's own checks (known dtype, bytes
+ * matching the shape, data blocks tiling the data section) or is empty (the
  * Python loader then takes the file and raises the reference's errors);
  * PLORA_ERR_INVALID_ARGUMENT when the file cannot be opened or read.  No
  * counterpart in the reference (its loader is Python). */

@@ -8,7 +8,8 @@
 // consistent, all LoRA keys inside the configured modules -- and answers
 // PLORA_ERR_UNSUPPORTED otherwise, so that the Python loader (which raises the
 // reference's exact errors) takes over.  Key matching is the reference's
-// (src/polylora/store.py: a module's weight is the first key, in file order,
+// (src/polylora/store.py: a module's weight is the first key, in data-offset
+// order (the order safetensors' load_file returns the keys in),
 // ending in "<module>.<lora_A|lora_B>[.<adapter name>].weight").
 //
 // safetensors layout: 8-byte little-endian header length n, n bytes of JSON
@@ -20,6 +21,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
@@ -39,6 +41,7 @@ namespace peft {
 struct JVal {
   enum Kind { kNull, kBool, kNum, kStr, kArr, kObj } kind = kNull;
   double num = 0;
+  bool int_lit = false;  // the number was written as plain decimal digits
   std::string str;
   std::vector<JVal> arr;
   std::vector<std::pair<std::string, JVal>> obj;  // insertion (file) order
@@ -138,7 +141,7 @@ class JParser {
     ++p_;
     return true;
   }
-  bool number(double& out) {
+  bool number(double& out, bool& int_lit) {
     const char* s = p_;
     if (p_ < end_ && *p_ == '-') ++p_;
     while (p_ < end_ && ((*p_ >= '0' && *p_ <= '9') || *p_ == '.' || *p_ == 'e' || *p_ == 'E' ||
@@ -150,6 +153,8 @@ class JParser {
     buf[p_ - s] = 0;
     char* stop = nullptr;
     out = strtod(buf, &stop);
+    int_lit = true;
+    for (const char* q = s; q < p_; ++q) int_lit = int_lit && *q >= '0' && *q <= '9';
     return stop == buf + (p_ - s);
   }
   bool value(JVal& v, int depth) {
@@ -219,7 +224,7 @@ class JParser {
     }
     if (lit("null")) return true;
     v.kind = JVal::kNum;
-    return number(v.num);
+    return number(v.num, v.int_lit);
   }
 };
 
@@ -227,8 +232,22 @@ class JParser {
 struct TensorInfo {
   std::string name, dtype;
   std::vector<int64_t> shape;
+  bool has_shape = false;
   int64_t begin = -1, end = -1;
 };
+
+// Element bytes of the safetensors dtypes this packer checks (0: any other,
+// which the Python loader then judges).
+inline int64_t dtype_bytes(const std::string& d) {
+  if (d == "BOOL" || d == "U8" || d == "I8" || d == "F8_E5M2" || d == "F8_E4M3") return 1;
+  if (d == "I16" || d == "U16" || d == "F16" || d == "BF16") return 2;
+  if (d == "I32" || d == "U32" || d == "F32") return 4;
+  if (d == "I64" || d == "U64" || d == "F64") return 8;
+  return 0;
+}
+
+// Header size limit of the safetensors format's loader.
+constexpr uint64_t kMaxHeaderBytes = 100000000;
 
 // A file opened for positioned reads (closed on destruction).  Tensors are
 // read with pread straight into the image: one kernel copy per tensor, no
@@ -290,7 +309,7 @@ extern "C" int plora_peft_pack(const char* path, const char* const* modules, int
   if (!file.read_at(head, 8, 0)) return PLORA_ERR_INVALID_ARGUMENT;
   uint64_t hlen = 0;
   for (int i = 7; i >= 0; --i) hlen = (hlen << 8) | head[i];
-  if (hlen > file.size - 8) return PLORA_ERR_UNSUPPORTED;
+  if (hlen > file.size - 8 || hlen > kMaxHeaderBytes) return PLORA_ERR_UNSUPPORTED;
   std::string header((size_t)hlen, '\0');
   if (!file.read_at(&header[0], (size_t)hlen, 8)) return PLORA_ERR_INVALID_ARGUMENT;
   JVal root;
@@ -302,7 +321,12 @@ extern "C" int plora_peft_pack(const char* path, const char* const* modules, int
   tensors.reserve(root.obj.size());
   std::unordered_set<std::string> seen;
   for (auto& kv : root.obj) {
-    if (kv.first == "__metadata__") continue;
+    if (kv.first == "__metadata__") {  // a map of strings, or the format's loader refuses the file
+      if (kv.second.kind != JVal::kObj) return PLORA_ERR_UNSUPPORTED;
+      for (auto& m : kv.second.obj)
+        if (m.second.kind != JVal::kStr) return PLORA_ERR_UNSUPPORTED;
+      continue;
+    }
     if (!seen.insert(kv.first).second) return PLORA_ERR_UNSUPPORTED;  // duplicate names
     const JVal& t = kv.second;
     if (t.kind != JVal::kObj) return PLORA_ERR_UNSUPPORTED;
@@ -312,13 +336,15 @@ extern "C" int plora_peft_pack(const char* path, const char* const* modules, int
       if (f.first == "dtype" && f.second.kind == JVal::kStr) {
         info.dtype = f.second.str;
       } else if (f.first == "shape" && f.second.kind == JVal::kArr) {
+        info.has_shape = true;
         for (auto& d : f.second.arr) {
-          if (d.kind != JVal::kNum || !is_int(d.num)) return PLORA_ERR_UNSUPPORTED;
+          if (d.kind != JVal::kNum || !d.int_lit || !is_int(d.num)) return PLORA_ERR_UNSUPPORTED;
           info.shape.push_back((int64_t)d.num);
         }
       } else if (f.first == "data_offsets" && f.second.kind == JVal::kArr && f.second.arr.size() == 2) {
         if (f.second.arr[0].kind != JVal::kNum || f.second.arr[1].kind != JVal::kNum ||
-            !is_int(f.second.arr[0].num) || !is_int(f.second.arr[1].num))
+            !f.second.arr[0].int_lit || !f.second.arr[1].int_lit || !is_int(f.second.arr[0].num) ||
+            !is_int(f.second.arr[1].num))
           return PLORA_ERR_UNSUPPORTED;
         info.begin = (int64_t)f.second.arr[0].num;
         info.end = (int64_t)f.second.arr[1].num;
@@ -326,6 +352,30 @@ extern "C" int plora_peft_pack(const char* path, const char* const* modules, int
     }
     tensors.push_back(std::move(info));
   }
+  // The checks the safetensors loader makes on every tensor, which the Python
+  // path runs and raises on: a known dtype, a shape whose bytes are the
+  // tensor's, and data blocks that tile the data section from 0 to its end.
+  // Files failing them, and files with empty tensors, are left to that path.
+  for (auto& t : tensors) {
+    const int64_t esz = dtype_bytes(t.dtype);
+    if (esz == 0 || !t.has_shape || t.begin < 0 || t.end <= t.begin) return PLORA_ERR_UNSUPPORTED;
+    int64_t n = 1;
+    for (int64_t d : t.shape) {
+      if (d <= 0 || d > INT32_MAX || n > (INT64_MAX / esz) / d) return PLORA_ERR_UNSUPPORTED;
+      n *= d;
+    }
+    if (n * esz != t.end - t.begin) return PLORA_ERR_UNSUPPORTED;
+  }
+  // data-offset order: the order safetensors' load_file returns the keys in,
+  // which decides the reference's first matching key
+  std::sort(tensors.begin(), tensors.end(),
+            [](const TensorInfo& a, const TensorInfo& b) { return a.begin < b.begin; });
+  int64_t expect = 0;
+  for (auto& t : tensors) {
+    if (t.begin != expect) return PLORA_ERR_UNSUPPORTED;
+    expect = t.end;
+  }
+  if (expect != data_len) return PLORA_ERR_UNSUPPORTED;
 
   std::vector<std::string> names(modules, modules + num_modules);
   const std::unordered_set<std::string_view> wanted(names.begin(), names.end());
@@ -346,7 +396,7 @@ extern "C" int plora_peft_pack(const char* path, const char* const* modules, int
       break;
     }
   }
-  // (module, side) -> first tensor, in file order, whose prefix ends with the module name
+  // (module, side) -> first tensor, in data-offset order, whose prefix ends with the module name
   const std::string name(adapter_name);
   std::map<std::pair<std::string, int>, int> index;
   for (int k = 0; k < (int)tensors.size(); ++k) {
