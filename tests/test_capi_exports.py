@@ -113,3 +113,32 @@ def test_segment_and_slot_fill_limits_rejected_before_cuda(native):
     assert fill(4, 4096, 4096) == native.ERR_INVALID_ARGUMENT
     assert fill(1, 47, 4096) == native.ERR_INVALID_ARGUMENT and "records" in native.last_error()
     assert fill(1, 4096, 4095) == native.ERR_WORKSPACE
+
+
+def test_header_is_plain_c_and_links(tmp_path, native):
+    """A C11 program that includes the header (pedantic, warnings as errors),
+    takes the address of every declared entry point and links against the
+    library: the boundary is a C ABI, usable without C++ or CUDA headers."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    lib = Path(native.load()._name)
+    names = declared_functions()
+    src = tmp_path / "caller.c"
+    src.write_text(
+        '#include "polylora_b200.h"\n#include <stdio.h>\n'
+        "typedef void (*fn)(void);\n"
+        "_Static_assert(sizeof(plora_slot_module) == 48, \"plora_slot_module layout\");\n"
+        "_Static_assert(sizeof(plora_slot_record) == 24, \"plora_slot_record layout\");\n"
+        "static const fn entry_points[] = {\n" + ",\n".join(f"  (fn){n}" for n in names) + "\n};\n"
+        'int main(void) { printf("%d\\n", (int)(sizeof entry_points / sizeof entry_points[0])); return 0; }\n')
+    out = tmp_path / "caller"
+    res = subprocess.run([cc, "-std=c11", "-Wall", "-Wextra", "-Werror", "-pedantic", f"-I{HEADER.parent}", str(src),
+                          f"-L{lib.parent}", f"-l:{lib.name}", f"-Wl,-rpath,{lib.parent}", "-o", str(out)],
+                         capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+    run = subprocess.run([str(out)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0 and run.stdout.strip() == str(len(names)), run.stderr
