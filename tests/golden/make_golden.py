@@ -12,6 +12,7 @@ the outputs of:
 * ``GpuAdapterCache.ensure_resident`` sequences (cache.py)    -> slot_sequences.json
   (run with PYTHONHASHSEED=0; the script re-executes itself to set it)
 * PEFT parsing + disk manifest (store.py)                     -> peft_store.npz / manifest.json
+* CpuAdapterStore's in-memory LRU sequences (store.py)        -> cpu_lru_sequences.json
 * a tiny DeBERTa ``PolyLoraModel`` CPU forward (model.py)     -> model_tiny.pt
 
 Nothing under tests/ reads the reference at run time; only these files.
@@ -275,11 +276,48 @@ def gen_model_tiny(polylora) -> None:
     }, OUT / "model_tiny.pt")
 
 
+def gen_cpu_lru_sequences(polylora) -> None:
+    """CpuAdapterStore's in-memory LRU (store.py:184-219, 425-436) on seeded
+    random operation sequences: outcome and resident order after each op."""
+    from polylora.store import CpuAdapterStore, CpuLayerWeights
+
+    rng = np.random.default_rng(11)
+    ids = [f"a{i}" for i in range(6)] + ["__base__"]
+    layers = {"m": CpuLayerWeights(torch.ones(4, 2), torch.ones(2, 4), 2, 1.0)}
+    sequences = []
+    for _ in range(60):
+        cap = [None, 1, 2, 3, 4][int(rng.integers(0, 5))]
+        store = CpuAdapterStore(max_adapters=cap)
+        steps = []
+        for _ in range(int(rng.integers(1, 26))):
+            kind = ["add", "get", "touch", "exclude"][int(rng.integers(0, 4))]
+            arg = sorted({ids[int(i)] for i in rng.integers(0, len(ids), int(rng.integers(0, 5)))}) if kind == "exclude" \
+                else ids[int(rng.integers(0, len(ids)))]
+            try:
+                if kind == "add":
+                    store.add_adapter(arg, layers)
+                elif kind == "get":
+                    store.get(arg)
+                elif kind == "touch":
+                    store.touch(arg)
+                else:
+                    store.set_eviction_exclusions(set(arg))
+                outcome = ["ok"]
+            except (KeyError, ValueError, RuntimeError) as exc:
+                outcome = [type(exc).__name__, str(exc)]
+            steps.append({"op": kind, "arg": arg, "outcome": outcome, "resident": list(store.adapters)})
+        sequences.append({"max_adapters": cap, "steps": steps})
+    (OUT / "cpu_lru_sequences.json").write_text(json.dumps(sequences, separators=(",", ":")))
+
+
 def main() -> None:
     src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("POLYLORA_REFERENCE_SRC", "")
     polylora = _import_reference(src)
     if "--slots-only" in sys.argv:
         gen_slot_sequences(polylora)
+        return
+    if "--lru-only" in sys.argv:
+        gen_cpu_lru_sequences(polylora)
         return
     from polylora import layers, sgmv
 
@@ -287,6 +325,7 @@ def main() -> None:
     gen_reference_forward(layers)
     gen_slot_sequences(polylora)
     gen_peft_store(polylora)
+    gen_cpu_lru_sequences(polylora)
     gen_model_tiny(polylora)
     print("golden fixtures written to", OUT)
 

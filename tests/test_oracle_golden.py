@@ -126,3 +126,59 @@ def test_slot_policy_oracle_matches_reference_sequences(golden_dir):
                          capture_output=True, text=True, env=env)
     assert res.returncode == 0, res.stderr + res.stdout
     assert json.loads((golden_dir / "slot_sequences.json").read_text())["hashseed"] == 0
+
+
+def _replay_lru(make, seq):
+    store = make(seq["max_adapters"])
+    for step in seq["steps"]:
+        try:
+            if step["op"] == "add":
+                store.add(step["arg"])
+            elif step["op"] == "get":
+                store.get(step["arg"])
+            elif step["op"] == "touch":
+                store.touch(step["arg"])
+            else:
+                store.exclude(set(step["arg"]))
+            outcome = ["ok"]
+        except (KeyError, ValueError, RuntimeError) as exc:
+            outcome = [type(exc).__name__, str(exc)]
+        assert outcome == step["outcome"], step
+        assert store.resident() == step["resident"], step
+
+
+def test_cpu_lru_oracle_and_store_match_reference_sequences(golden_dir):
+    """The CPU tier's LRU (oracle/store_ref.py, and CpuAdapterStore itself)
+    replays the reference's recorded operation sequences exactly."""
+    import torch
+
+    from oracle.store_ref import CpuLru
+    from polylora_b200.store import CpuAdapterStore, CpuLayerWeights
+
+    layers = {"m": CpuLayerWeights(torch.ones(4, 2), torch.ones(2, 4), 2, 1.0)}
+
+    class OracleView:
+        def __init__(self, cap):
+            self.s = CpuLru(cap)
+            self.add, self.get, self.touch = self.s.add_adapter, self.s.get, self.s.touch
+            self.exclude = self.s.set_eviction_exclusions
+
+        def resident(self):
+            return list(self.s.adapters)
+
+    class StoreView:
+        def __init__(self, cap):
+            self.s = CpuAdapterStore(max_adapters=cap)
+            self.get, self.touch, self.exclude = self.s.get, self.s.touch, self.s.set_eviction_exclusions
+
+        def add(self, a):
+            self.s.add_adapter(a, layers)
+
+        def resident(self):
+            return list(self.s.adapters)
+
+    sequences = json.loads((golden_dir / "cpu_lru_sequences.json").read_text())
+    assert len(sequences) == 60
+    for seq in sequences:
+        _replay_lru(OracleView, seq)
+        _replay_lru(StoreView, seq)
