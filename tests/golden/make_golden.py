@@ -13,6 +13,7 @@ the outputs of:
   (run with PYTHONHASHSEED=0; the script re-executes itself to set it)
 * PEFT parsing + disk manifest (store.py)                     -> peft_store.npz / manifest.json
 * CpuAdapterStore's in-memory LRU sequences (store.py)        -> cpu_lru_sequences.json
+* DiskAdapterCache operation sequences (store.py)             -> disk_sequences.json
 * a tiny DeBERTa ``PolyLoraModel`` CPU forward (model.py)     -> model_tiny.pt
 
 Nothing under tests/ reads the reference at run time; only these files.
@@ -310,6 +311,63 @@ def gen_cpu_lru_sequences(polylora) -> None:
     (OUT / "cpu_lru_sequences.json").write_text(json.dumps(sequences, separators=(",", ":")))
 
 
+DISK_IDS = ["a", "b", "c/d", "e f", "ünï", "__x"]
+
+
+def make_disk_sources(root: Path) -> list[Path]:
+    """Three valid PEFT directories and one without weights."""
+    srcs = []
+    for i in range(4):
+        d = root / f"src{i}"
+        d.mkdir(parents=True, exist_ok=True)
+        (d / "adapter_config.json").write_text(json.dumps({"peft_type": "LORA", "lora_alpha": 4, "r": 2}))
+        if i < 3:
+            (d / "adapter_model.bin").write_bytes(b"weights-%d" % i)
+        srcs.append(d)
+    return srcs
+
+
+def gen_disk_sequences(polylora) -> None:
+    """DiskAdapterCache (store.py:36-148) on seeded random operation sequences:
+    outcome, entry order, directories on disk and manifest text after each op
+    ("reopen" builds a new cache over the same directory)."""
+    from polylora.store import DiskAdapterCache
+
+    rng = np.random.default_rng(12)
+    sequences = []
+    for _ in range(30):
+        cap = [None, 1, 2, 3][int(rng.integers(0, 4))]
+        with tempfile.TemporaryDirectory() as tmp:
+            srcs = make_disk_sources(Path(tmp) / "sources")
+            cache_dir = Path(tmp) / "cache"
+            cache = DiskAdapterCache(cache_dir, max_adapters=cap)
+            steps = []
+            for _ in range(int(rng.integers(1, 16))):
+                kind = ["add", "add", "get", "touch", "reopen"][int(rng.integers(0, 5))]
+                ident = int(rng.integers(0, len(DISK_IDS)))
+                src = int(rng.integers(0, len(srcs)))
+                name = ["default", "other"][int(rng.integers(0, 2))]
+                try:
+                    if kind == "add":
+                        cache.add_adapter(DISK_IDS[ident], srcs[src], name)
+                    elif kind == "get":
+                        cache.get(DISK_IDS[ident])
+                    elif kind == "touch":
+                        cache.touch(DISK_IDS[ident])
+                    else:
+                        cache = DiskAdapterCache(cache_dir, max_adapters=cap)
+                    outcome = ["ok"]
+                except (KeyError, FileNotFoundError, RuntimeError) as exc:
+                    outcome = [type(exc).__name__, str(exc).replace(str(srcs[src]), "<src>")]
+                manifest = cache_dir / "manifest.json"
+                steps.append({"op": kind, "id": ident, "src": src, "name": name, "outcome": outcome,
+                              "entries": list(cache.entries),
+                              "dirs": sorted(p.name for p in cache_dir.iterdir() if p.is_dir()),
+                              "manifest": manifest.read_text() if manifest.exists() else None})
+            sequences.append({"max_adapters": cap, "steps": steps})
+    (OUT / "disk_sequences.json").write_text(json.dumps(sequences, separators=(",", ":")))
+
+
 def main() -> None:
     src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("POLYLORA_REFERENCE_SRC", "")
     polylora = _import_reference(src)
@@ -319,6 +377,9 @@ def main() -> None:
     if "--lru-only" in sys.argv:
         gen_cpu_lru_sequences(polylora)
         return
+    if "--disk-only" in sys.argv:
+        gen_disk_sequences(polylora)
+        return
     from polylora import layers, sgmv
 
     gen_flat_schedule(sgmv)
@@ -326,6 +387,7 @@ def main() -> None:
     gen_slot_sequences(polylora)
     gen_peft_store(polylora)
     gen_cpu_lru_sequences(polylora)
+    gen_disk_sequences(polylora)
     gen_model_tiny(polylora)
     print("golden fixtures written to", OUT)
 

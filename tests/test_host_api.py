@@ -507,3 +507,42 @@ def test_native_packer_declines_hostile_headers(tmp_path):
         assert pack(path) == _native.ERR_UNSUPPORTED, name
         assert bool((image == 0xAB).all()), f"{name}: image written"
     assert pack(tmp_path / "missing.safetensors") == _native.ERR_INVALID_ARGUMENT
+
+
+def test_disk_cache_replays_reference_sequences(tmp_path, golden_dir):
+    """DiskAdapterCache on operation sequences recorded from the reference
+    (adds, invalid sources, gets, touches, reopening from the manifest): the
+    outcome, entry order, directories on disk and manifest text match after
+    every step."""
+    ids = ["a", "b", "c/d", "e f", "ünï", "__x"]
+    sequences = json.loads((golden_dir / "disk_sequences.json").read_text())
+    for n, seq in enumerate(sequences):
+        root = tmp_path / f"s{n}"
+        srcs = []
+        for i in range(4):  # three valid PEFT directories and one without weights
+            d = root / "sources" / f"src{i}"
+            d.mkdir(parents=True)
+            (d / "adapter_config.json").write_text(json.dumps({"peft_type": "LORA", "lora_alpha": 4, "r": 2}))
+            if i < 3:
+                (d / "adapter_model.bin").write_bytes(b"weights-%d" % i)
+            srcs.append(d)
+        cache_dir = root / "cache"
+        cache = DiskAdapterCache(cache_dir, max_adapters=seq["max_adapters"])
+        for step in seq["steps"]:
+            try:
+                if step["op"] == "add":
+                    cache.add_adapter(ids[step["id"]], srcs[step["src"]], step["name"])
+                elif step["op"] == "get":
+                    cache.get(ids[step["id"]])
+                elif step["op"] == "touch":
+                    cache.touch(ids[step["id"]])
+                else:
+                    cache = DiskAdapterCache(cache_dir, max_adapters=seq["max_adapters"])
+                outcome = ["ok"]
+            except (KeyError, FileNotFoundError, RuntimeError) as exc:
+                outcome = [type(exc).__name__, str(exc).replace(str(srcs[step["src"]]), "<src>")]
+            manifest = cache_dir / "manifest.json"
+            assert outcome == step["outcome"], (n, step)
+            assert list(cache.entries) == step["entries"], (n, step)
+            assert sorted(p.name for p in cache_dir.iterdir() if p.is_dir()) == step["dirs"], (n, step)
+            assert (manifest.read_text() if manifest.exists() else None) == step["manifest"], (n, step)
