@@ -94,6 +94,10 @@ def test_product_path_has_no_cpu_fallback():
     with pytest.raises(RuntimeError, match="CUDA"):
         sgmv_lora_a_fwd(x, w, torch.ones(2, dtype=torch.int32), torch.zeros(2, dtype=torch.int64),
                         torch.zeros(3, dtype=torch.int32))
+    from polylora_b200.host_io import HostLoraPipeline
+
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        HostLoraPipeline("cpu")
 
 
 def test_segment_and_slot_fill_limits_rejected_before_cuda(native):
