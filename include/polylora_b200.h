@@ -74,10 +74,30 @@ int plora_device_status(int32_t* status_out, int32_t clear);
  * No counterpart in the reference. */
 int64_t plora_weight_split_tokens_per_sm(int64_t value);
 
+/* Kernel family of rank-16 calls of many tokens (max_rank 16, 16-bit types,
+ * K % 512 == 0 and K <= 4096 for the shrink, N % 512 == 0 and N <= 4096 for
+ * the expand): with value 1 (the default) they stream token rows through
+ * shared memory by bulk copies and keep the slot's weights in registers; with
+ * 0 they use the windowed tensor-core kernels that serve every other rank.
+ * value < 0 only reads.  Returns the previous setting.  Process-wide; the two
+ * families agree within the documented tolerance (fp32 summation order).  No
+ * counterpart in the reference. */
+int32_t plora_stream_kernels(int32_t value);
+
+/* Sets the limit of every bounded pipeline wait on the current device to
+ * limit_ns (default 1 s) and returns the previous one in *previous (if not
+ * null).  A wait that runs out sets PLORA_DEV_WAIT_TIMEOUT, and the kernel
+ * skips its remaining work and returns; with 0, any wait that is not complete
+ * when first polled runs out.  Meant for tests of that path.  Synchronises
+ * the device.  No counterpart in the reference. */
+int plora_set_wait_limit_ns(uint64_t limit_ns, uint64_t* previous);
+
 /* Workspace bytes needed by plora_build_segments, plora_sgmv_a_fwd and
  * plora_sgmv_b_fwd for a batch of num_rows x max_seq tokens over num_slots
  * slots (segment scratch plus, for the *_fwd calls, the table itself).
- * The workspace must be 256-byte aligned. */
+ * The workspace must be 256-byte aligned.  Returns 0 for arguments those
+ * calls reject: negative sizes, num_rows x max_seq beyond INT32_MAX tokens,
+ * num_slots outside [1, 4096]. */
 size_t plora_workspace_size(int64_t num_rows, int64_t max_seq, int32_t num_slots);
 
 /* ---------------------------------------------------------------------------

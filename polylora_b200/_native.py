@@ -82,6 +82,8 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "plora_last_error": (ctypes.c_char_p, []),
     "plora_device_status": (ctypes.c_int, [ctypes.POINTER(_i32), _i32]),
     "plora_weight_split_tokens_per_sm": (_i64, [_i64]),
+    "plora_stream_kernels": (_i32, [_i32]),
+    "plora_set_wait_limit_ns": (ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]),
     "plora_peft_pack": (
         ctypes.c_int,
         [ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p), _i32, ctypes.c_char_p, _i32, ctypes.c_double,
@@ -205,6 +207,20 @@ def weight_split_tokens_per_sm(value: int = -1) -> int:
     """Sets (value >= 0) and returns the previous work-split threshold of the
     tensor-core kernels, in tokens per SM (see plora_weight_split_tokens_per_sm)."""
     return int(load().plora_weight_split_tokens_per_sm(value))
+
+
+def stream_kernels(value: int = -1) -> int:
+    """Enables (1) or disables (0) the rank-16 stream kernels and returns the
+    previous setting; -1 only reads (see plora_stream_kernels)."""
+    return int(load().plora_stream_kernels(value))
+
+
+def set_wait_limit_ns(limit_ns: int) -> int:
+    """Sets the bounded-wait limit of the current device and returns the
+    previous one (see plora_set_wait_limit_ns)."""
+    prev = ctypes.c_uint64(0)
+    check("plora_set_wait_limit_ns", load().plora_set_wait_limit_ns(int(limit_ns), ctypes.byref(prev)))
+    return int(prev.value)
 
 
 def workspace_size(num_rows: int, max_seq: int, num_slots: int) -> int:

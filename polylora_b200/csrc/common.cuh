@@ -21,8 +21,14 @@ __device__ __forceinline__ void raise_status(int bits) { atomicOr(&g_device_stat
 
 // Upper bound of any single pipeline wait.  A correct launch never waits more
 // than microseconds; after this the kernel records PLORA_DEV_WAIT_TIMEOUT and
-// unwinds instead of spinning forever.
+// unwinds instead of spinning forever.  1 s unless plora_set_wait_limit_ns
+// changed it (tests shorten it to make a wait expire; 0 expires every wait
+// that is not already complete when first polled).
 constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
+__device__ uint64_t g_wait_limit_ns = kWaitLimitNs;
+__device__ __forceinline__ uint64_t wait_limit_ns() {
+  return *reinterpret_cast<volatile uint64_t*>(&g_wait_limit_ns);
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -83,20 +89,21 @@ __device__ __forceinline__ bool mbar_try_wait_parked(uint64_t* bar, uint32_t par
 
 // Waits until the phase with the given parity of `bar` has completed.  Gives
 // up when `abort_flag` (shared) is raised by another role or after
-// kWaitLimitNs; on expiry raises the device status and the abort flag.
+// wait_limit_ns(); on expiry raises the device status and the abort flag.
 // Returns false when the caller must unwind.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t limit = wait_limit_ns();
   const uint64_t t0 = global_timer_ns();
   for (;;) {
-    if (mbar_try_wait_parked(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 >= limit) {
       *abort_flag = 1;
       raise_status(PLORA_DEV_WAIT_TIMEOUT);
       return false;
     }
+    if (mbar_try_wait_parked(bar, parity)) return true;
   }
 }
 

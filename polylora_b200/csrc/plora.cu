@@ -14,6 +14,7 @@
 #include "segments.cuh"
 #include "sgmv_simt.cuh"
 #include "sgmv_grid.cuh"
+#include "sgmv_stream.cuh"
 #include "peft_pack.h"
 
 using namespace plora;
@@ -66,6 +67,24 @@ std::mutex g_dev_mu;
 // every CTA stream the whole LoRA weights of each slot it touches).
 std::atomic<int64_t> g_wsplit_tokens_per_sm{16};
 
+// Rank-16 calls of many tokens run the stream kernels (sgmv_stream.cuh) when
+// this is non-zero (the default); 0 keeps them on the windowed mma kernels.
+std::atomic<int32_t> g_stream_kernels{1};
+
+// A CTA's share of the token list (at most ceil(num_tokens / SMs)) must fit
+// the stream kernels' shared-memory copy of its token ids.
+bool stream_share_ok(int64_t num_tokens, const DeviceInfo* di) {
+  return (num_tokens + di->sm_count - 1) / di->sm_count <= kStreamMaxShare;
+}
+bool stream_shrink_ok(int64_t R, int64_t K, int64_t num_tokens, const DeviceInfo* di) {
+  return g_stream_kernels.load(std::memory_order_relaxed) != 0 && R == kStreamRank && K % 512 == 0 &&
+         K <= kStreamMaxDim && stream_share_ok(num_tokens, di);
+}
+bool stream_expand_ok(int64_t R, int64_t N, int64_t num_tokens, const DeviceInfo* di) {
+  return g_stream_kernels.load(std::memory_order_relaxed) != 0 && R == kStreamRank && N % 512 == 0 &&
+         N <= kStreamMaxDim && stream_share_ok(num_tokens, di);
+}
+
 bool use_weight_split(int64_t num_tokens, const DeviceInfo* di) {
   return num_tokens <= g_wsplit_tokens_per_sm.load(std::memory_order_relaxed) * di->sm_count;
 }
@@ -117,6 +136,10 @@ int device_info(DeviceInfo** out) {
     SET_GRID_ALL(32)
     SET_GRID_ALL(64)
 #undef SET_GRID_ALL
+    SET_GRID((sgmv_shrink_stream_kernel<true>), kStreamSmemLimit)
+    SET_GRID((sgmv_shrink_stream_kernel<false>), kStreamSmemLimit)
+    SET_GRID((sgmv_expand_stream_kernel<true>), kStreamSmemLimit)
+    SET_GRID((sgmv_expand_stream_kernel<false>), kStreamSmemLimit)
 #undef SET_GRID
     d.attrs_set = true;
   }
@@ -203,6 +226,12 @@ struct FwdWorkspace {
   int32_t* token_index;
 };
 
+// num_rows x max_seq token ids fit in int32 (checked before any product is formed).
+bool token_count_ok(int64_t num_rows, int64_t max_seq) {
+  if (num_rows < 0 || max_seq < 0) return false;
+  return max_seq == 0 || num_rows <= (int64_t)INT32_MAX / max_seq;
+}
+
 size_t fwd_workspace_bytes(int64_t num_rows, int64_t max_seq, int32_t num_slots) {
   return seg_workspace_bytes(num_rows, num_slots) + align256((size_t)(num_slots + 1) * 4) +
          align256((size_t)(num_rows * max_seq) * 4);
@@ -215,7 +244,7 @@ int build_segments(const int64_t* wi, const int32_t* seq_lens, const int32_t* ra
     return fail(PLORA_ERR_UNSUPPORTED, "num_slots %d outside [1, %d]", num_slots, kSegMaxSlots);
   if (num_rows < 0 || max_seq < 0)
     return fail(PLORA_ERR_INVALID_ARGUMENT, "negative num_rows/max_seq");
-  if (num_rows * max_seq > (int64_t)INT32_MAX)
+  if (!token_count_ok(num_rows, max_seq))
     return fail(PLORA_ERR_UNSUPPORTED, "num_rows*max_seq exceeds int32 token ids");
   if (!slot_start) return fail(PLORA_ERR_INVALID_ARGUMENT, "slot_start is null");
   if (num_rows == 0 || max_seq == 0) {
@@ -331,6 +360,17 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
 #undef LAUNCH_SHRINK_GRID
       return check_launch("sgmv_shrink_grid_kernel");
     }
+    if (stream_shrink_ok(R, K, num_tokens, di)) {  // rank 16: rows through a bulk-copy ring, A in registers
+      const StreamPlan plan = shrink_stream_plan(K, seg.num_slots);
+      if (plan.nst >= 2) {
+        // the kernel reads its inputs only after griddep_wait(): always launched programmatically
+        PLORA_CUDA(launch_kernel(bf ? sgmv_shrink_stream_kernel<true> : sgmv_shrink_stream_kernel<false>,
+                                 dim3(di->sm_count), dim3(kStreamThreads), plan.smem_bytes, stream, true, 0,
+                                 args, plan),
+                   "launch sgmv_shrink_stream_kernel");
+        return check_launch("sgmv_shrink_stream_kernel");
+      }
+    }
     CUtensorMap map8, map1;
     const CUtensorMapSwizzle swz = R == 16   ? CU_TENSOR_MAP_SWIZZLE_32B
                                    : R == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
@@ -405,6 +445,19 @@ int expand_impl(const void* tmp, const void* b, void* y, const int32_t* ranks, c
       }
 #undef LAUNCH_EXPAND_GRID
       return check_launch("sgmv_expand_grid_kernel");
+    }
+    if (stream_expand_ok(R, N, num_tokens, di)) {  // rank 16: rows through a bulk-copy ring, B in registers
+      const StreamPlan plan = expand_stream_plan(N, seg.num_slots);
+      if (plan.smem_bytes <= (uint32_t)kStreamSmemLimit) {
+        // programmatic only right after this library's shrink (after_shrink): the kernel
+        // reads the segment table and LoRA-B before griddep_wait(), tmp after it; y is
+        // only added to, after tmp
+        PLORA_CUDA(launch_kernel(bf ? sgmv_expand_stream_kernel<true> : sgmv_expand_stream_kernel<false>,
+                                 dim3(di->sm_count), dim3(kStreamThreads), plan.smem_bytes, stream,
+                                 after_shrink, 0, args, plan),
+                   "launch sgmv_expand_stream_kernel");
+        return check_launch("sgmv_expand_stream_kernel");
+      }
     }
     CUtensorMap mapn, map1;
     const uint32_t box = R == 16 ? ExpandMmaCfg<16>::kBoxChunks
@@ -488,6 +541,20 @@ int64_t plora_weight_split_tokens_per_sm(int64_t value) {
   return value >= 0 ? g_wsplit_tokens_per_sm.exchange(value) : g_wsplit_tokens_per_sm.load();
 }
 
+int32_t plora_stream_kernels(int32_t value) {
+  return value >= 0 ? g_stream_kernels.exchange(value ? 1 : 0) : g_stream_kernels.load();
+}
+
+int plora_set_wait_limit_ns(uint64_t limit_ns, uint64_t* previous) {
+  g_last_error.clear();
+  uint64_t old = 0;
+  PLORA_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  PLORA_CUDA(cudaMemcpyFromSymbol(&old, g_wait_limit_ns, sizeof(old)), "read wait limit");
+  PLORA_CUDA(cudaMemcpyToSymbol(g_wait_limit_ns, &limit_ns, sizeof(limit_ns)), "set wait limit");
+  if (previous) *previous = old;
+  return PLORA_OK;
+}
+
 int plora_device_status(int32_t* status_out, int32_t clear) {
   int v = 0;
   PLORA_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
@@ -501,7 +568,7 @@ int plora_device_status(int32_t* status_out, int32_t clear) {
 }
 
 size_t plora_workspace_size(int64_t num_rows, int64_t max_seq, int32_t num_slots) {
-  if (num_rows < 0 || max_seq < 0 || num_slots < 1) return 0;
+  if (!token_count_ok(num_rows, max_seq) || num_slots < 1 || num_slots > kSegMaxSlots) return 0;
   return fwd_workspace_bytes(num_rows, max_seq, num_slots);
 }
 
@@ -598,6 +665,9 @@ int plora_sgmv_a_fwd(const void* x, const void* lora_a, void* tmp, const int32_t
   g_last_error.clear();
   int st = check_common(dtype, num_slots, max_rank);
   if (st) return st;
+  if (!token_count_ok(num_rows, max_seq))
+    return fail(PLORA_ERR_UNSUPPORTED, "num_rows %lld x max_seq %lld: negative or beyond int32 token ids",
+                (long long)num_rows, (long long)max_seq);
   if (num_rows == 0 || max_seq == 0) return PLORA_OK;  // sgmv.py:159-160
   const size_t need = fwd_workspace_bytes(num_rows, max_seq, num_slots);
   if (!workspace || workspace_size < need)
@@ -620,6 +690,9 @@ int plora_sgmv_b_fwd(const void* tmp, const void* lora_b, void* y, const int32_t
   g_last_error.clear();
   int st = check_common(dtype, num_slots, max_rank);
   if (st) return st;
+  if (!token_count_ok(num_rows, max_seq))
+    return fail(PLORA_ERR_UNSUPPORTED, "num_rows %lld x max_seq %lld: negative or beyond int32 token ids",
+                (long long)num_rows, (long long)max_seq);
   if (num_rows == 0 || max_seq == 0) return PLORA_OK;  // sgmv.py:314-315
   const size_t need = fwd_workspace_bytes(num_rows, max_seq, num_slots);
   if (!workspace || workspace_size < need)
@@ -663,23 +736,58 @@ int plora_slot_fill(const plora_slot_module* modules, int32_t num_modules, int32
   return check_launch("slot_fill_kernel");
 }
 
-// Device address of g_noalloc_scratch, looked up once per device with that
-// device current (the first plora_sgmv_a_fwd_noalloc call on the device).
+// Device address of g_noalloc_scratch, looked up once per device and CUDA
+// context with that device current (the first plora_sgmv_a_fwd_noalloc call
+// there).  The cache is keyed on the context's unique id: after
+// cudaDeviceReset the module is loaded again in a new context, and the array
+// may live at another address.
 namespace {
-void* g_noalloc_ptr[kMaxDevices] = {};
+struct NoallocScratch {
+  unsigned long long ctx_id = 0;
+  void* ptr = nullptr;
+};
+NoallocScratch g_noalloc[kMaxDevices];
 std::mutex g_noalloc_mu;
+
+// Unique id of the calling thread's current CUDA context (0 if unavailable).
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
 
 int noalloc_scratch(void** out) {
   int dev = 0;
   PLORA_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(PLORA_ERR_UNSUPPORTED, "device ordinal %d", dev);
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  NoallocScratch& e = g_noalloc[dev];
+  const unsigned long long id = current_context_id();  // 0 before the runtime set one up
+  if (!e.ptr || id == 0 || e.ctx_id != id) {
     void* p = nullptr;
+    // also makes the runtime's context for `dev` current on this thread
     PLORA_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(noalloc scratch)");
-    g_noalloc_ptr[dev] = p;
+    e.ptr = p;
+    e.ctx_id = current_context_id();
   }
-  *out = g_noalloc_ptr[dev];
+  *out = e.ptr;
   return PLORA_OK;
 }
 }  // namespace
@@ -694,6 +802,9 @@ extern "C" int plora_sgmv_a_fwd_noalloc(const void* x, const void* lora_a, void*
   int st = check_common(dtype, num_slots, max_rank);
   if (st) return st;
   if (num_rows < 0 || max_seq < 0) return fail(PLORA_ERR_INVALID_ARGUMENT, "negative num_rows/max_seq");
+  if (!token_count_ok(num_rows, max_seq))
+    return fail(PLORA_ERR_UNSUPPORTED, "num_rows %lld x max_seq %lld exceeds int32 token ids",
+                (long long)num_rows, (long long)max_seq);
   if (num_rows == 0 || max_seq == 0) return PLORA_OK;
   const size_t need = fwd_workspace_bytes(num_rows, max_seq, num_slots);
   if (need > (size_t)PLORA_NOALLOC_SCRATCH_BYTES)

@@ -19,15 +19,19 @@ pytestmark = pytest.mark.gpu
 TOL = {"bfloat16": 2e-2, "float16": 2e-2, "float32": 1e-5}
 
 
-@pytest.fixture(params=["token_split", "weight_split"])
+@pytest.fixture(params=["stream", "token_split", "weight_split"])
 def split_mode(request):
-    """Runs the test under each work split of the tensor-core kernels: every
-    CTA a share of the tokens, or each slot's weights spread over the grid."""
+    """Runs the test under each kernel family of the tensor-core path: every
+    CTA a share of the tokens, with rank-16 calls on the stream kernels (rows
+    by bulk copies, weights in registers) or on the windowed kernels; or each
+    slot's weights spread over the grid (slot grid)."""
     from polylora_b200 import _native
 
-    prev = _native.weight_split_tokens_per_sm(0 if request.param == "token_split" else 1 << 40)
+    prev = _native.weight_split_tokens_per_sm(1 << 40 if request.param == "weight_split" else 0)
+    prev_stream = _native.stream_kernels(0 if request.param == "token_split" else 1)
     yield request.param
     _native.weight_split_tokens_per_sm(prev)
+    _native.stream_kernels(prev_stream)
 TORCH = {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}
 
 
