@@ -187,16 +187,21 @@ class GpuAdapterCache:
         # the copy reading it has been recorded (note_image_use)
         lock = getattr(self.store, "locked", None)
         with lock() if lock is not None else contextlib.nullcontext():
-            adapter = self.store.get(adapter_id)
+            # A failure anywhere before the slot is filled (the CPU or disk tier
+            # cannot produce the adapter, its weights do not fit the modules, its
+            # image cannot be built) leaves the slot free with rank 0 and scale 0
+            # in every module, the state the reference's zero-on-evict leaves
+            # (cache.py:97-150), and the error propagates.
             try:
+                adapter = self.store.get(adapter_id)
                 self._validate(adapter_id, adapter)
-            except ValueError:
+                if self.device.type == "cuda":
+                    self._fill_slot_native(adapter_id, slot)
+                else:
+                    self._fill_slot_host(adapter, slot)
+            except BaseException:
                 self._clear_slot(slot)
                 raise
-            if self.device.type == "cuda":
-                self._fill_slot_native(adapter_id, slot)
-            else:
-                self._fill_slot_host(adapter, slot)
             self.adapter_to_slot[adapter_id] = slot
             self.slot_to_adapter[slot] = adapter_id
             self._touch(adapter_id)

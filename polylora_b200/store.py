@@ -39,6 +39,38 @@ from ._native import SlotRecord
 _SUPPORTED_OPTIONS = ("use_dora", "lora_bias", "use_rslora")
 
 
+def _load_safetensors(path: Path) -> dict[str, torch.Tensor]:
+    try:
+        from safetensors.torch import load_file
+    except ImportError as exc:
+        raise ImportError("safetensors is required to load adapter_model.safetensors") from exc
+    return load_file(str(path), device="cpu")
+
+
+def _load_torch_bin(path: Path) -> dict[str, torch.Tensor]:
+    return torch.load(path, map_location="cpu")
+
+
+_PEFT_WEIGHT_FILES = (("adapter_model.safetensors", _load_safetensors), ("adapter_model.bin", _load_torch_bin))
+
+# adapter_config.json rules, checked in this order: (refuses the config, error message)
+_CONFIG_RULES = (
+    (lambda c: c.get("peft_type") not in (None, "LORA"), lambda c: f"Unsupported PEFT adapter type: {c.get('peft_type')!r}"),
+    (lambda c: bool(c.get("use_dora", False)), lambda c: "DoRA adapters are not supported"),
+    (lambda c: bool(c.get("use_rslora", False)), lambda c: "RS-LoRA adapters are not supported"),
+    (lambda c: bool(c.get("lora_bias", False)), lambda c: "LoRA bias is not supported"),
+    (lambda c: float(c.get("lora_dropout", 0.0)) != 0.0, lambda c: "LoRA dropout is not supported by the inference runtime"),
+    (lambda c: "lora_alpha" not in c, lambda c: "adapter_config.json is missing lora_alpha"),
+)
+
+
+def _capacity(max_adapters: int | None) -> int | None:
+    """An LRU tier's bound: None (unbounded) or a positive count."""
+    if max_adapters is None or max_adapters >= 1:
+        return max_adapters
+    raise ValueError("max_adapters must be at least 1")
+
+
 @dataclass(frozen=True)
 class CpuLayerWeights:
     A: torch.Tensor  # (in_features, rank)
@@ -72,15 +104,14 @@ class DiskAdapterCache:
     _MANIFEST_NAME = "manifest.json"
 
     def __init__(self, cache_dir: str | Path, max_adapters: int | None = None) -> None:
-        if max_adapters is not None and max_adapters < 1:
-            raise ValueError("max_adapters must be at least 1")
+        # entries in LRU order (most recent last); the manifest on disk mirrors them
+        self.max_adapters = _capacity(max_adapters)
         self.cache_dir = Path(cache_dir)
-        self.max_adapters = max_adapters
-        self.cache_dir.mkdir(parents=True, exist_ok=True)
         self.entries: OrderedDict[str, DiskAdapterEntry] = OrderedDict()
         self._json_blocks: dict[str, str] = {}  # adapter_id -> its manifest entry, serialised
+        self.cache_dir.mkdir(parents=True, exist_ok=True)
         self._load_manifest()
-        self._evict_if_needed()
+        self._evict_if_needed()  # a manifest written under a larger bound
 
     def __contains__(self, adapter_id: str) -> bool:
         return adapter_id in self.entries
@@ -90,15 +121,19 @@ class DiskAdapterCache:
         return self.cache_dir / self._MANIFEST_NAME
 
     def get(self, adapter_id: str) -> DiskAdapterEntry:
-        if adapter_id not in self.entries:
+        """The entry of a registered adapter, which becomes the most recently used."""
+        entry = self.entries.get(adapter_id)
+        if entry is None:
             raise KeyError(f"Unknown disk LoRA adapter id: {adapter_id}")
         self.touch(adapter_id)
-        return self.entries[adapter_id]
+        return entry
 
     def touch(self, adapter_id: str) -> None:
-        if adapter_id in self.entries:
-            self.entries.move_to_end(adapter_id)
-            self._write_manifest()
+        """Marks an entry most recently used; unknown ids are ignored."""
+        if adapter_id not in self.entries:
+            return
+        self.entries.move_to_end(adapter_id)
+        self._write_manifest()
 
     def add_adapter(self, adapter_id: str, adapter_path: str | Path, peft_adapter_name: str = "default") -> Path:
         source = Path(adapter_path)
@@ -278,12 +313,12 @@ class CpuAdapterStore:
         module_names: list[str] | None = None,
         prefetch_workers: int | None = None,
     ) -> None:
-        if max_adapters is not None and max_adapters < 1:
-            raise ValueError("max_adapters must be at least 1")
+        self.max_adapters = _capacity(max_adapters)
         self.base_adapter_id = base_adapter_id
-        self.max_adapters = max_adapters
         self.disk_cache = disk_cache
         self.module_names = module_names
+        # resident adapters in LRU order (most recent last), and the ids the GPU
+        # tier holds, which this tier must not evict
         self.adapters: OrderedDict[str, CpuAdapter] = OrderedDict()
         self.eviction_exclusions: set[str] = set()
         self._images: dict[tuple, tuple[torch.Tensor, list]] = {}
@@ -504,19 +539,16 @@ class CpuAdapterStore:
         module_names: list[str],
         peft_adapter_name: str | None = None,
     ) -> None:
+        # the PEFT model names its adapters; ours default to the same name
         name = peft_adapter_name or adapter_id
-        adapter_config = getattr(peft_model, "peft_config", {}).get(name)
-        if adapter_config is None:
+        configs = getattr(peft_model, "peft_config", {})
+        if name not in configs or configs[name] is None:
             raise ValueError(f"PEFT model does not contain adapter {name!r}")
-        self._validate_peft_config(adapter_config)
-        self.add_adapter_from_peft_state_dict(
-            adapter_id=adapter_id,
-            state_dict=peft_model.state_dict(),
-            module_names=module_names,
-            lora_alpha=float(getattr(adapter_config, "lora_alpha")),
-            peft_adapter_name=name,
-            config=self._config_to_dict(adapter_config),
-        )
+        peft_cfg = configs[name]
+        self._validate_peft_config(peft_cfg)
+        alpha = float(getattr(peft_cfg, "lora_alpha"))
+        self.add_adapter_from_peft_state_dict(adapter_id, peft_model.state_dict(), module_names, alpha,
+                                              peft_adapter_name=name, config=self._config_to_dict(peft_cfg))
 
     def load_adapter_from_disk(
         self,
@@ -629,15 +661,9 @@ class CpuAdapterStore:
         module_names: list[str],
         peft_adapter_name: str = "default",
     ) -> None:
-        config, state_dict = self._read_peft_dir(Path(adapter_path))
-        self.add_adapter_from_peft_state_dict(
-            adapter_id=adapter_id,
-            state_dict=state_dict,
-            module_names=module_names,
-            lora_alpha=float(config["lora_alpha"]),
-            peft_adapter_name=peft_adapter_name,
-            config=config,
-        )
+        config, weights = self._read_peft_dir(Path(adapter_path))
+        self.add_adapter_from_peft_state_dict(adapter_id, weights, module_names, float(config["lora_alpha"]),
+                                              peft_adapter_name=peft_adapter_name, config=config)
 
     def _read_peft_dir(self, adapter_path: Path) -> tuple[dict[str, Any], dict[str, torch.Tensor]]:
         """Validated adapter_config.json and the weights of a PEFT directory."""
@@ -668,45 +694,38 @@ class CpuAdapterStore:
 
     @staticmethod
     def _load_peft_state_dict(adapter_path: Path) -> dict[str, torch.Tensor]:
-        st_path = adapter_path / "adapter_model.safetensors"
-        bin_path = adapter_path / "adapter_model.bin"
-        if st_path.exists():
-            try:
-                from safetensors.torch import load_file
-            except ImportError as exc:
-                raise ImportError("safetensors is required to load adapter_model.safetensors") from exc
-            return load_file(str(st_path), device="cpu")
-        if bin_path.exists():
-            return torch.load(bin_path, map_location="cpu")
+        """The adapter's weights: adapter_model.safetensors if present, else
+        adapter_model.bin (the order PEFT's own loader prefers)."""
+        for filename, load in _PEFT_WEIGHT_FILES:
+            path = adapter_path / filename
+            if path.exists():
+                return load(path)
         raise FileNotFoundError(f"No PEFT adapter weights found in {adapter_path}")
 
     @staticmethod
     def _validate_peft_config(config: Any) -> None:
-        for name in _SUPPORTED_OPTIONS:
-            if hasattr(config, name) and getattr(config, name) != False:  # noqa: E712
-                raise ValueError(f"Unsupported PEFT LoRA option: {name}={getattr(config, name)!r}")
+        """A PEFT LoraConfig object: the options the runtime cannot apply are refused."""
+        for option in _SUPPORTED_OPTIONS:
+            value = getattr(config, option, False)
+            if value != False:  # noqa: E712  (the reference compares with != False)
+                raise ValueError(f"Unsupported PEFT LoRA option: {option}={value!r}")
         if getattr(config, "lora_dropout", 0.0) not in (0, 0.0):
             raise ValueError("LoRA dropout is not supported by the inference runtime")
 
     @staticmethod
     def _validate_peft_config_dict(config: dict[str, Any]) -> None:
-        if config.get("peft_type") not in (None, "LORA"):
-            raise ValueError(f"Unsupported PEFT adapter type: {config.get('peft_type')!r}")
-        for key, label in (("use_dora", "DoRA adapters"), ("use_rslora", "RS-LoRA adapters"), ("lora_bias", "LoRA bias")):
-            if config.get(key, False):
-                raise ValueError(f"{label} {'is' if key == 'lora_bias' else 'are'} not supported")
-        if float(config.get("lora_dropout", 0.0)) != 0.0:
-            raise ValueError("LoRA dropout is not supported by the inference runtime")
-        if "lora_alpha" not in config:
-            raise ValueError("adapter_config.json is missing lora_alpha")
+        """adapter_config.json: the first failing rule of _CONFIG_RULES raises."""
+        for refused, message in _CONFIG_RULES:
+            if refused(config):
+                raise ValueError(message(config))
 
     @staticmethod
     def _config_to_dict(config: Any) -> dict[str, Any]:
-        if hasattr(config, "to_dict"):
-            return dict(config.to_dict())
-        if hasattr(config, "__dict__"):
-            return dict(config.__dict__)
-        return {}
+        """A plain dict of a PEFT config object (to_dict() when it has one)."""
+        to_dict = getattr(config, "to_dict", None)
+        if to_dict is not None:
+            return dict(to_dict())
+        return dict(vars(config)) if hasattr(config, "__dict__") else {}
 
     # ------------------------------------------------------------------ GPU refill images
     def slot_image(self, adapter_id: str, module_names: list[str], dtype: torch.dtype) -> tuple[torch.Tensor, list]:

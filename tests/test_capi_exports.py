@@ -146,3 +146,37 @@ def test_header_is_plain_c_and_links(tmp_path, native):
     assert res.returncode == 0, res.stderr
     run = subprocess.run([str(out)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0 and run.stdout.strip() == str(len(names)), run.stderr
+
+
+@pytest.mark.parametrize("rows,seq", [(1 << 18, 1 << 46), (1 << 40, 1 << 30), (3, -1), (-2, 5), (1 << 31, 1)])
+def test_token_count_overflow_rejected_before_cuda(native, rows, seq):
+    """num_rows x max_seq that overflows int64 (e.g. 2^18 x 2^46 wraps to 0), is
+    negative, or exceeds int32 token ids is refused by every entry point that
+    sizes scratch from it, before any CUDA call: no scratch carve can then run
+    past its buffer."""
+    lib = native.load()
+    dummy = 0x1000
+    assert native.workspace_size(rows, seq, 65) == 0
+    st = lib.plora_sgmv_a_fwd_noalloc(dummy, dummy, dummy, dummy, dummy, dummy, rows, seq, 64, 16, 65, 1,
+                                      native.DTYPE_BF16, None)
+    assert st in (native.ERR_UNSUPPORTED, native.ERR_INVALID_ARGUMENT), native.last_error()
+    st = lib.plora_sgmv_a_fwd(dummy, dummy, dummy, dummy, dummy, dummy, rows, seq, 64, 16, 65, 1,
+                              native.DTYPE_BF16, dummy, 1 << 30, None)
+    assert st in (native.ERR_UNSUPPORTED, native.ERR_INVALID_ARGUMENT), native.last_error()
+    st = lib.plora_sgmv_b_fwd(dummy, dummy, dummy, dummy, dummy, dummy, dummy, rows, seq, 16, 64, 65,
+                              native.DTYPE_BF16, dummy, 1 << 30, None)
+    assert st in (native.ERR_UNSUPPORTED, native.ERR_INVALID_ARGUMENT), native.last_error()
+    st = lib.plora_build_segments(dummy, dummy, dummy, rows, seq, 65, dummy, dummy, dummy, 1 << 30, None)
+    assert st in (native.ERR_UNSUPPORTED, native.ERR_INVALID_ARGUMENT), native.last_error()
+
+
+def test_stream_kernel_switch_round_trips(native):
+    prev = native.stream_kernels()
+    try:
+        assert prev in (0, 1)
+        assert native.stream_kernels(0) == prev
+        assert native.stream_kernels() == 0
+        assert native.stream_kernels(5) == 0  # any non-zero value enables
+        assert native.stream_kernels() == 1
+    finally:
+        native.stream_kernels(prev)
