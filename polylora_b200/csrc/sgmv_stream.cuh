@@ -24,7 +24,8 @@
 //    the partials of the group just published.
 //  * expand: warp w owns N columns [w N/16, (w + 1) N/16).  Per group of 8
 //    tokens it computes delta = tmp B for its columns (mma.sync with the tmp
-//    rows, which arrive by cp.async, as A fragments), rounds scale * delta to
+//    rows as A fragments; the share's tmp rows are gathered into shared
+//    memory by cp.async once, at the start), rounds scale * delta to
 //    the activation type, regroups the fragments so that each lane holds 8
 //    consecutive columns of one row (stmatrix into a per-warp tile), and
 //    adds them to y with `red.global.add.noftz.v4.{bf16x2,f16x2}`: the L2
@@ -35,9 +36,12 @@
 // there is no producer role.  Work split: a CTA per SM takes a contiguous
 // share of the slot-ordered token list (its token ids are copied to shared
 // memory once, so no global load sits between a stage landing and its
-// refill), cut into groups of <= 8 tokens of one slot.  Every wait is
-// bounded; after an expiry or an abort the warps leave their loops, and
-// thread 0 waits (bounded) for the loads already issued before the CTA exits.
+// refill), cut into groups of <= 8 tokens of one slot.  At the start the
+// slot table is read first, so that the first weight stages are issued one
+// global round trip after launch, while the token ids are still on their way.
+// Every wait is bounded; after an expiry or an abort the warps leave their
+// loops, and thread 0 waits (bounded) for the loads already issued before the
+// CTA exits.
 //
 // Reference semantics: src/polylora/sgmv.py:63-138 (_sgmv_lora_a_kernel) and
 // sgmv.py:178-275 (_sgmv_lora_b_kernel).
@@ -60,23 +64,23 @@ constexpr int kStreamWeightParts = 2;      // weight stages per slot
 constexpr int kStreamMaxShare = 1024;
 constexpr int kShrinkPartBufs = 3;                                     // partial buffers in flight
 constexpr int kShrinkPartBytes = kStreamWarps * 32 * 16;               // one group's 16 partials
-constexpr int kExpandTmpSlots = 16;                                    // tmp-row slots in flight
-constexpr int kExpandTmpBytes = kStreamGroup * kStreamRank * 2;        // one group's tmp rows
+constexpr int kShrinkTmpTileBytes = kStreamWarps * kStreamGroup * kStreamRank * 2;  // per warp: a group's tmp rows
+constexpr int kExpandTmpRowBytes = kStreamRank * 2;                    // one token's tmp row
 constexpr int kExpandRegroupBytes = kStreamWarps * kStreamGroup * 64;  // per warp 8 rows x 32 columns
 
 // Shared-memory plan of a stream kernel (host and device alike), offsets from
 // the 128-byte aligned base:
-//   shrink: [nst token/weight stages][3 partial buffers][barriers][token ids][slot table]
-//   expand: [2 weight stages][16 tmp-row slots][regroup tiles][barriers][token ids][slot table]
+//   shrink: [nst token/weight stages][3 partial buffers][tmp tiles][barriers][token ids][slot table]
+//   expand: [2 weight stages][tmp rows of the share][regroup tiles][barriers][token ids][slot table]
 // Barrier area: per stage / slot an mbarrier (8 B), a release count and the
 // index of the last item loaded (4 B each); then 6 more mbarriers (the
 // shrink's partial hand-off) and the abort flag.
 struct StreamPlan {
-  int nst;               // shrink: ring stages; expand: tmp-row slots
+  int nst;               // shrink: ring stages; expand: weight stages
   uint32_t pitch;        // token / weight row pitch in a stage
   uint32_t stage_bytes;  // 8 rows
-  uint32_t aux_off;      // shrink: partial buffers; expand: tmp-row slots
-  uint32_t rg_off;       // expand: regroup tiles
+  uint32_t aux_off;      // shrink: partial buffers; expand: the share's tmp rows
+  uint32_t rg_off;       // regroup tiles (shrink: tmp rows of a group; expand: delta columns)
   uint32_t bar_off, tok_off, tab_off;
   uint32_t smem_bytes;   // dynamic shared memory to request (includes 128 B of alignment slack)
 };
@@ -88,13 +92,14 @@ __host__ __device__ inline StreamPlan shrink_stream_plan(int64_t K, int64_t num_
   p.pitch = (uint32_t)(K * 2 + 16);
   p.stage_bytes = p.pitch * kStreamGroup;
   const int64_t tab = slot_tab_bytes(num_slots);
-  const int64_t fixed = 128 + kShrinkPartBufs * kShrinkPartBytes + stream_bar_bytes(0) + kStreamMaxShare * 4 + tab;
+  const int64_t fixed =
+      128 + kShrinkPartBufs * kShrinkPartBytes + kShrinkTmpTileBytes + stream_bar_bytes(0) + kStreamMaxShare * 4 + tab;
   int64_t nst = (kStreamSmemLimit - fixed) / ((int64_t)p.stage_bytes + 16);
   if (nst > kStreamMaxStages) nst = kStreamMaxStages;
   p.nst = (int)nst;
   p.aux_off = (uint32_t)(nst * p.stage_bytes);
   p.rg_off = p.aux_off + kShrinkPartBufs * kShrinkPartBytes;
-  p.bar_off = p.rg_off;
+  p.bar_off = p.rg_off + kShrinkTmpTileBytes;
   p.tok_off = p.bar_off + stream_bar_bytes(p.nst);
   p.tab_off = p.tok_off + kStreamMaxShare * 4;
   p.smem_bytes = (uint32_t)(128 + p.tab_off + tab);
@@ -103,13 +108,13 @@ __host__ __device__ inline StreamPlan shrink_stream_plan(int64_t K, int64_t num_
 
 __host__ __device__ inline StreamPlan expand_stream_plan(int64_t N, int64_t num_slots) {
   StreamPlan p;
-  p.nst = kExpandTmpSlots;
+  p.nst = kStreamWeightParts;
   p.pitch = (uint32_t)(N * 2 + 16);
   p.stage_bytes = p.pitch * kStreamGroup;
   p.aux_off = kStreamWeightParts * p.stage_bytes;
-  p.rg_off = p.aux_off + kExpandTmpSlots * kExpandTmpBytes;
+  p.rg_off = p.aux_off + kStreamMaxShare * kExpandTmpRowBytes;
   p.bar_off = p.rg_off + kExpandRegroupBytes;
-  p.tok_off = p.bar_off + stream_bar_bytes(kStreamWeightParts + kExpandTmpSlots);
+  p.tok_off = p.bar_off + stream_bar_bytes(kStreamWeightParts);
   p.tab_off = p.tok_off + kStreamMaxShare * 4;
   p.smem_bytes = (uint32_t)(128 + p.tab_off + slot_tab_bytes(num_slots));
   return p;
@@ -337,13 +342,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const int lane = threadIdx.x & 31;
   griddep_wait();    // inputs (segment table, x) come from earlier kernels
   griddep_launch();  // the expand may start on SMs this grid releases
-  const int64_t total = ld_cg_i32(args.seg.slot_start + args.seg.num_slots);
-  const int64_t begin = total * blockIdx.x / gridDim.x;
-  const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
-  if (begin >= end) return;  // uniform across the CTA
-
   const SlotTab tab = stage_slot_tab(args.seg, args.ranks, nullptr, tab_mem);
-  stream_stage_tokens(args.seg.token_index, begin, end, tok_s);
   if (threadIdx.x == 0) {
     ring.init();
     for (int i = 0; i < kShrinkPartBufs; ++i) {
@@ -353,7 +352,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  __syncthreads();
+  __syncthreads();  // slot table staged, barriers initialised
+  const int64_t total = tab.ss[tab.ns];
+  const int64_t begin = total * blockIdx.x / gridDim.x;
+  const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
+  if (begin >= end) return;  // uniform across the CTA
   const uint32_t stage0 = smem_u32(smem);
   const uint32_t row_bytes = (uint32_t)K * 2;
   const uint64_t pol = l2_evict_first_policy();
@@ -376,8 +379,16 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   RingSeq lc;  // load cursor: nst items ahead of consumption; warp 0 issues the first nst
   lc.init(tab, begin, end);
   RingItem q;
-  for (int ii = 0; ii < nst && lc.next(tab, begin, q); ++ii)
-    if (warp == 0) issue(ii, q);
+  {
+    // weight stages first (they need only the table), token stages once the ids are staged
+    RingSeq pre = lc;
+    for (int ii = 0; ii < nst && pre.next(tab, begin, q); ++ii)
+      if (warp == 0 && q.part >= 0) issue(ii, q);
+    stream_stage_tokens(args.seg.token_index, begin, end, tok_s);
+    __syncthreads();
+    for (int ii = 0; ii < nst && lc.next(tab, begin, q); ++ii)
+      if (warp == 0 && q.part < 0) issue(ii, q);
+  }
 
   const int g = lane >> 2;  // fragment row group
   const int t = lane & 3;   // lane within the quad
@@ -392,6 +403,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const uint32_t w_off = (uint32_t)(kw0 - my_part * (K >> 1) + 8 * (lane >> 4) + (lane & 7)) * 32 +
                          16 * ((lane >> 3) & 1);
   uint16_t* tmp = reinterpret_cast<uint16_t*>(args.tmp);
+  uint16_t* tile = reinterpret_cast<uint16_t*>(smem + plan.rg_off) + warp * kStreamGroup * kStreamRank;
   // Adds the 16 partials of group gi (warp order), rounds and writes its tmp rows.
   auto reduce = [&](int gi, const RingItem& grp) -> bool {
     const int pb = gi % kShrinkPartBufs;
@@ -408,14 +420,20 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&pempty[pb]);
+    // rounded values -> the warp's tile [token][rank]; then lane l writes 16 bytes
+    // (ranks 8 (l & 1) ..) of token l >> 1 with one vector store
     const int n_eff = min(tab.rk[grp.slot] * args.stack_num, args.R);
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
-      if (2 * t + h < grp.cnt) {  // token 2t + h of the group
-        const int64_t row = (int64_t)tok_s[grp.start + 2 * t + h] * args.R;
-        tmp[row + g] = E::from_f(g < n_eff ? v[h] : 0.f);
-        tmp[row + g + 8] = E::from_f(g + 8 < n_eff ? v[2 + h] : 0.f);
-      }
+    for (int h = 0; h < 2; ++h) {
+      tile[(2 * t + h) * kStreamRank + g] = E::from_f(g < n_eff ? v[h] : 0.f);
+      tile[(2 * t + h) * kStreamRank + g + 8] = E::from_f(g + 8 < n_eff ? v[2 + h] : 0.f);
+    }
+    __syncwarp();
+    if (lane < 2 * grp.cnt) {
+      const int64_t row = (int64_t)tok_s[grp.start + (lane >> 1)] * args.R;
+      *reinterpret_cast<uint4*>(tmp + row + 8 * (lane & 1)) = reinterpret_cast<const uint4*>(tile)[lane];
+    }
+    __syncwarp();
     return true;
   };
 
@@ -492,76 +510,61 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 // the reference's rounding order; tokens of rank-0 slots and padding are not
 // touched.  N % 512 == 0, N <= 4096.
 //
-// Two rings: weight stages (B[slot] rank rows 8p .. 8p + 7 at the stage's row
-// pitch; every warp takes the fragments of its columns from both) and
-// tmp-row slots (a group's 8 tmp rows, 32 bytes each, by cp.async).  Items
-// are consumed in the order of RingSeq; each ring is refilled from its own
-// cursor.
+// Weight stages (B[slot] rank rows 8p .. 8p + 7 at the stage's row pitch;
+// every warp takes the fragments of its columns from both) go through a ring
+// of two, refilled from their own cursor; the tmp rows of the whole share are
+// gathered into shared memory once.
 template <bool BF16>
 __global__ void __launch_bounds__(kStreamThreads, 1)
     sgmv_expand_stream_kernel(const ExpandArgs args, const StreamPlan plan) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align128(smem_raw);
   const int N = args.N;
-  StreamRing wring, tring;
+  StreamRing wring;
   wring.carve(smem + plan.bar_off, kStreamWeightParts);
-  tring.carve(smem + plan.bar_off + kStreamWeightParts * 16, kExpandTmpSlots);
-  volatile int* abort_flag =
-      reinterpret_cast<volatile int*>(smem + plan.bar_off + (kStreamWeightParts + kExpandTmpSlots) * 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + plan.bar_off + kStreamWeightParts * 16);
   int32_t* tok_s = reinterpret_cast<int32_t*>(smem + plan.tok_off);
   int32_t* tab_mem = reinterpret_cast<int32_t*>(smem + plan.tab_off);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t total = ld_cg_i32(args.seg.slot_start + args.seg.num_slots);
+  const SlotTab tab = stage_slot_tab(args.seg, args.ranks, args.scales, tab_mem);
+  if (threadIdx.x == 0) {
+    wring.init();
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();  // slot table staged, barriers initialised
+  const int64_t total = tab.ss[tab.ns];
   const int64_t begin = total * blockIdx.x / gridDim.x;
   const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
   if (begin >= end) return;  // uniform across the CTA
 
-  const SlotTab tab = stage_slot_tab(args.seg, args.ranks, args.scales, tab_mem);
-  stream_stage_tokens(args.seg.token_index, begin, end, tok_s);
-  if (threadIdx.x == 0) {
-    wring.init();
-    tring.init();
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  __syncthreads();
   const uint32_t stage0 = smem_u32(smem);
-  const uint32_t tmp0 = stage0 + plan.aux_off;
   const uint32_t row_bytes = (uint32_t)N * 2;
-  const uint32_t tmp_row = (uint32_t)args.R * 2;  // 32 bytes
   const uint64_t pol = l2_evict_first_policy();
   // weight item wi -> weight stage wi % 2
   auto issue_w = [&](int wi, const RingItem& q) {
     ring_issue_weights(wring, wi, args.b + ((int64_t)q.slot * 2 + q.part) * 8 * row_bytes,
                        stage0 + (wi % kStreamWeightParts) * plan.stage_bytes, plan.pitch, row_bytes, pol, lane);
   };
-  // token group ti -> tmp slot ti % 16: two 16-byte halves of each tmp row by cp.async
-  auto issue_t = [&](int ti, const RingItem& q) {
-    const int s = ti % kExpandTmpSlots;
-    if (lane < 2 * q.cnt) {
-      const int64_t tok = tok_s[q.start + (lane >> 1)];
-      cp_async16_cg(tmp0 + s * kExpandTmpBytes + lane * 16, args.tmp + tok * tmp_row + (lane & 1) * 16);
-      cp_async_mbar_arrive(&tring.full[s]);
-    }
-    __syncwarp();
-    if (lane == 0) {
-      tring.loaded[s] = ti;
-      mbar_arrive(&tring.full[s]);
-    }
-  };
-
-  RingSeq lcw, lct;  // load cursors: 2 weight items / 16 token groups ahead
+  RingSeq lcw;  // load cursor of the weight stages, 2 ahead
   lcw.init(tab, begin, end);
-  lct.init(tab, begin, end);
   RingItem q;
   for (int wi = 0; wi < kStreamWeightParts && lcw.next_of(tab, begin, q, true); ++wi)
     if (warp == 0) issue_w(wi, q);
-  // tmp is the previous kernel's output: read only once that grid has completed
+  stream_stage_tokens(args.seg.token_index, begin, end, tok_s);
+  __syncthreads();
+  // tmp is the previous kernel's output: read only once that grid has completed;
+  // every thread gathers 16-byte halves of the share's tmp rows
   griddep_wait();
-  for (int ti = 0; ti < kExpandTmpSlots && lct.next_of(tab, begin, q, false); ++ti)
-    if (warp == 0) issue_t(ti, q);
+  const int share = (int)(end - begin);
+  for (int i = threadIdx.x; i < 2 * share; i += kStreamThreads)
+    cp_async16_cg(stage0 + plan.aux_off + i * 16,
+                  args.tmp + (int64_t)tok_s[i >> 1] * kExpandTmpRowBytes + (i & 1) * 16);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
 
   const int g = lane >> 2;  // fragment row group: token g of the group
   const int t = lane & 3;   // lane within the quad
@@ -580,7 +583,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   int kr = 0;
   RingSeq it;
   it.init(tab, begin, end);
-  int wi = 0, ti = 0;
+  int wi = 0;
   RingItem cq;
   while (it.next(tab, begin, cq)) {
     if (cq.part >= 0) {  // weight stage: rank rows 8 part .. of this warp's columns
@@ -612,13 +615,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     }
     // token group: A fragments from the tmp row of token g (mma rows 8..15 are
     // zero), columns >= kr as zero
-    const int s = ti % kExpandTmpSlots;
-    if (!mbar_wait_warp(&tring.full[s], (uint32_t)(ti / kExpandTmpSlots) & 1u, abort_flag)) break;
     uint32_t fa[4] = {0u, 0u, 0u, 0u};
     const bool vrow = g < cq.cnt;
+    int64_t tok = 0;
     if (vrow) {
       const uint32_t* trow =
-          reinterpret_cast<const uint32_t*>(smem + plan.aux_off + s * kExpandTmpBytes + g * tmp_row);
+          reinterpret_cast<const uint32_t*>(smem + plan.aux_off + (cq.start + g) * kExpandTmpRowBytes);
       auto ld2 = [&](int k) -> uint32_t {
         if (k >= kr) return 0u;
         const uint32_t w = trow[k >> 1];
@@ -626,13 +628,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       };
       fa[0] = ld2(2 * t);
       fa[2] = ld2(2 * t + 8);
+      tok = tok_s[cq.start + g];
     }
-    const int64_t tok = vrow ? (int64_t)tok_s[cq.start + g] : 0;
-    // the tmp slot is free as soon as every warp has its fragments
-    const bool last = tring.release(s, lane);
-    RingItem nq;
-    if (lct.next_of(tab, begin, nq, false) && last) issue_t(ti + kExpandTmpSlots, nq);
-    ++ti;
     uint8_t* yrow = args.y + tok * row_bytes + (c0w + 8 * t) * 2;
 #pragma unroll
     for (int i = 0; i < 32; i += 4)
@@ -652,10 +649,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       }
   }
   __syncthreads();  // every warp is out of its loop
-  if (threadIdx.x == 0) {
-    wring.drain();
-    tring.drain();
-  }
+  if (threadIdx.x == 0) wring.drain();
 }
 
 }  // namespace plora
