@@ -19,9 +19,9 @@
 //    multiplies its slice of the 8 rows by its A fragments (mma.sync
 //    m16n8k16, D^T = A^T x^T, fp32) and publishes the 16 x 8 partial in
 //    shared memory.  Group i's partials are added, in warp order
-//    (deterministic), by warp i mod 16 one group later, which rounds and
-//    writes tmp: the reduction is spread over the warps and never waits on
-//    the partials of the group just published.
+//    (deterministic), by warp i mod 16 two groups later, which rounds and
+//    writes tmp: the reduction is spread over the warps, and by then every
+//    warp has long published group i, so the reducer does not wait.
 //  * expand: warp w owns N columns [w N/16, (w + 1) N/16).  Per group of 8
 //    tokens it computes delta = tmp B for its columns (mma.sync with the tmp
 //    rows as A fragments; the share's tmp rows are gathered into shared
@@ -63,14 +63,17 @@ constexpr int kStreamWeightParts = 2;      // weight stages per slot
 // exceeds this times the SM count use the windowed kernels instead.
 constexpr int kStreamMaxShare = 1024;
 constexpr int kShrinkPartBufs = 3;                                     // partial buffers in flight
+constexpr int kShrinkReduceLag = 2;  // group i is reduced at group i + 2 (< kShrinkPartBufs)
 constexpr int kShrinkPartBytes = kStreamWarps * 32 * 16;               // one group's 16 partials
 constexpr int kShrinkTmpTileBytes = kStreamWarps * kStreamGroup * kStreamRank * 2;  // per warp: a group's tmp rows
+constexpr int kShrinkMetaBytes = 64;  // per partial buffer: slot, token count, start of its group
 constexpr int kExpandTmpRowBytes = kStreamRank * 2;                    // one token's tmp row
 constexpr int kExpandRegroupBytes = kStreamWarps * kStreamGroup * 64;  // per warp 8 rows x 32 columns
 
 // Shared-memory plan of a stream kernel (host and device alike), offsets from
 // the 128-byte aligned base:
-//   shrink: [nst token/weight stages][3 partial buffers][tmp tiles][barriers][token ids][slot table]
+//   shrink: [nst token/weight stages][3 partial buffers][tmp tiles][group of each buffer][barriers]
+//           [token ids][slot table]
 //   expand: [2 weight stages][tmp rows of the share][regroup tiles][barriers][token ids][slot table]
 // Barrier area: per stage / slot an mbarrier (8 B), a release count and the
 // index of the last item loaded (4 B each); then 6 more mbarriers (the
@@ -93,13 +96,14 @@ __host__ __device__ inline StreamPlan shrink_stream_plan(int64_t K, int64_t num_
   p.stage_bytes = p.pitch * kStreamGroup;
   const int64_t tab = slot_tab_bytes(num_slots);
   const int64_t fixed =
-      128 + kShrinkPartBufs * kShrinkPartBytes + kShrinkTmpTileBytes + stream_bar_bytes(0) + kStreamMaxShare * 4 + tab;
+      128 + kShrinkPartBufs * kShrinkPartBytes + kShrinkTmpTileBytes + kShrinkMetaBytes + stream_bar_bytes(0) +
+      kStreamMaxShare * 4 + tab;
   int64_t nst = (kStreamSmemLimit - fixed) / ((int64_t)p.stage_bytes + 16);
   if (nst > kStreamMaxStages) nst = kStreamMaxStages;
   p.nst = (int)nst;
   p.aux_off = (uint32_t)(nst * p.stage_bytes);
   p.rg_off = p.aux_off + kShrinkPartBufs * kShrinkPartBytes;
-  p.bar_off = p.rg_off + kShrinkTmpTileBytes;
+  p.bar_off = p.rg_off + kShrinkTmpTileBytes + kShrinkMetaBytes;
   p.tok_off = p.bar_off + stream_bar_bytes(p.nst);
   p.tab_off = p.tok_off + kStreamMaxShare * 4;
   p.smem_bytes = (uint32_t)(128 + p.tab_off + tab);
@@ -210,12 +214,14 @@ struct RingItem {
 
 struct RingSeq {
   int p, end, slot, wslot, wpart;  // wslot: slot whose weight stages were last emitted
-  __device__ void init(const SlotTab& t, int64_t b, int64_t e) {
+  bool low_half_only;              // slots of rank <= 8 need only weight stage 0 (expand)
+  __device__ void init(const SlotTab& t, int64_t b, int64_t e, bool rank8_one_stage = false) {
     p = 0;
     end = (int)(e - b);
     slot = (b < e) ? slot_of_position(t.ss, t.ns, b) : 0;
     wslot = -1;
     wpart = 0;
+    low_half_only = rank8_one_stage;
   }
   __device__ __forceinline__ bool next(const SlotTab& t, int64_t base, RingItem& it) {
     while (p < end) {
@@ -230,7 +236,7 @@ struct RingSeq {
       if (slot != wslot) {
         it.part = wpart;
         it.cnt = 0;
-        if (++wpart == kStreamWeightParts) {
+        if (++wpart == kStreamWeightParts || (low_half_only && t.rk[slot] <= 8)) {
           wpart = 0;
           wslot = slot;
         }
@@ -292,9 +298,10 @@ struct StreamRing {
 };
 
 // Arms stage s of item ii for `bytes` of bulk copies (lane 0 of the issuing warp).
+// The stage's earlier readers (ldmatrix) released it before the last of them
+// got here, so the copies may overwrite it.
 __device__ __forceinline__ void ring_arm(const StreamRing& r, int s, int ii, uint32_t bytes) {
   r.loaded[s] = ii;
-  fence_proxy_async_smem();  // earlier generic accesses of the stage before the copies
   mbar_arrive_expect_tx(&r.full[s], bytes);
 }
 
@@ -404,10 +411,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                          16 * ((lane >> 3) & 1);
   uint16_t* tmp = reinterpret_cast<uint16_t*>(args.tmp);
   uint16_t* tile = reinterpret_cast<uint16_t*>(smem + plan.rg_off) + warp * kStreamGroup * kStreamRank;
+  int32_t* pmeta = reinterpret_cast<int32_t*>(smem + plan.rg_off + kShrinkTmpTileBytes);  // [3][slot, cnt, start]
   // Adds the 16 partials of group gi (warp order), rounds and writes its tmp rows.
-  auto reduce = [&](int gi, const RingItem& grp) -> bool {
+  auto reduce = [&](int gi) -> bool {
     const int pb = gi % kShrinkPartBufs;
     if (!mbar_wait_warp(&pfull[pb], (uint32_t)(gi / kShrinkPartBufs) & 1u, abort_flag)) return false;
+    const int g_slot = pmeta[3 * pb], g_cnt = pmeta[3 * pb + 1], g_start = pmeta[3 * pb + 2];
     const float* pp = part + (size_t)pb * (kShrinkPartBytes / 4);
     float v[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -422,15 +431,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     if (lane == 0) mbar_arrive(&pempty[pb]);
     // rounded values -> the warp's tile [token][rank]; then lane l writes 16 bytes
     // (ranks 8 (l & 1) ..) of token l >> 1 with one vector store
-    const int n_eff = min(tab.rk[grp.slot] * args.stack_num, args.R);
+    const int n_eff = min(tab.rk[g_slot] * args.stack_num, args.R);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       tile[(2 * t + h) * kStreamRank + g] = E::from_f(g < n_eff ? v[h] : 0.f);
       tile[(2 * t + h) * kStreamRank + g + 8] = E::from_f(g + 8 < n_eff ? v[2 + h] : 0.f);
     }
     __syncwarp();
-    if (lane < 2 * grp.cnt) {
-      const int64_t row = (int64_t)tok_s[grp.start + (lane >> 1)] * args.R;
+    if (lane < 2 * g_cnt) {
+      const int64_t row = (int64_t)tok_s[g_start + (lane >> 1)] * args.R;
       *reinterpret_cast<uint4*>(tmp + row + 8 * (lane & 1)) = reinterpret_cast<const uint4*>(tile)[lane];
     }
     __syncwarp();
@@ -440,9 +449,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   RingSeq it;
   it.init(tab, begin, end);
   int ii = 0, ti = 0;
-  RingItem cq, prev;
-  prev.slot = prev.cnt = prev.start = 0;
-  prev.part = -1;
+  RingItem cq;
   bool ok = true;
   while (it.next(tab, begin, cq)) {
     const int s = ii % nst;
@@ -479,8 +486,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     ++ii;
     if (cq.part >= 0) continue;
 
-    // the previous group's reduction falls to warp (ti - 1) mod 16
-    if (ti > 0 && ((ti - 1) & (kStreamWarps - 1)) == warp && !reduce(ti - 1, prev)) {
+    // group ti - 2's reduction falls to warp (ti - 2) mod 16
+    const int rg = ti - kShrinkReduceLag;
+    if (rg >= 0 && (rg & (kStreamWarps - 1)) == warp && !reduce(rg)) {
       ok = false;
       break;
     }
@@ -494,13 +502,21 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     float* pp = part + (size_t)pb * (kShrinkPartBytes / 4);
     *reinterpret_cast<float4*>(pp + (warp * 32 + lane) * 4) =
         make_float4(acc[0] + acc2[0], acc[1] + acc2[1], acc[2] + acc2[2], acc[3] + acc2[3]);
+    if (warp == 0 && lane == 0) {  // the group this buffer now holds, for its reducer
+      pmeta[3 * pb] = cq.slot;
+      pmeta[3 * pb + 1] = cq.cnt;
+      pmeta[3 * pb + 2] = cq.start;
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(&pfull[pb]);
-    prev = cq;
     ++ti;
   }
-  // the last group's reduction
-  if (ok && ti > 0 && ((ti - 1) & (kStreamWarps - 1)) == warp) reduce(ti - 1, prev);
+  // the reductions of the last groups
+#pragma unroll
+  for (int k = 0; k < kShrinkReduceLag; ++k) {
+    const int rg = ti - kShrinkReduceLag + k;
+    if (ok && rg >= 0 && (rg & (kStreamWarps - 1)) == warp) ok = reduce(rg);
+  }
   __syncthreads();  // every warp is out of its loop
   if (threadIdx.x == 0) ring.drain();
 }
@@ -511,9 +527,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 // touched.  N % 512 == 0, N <= 4096.
 //
 // Weight stages (B[slot] rank rows 8p .. 8p + 7 at the stage's row pitch;
-// every warp takes the fragments of its columns from both) go through a ring
-// of two, refilled from their own cursor; the tmp rows of the whole share are
-// gathered into shared memory once.
+// every warp takes the fragments of its columns from both; a slot of rank
+// <= 8 has only stage 0, its rows 8..15 entering the mma as zeros) go through
+// a ring of two, refilled from their own cursor; the tmp rows of the whole
+// share are gathered into shared memory once.
 template <bool BF16>
 __global__ void __launch_bounds__(kStreamThreads, 1)
     sgmv_expand_stream_kernel(const ExpandArgs args, const StreamPlan plan) {
@@ -549,7 +566,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                        stage0 + (wi % kStreamWeightParts) * plan.stage_bytes, plan.pitch, row_bytes, pol, lane);
   };
   RingSeq lcw;  // load cursor of the weight stages, 2 ahead
-  lcw.init(tab, begin, end);
+  lcw.init(tab, begin, end, true);
   RingItem q;
   for (int wi = 0; wi < kStreamWeightParts && lcw.next_of(tab, begin, q, true); ++wi)
     if (warp == 0) issue_w(wi, q);
@@ -582,7 +599,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   float scale = 0.f;
   int kr = 0;
   RingSeq it;
-  it.init(tab, begin, end);
+  it.init(tab, begin, end, true);
   int wi = 0;
   RingItem cq;
   while (it.next(tab, begin, cq)) {
@@ -594,6 +611,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         kr = min(tab.rk[cq.slot], args.R);
       }
       const uint32_t sbase = stage0 + s * plan.stage_bytes;
+      const bool one_stage = kr <= 8;  // rank rows 8..15 are not loaded and enter as zeros
 #pragma unroll
       for (int i = 0; i < 32; i += 4)
         if (i < nt) {
@@ -601,10 +619,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           ldsm_x4_t(sbase + w_off + 16 * i, r);  // tiles i .. i + 3 (8 columns, 16 bytes each)
 #pragma unroll
           for (int m = 0; m < 4; ++m) {  // register indices must be compile-time
-            if (cq.part == 0)
+            if (cq.part == 0) {
               b[i + m][0] = r[m];
-            else
+              if (one_stage) b[i + m][1] = 0u;
+            } else {
               b[i + m][1] = r[m];
+            }
           }
         }
       const bool last = wring.release(s, lane);
