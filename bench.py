@@ -36,6 +36,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "mixed-adapter tokens/s at 1/2/4/8 B200; SGMV achieved HBM GB/s vs peak"
 T_TOKENS, K_IN, N_OUT, SLOTS, MAX_RANK = 16384, 4096, 4096, 65, 16
+SEG_ONE_LAUNCH_ROWS = 1024  # rows the one-launch segment builder takes (csrc/segments.cuh)
 E2E_CHUNKS = 8  # row chunks of the host-buffer pipeline (e2e leg)
 ELEM = 2  # bf16
 
@@ -60,6 +61,35 @@ def algorithmic_bytes(ranks, wi):
     expand = t_act * MAX_RANK * ELEM + rsum * N_OUT * ELEM + 2 * t_act * N_OUT * ELEM
     combined = t_act * (K_IN + 2 * N_OUT) * ELEM + (K_IN + N_OUT) * rsum * ELEM
     return t_act, shrink, expand, combined
+
+
+def kernel_source_digest() -> str:
+    """sha256 over the library's CUDA / C sources and header (the code a
+    profile of the kernels describes)."""
+    import hashlib
+
+    h = hashlib.sha256()
+    csrc = ROOT / "polylora_b200" / "csrc"
+    for path in sorted(list(csrc.glob("*.cu")) + list(csrc.glob("*.cuh")) + list(csrc.glob("*.h"))) + [
+            ROOT / "include" / "polylora_b200.h"]:
+        h.update(path.name.encode())
+        h.update(path.read_bytes())
+    return h.hexdigest()
+
+
+def traffic_record(kernel: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, when
+    that summary was captured on these exact sources; else (None, reason)."""
+    path = ROOT / "profiles" / "traffic_cfg2.json"
+    if not path.exists():
+        return None, "no ncu traffic record in profiles/"
+    rec = json.loads(path.read_text())
+    entry = rec.get("kernels", {}).get(kernel)
+    if entry is None:
+        return None, f"profiles/traffic_cfg2.json has no capture of {kernel}"
+    if rec.get("source_sha256") != kernel_source_digest():
+        return None, "profiles/traffic_cfg2.json was captured on other kernel sources"
+    return int(entry["dram_bytes_per_launch"]), "ncu capture of this build (profiles/traffic_cfg2.json)"
 
 
 def measured_peaks():
@@ -168,6 +198,86 @@ def cpu_baseline(seed: int, budget_s: float = 12.0, max_steps: int | None = None
     }
 
 
+def reference_own_cpu(seed: int = 0, rows: int = 2048, budget_s: float = 6.0) -> dict:
+    """The reference's own CPU code from baseline/_ref, unmodified, on the host
+    cores (all threads): (1) MultiLoraLinear._reference_forward
+    (src/polylora/layers.py:112-134, a Python loop over rows with .item()
+    reads) on the first `rows` rows of the config-2 batch, in fp32 and bf16;
+    (2) BASELINE config 1, the reference PolyLoraModel with
+    use_triton_kernels=False around a DeBERTa-v3-small-shaped encoder (fp32,
+    random init, 4 adapters, batch 8 x 128 right-padded), one forward."""
+    import types
+
+    import torch
+
+    out: dict = {"threads": os.cpu_count()}
+    try:
+        sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
+        from polylora import PolyLoraConfig as RefConfig, PolyLoraModel as RefModel
+        from polylora.layers import MultiLoraLinear as RefLinear
+        from polylora.store import CpuLayerWeights as RefWeights
+    except Exception as exc:  # noqa: BLE001
+        return {"unavailable": f"reference not importable from baseline/_ref: {type(exc).__name__}: {exc}"}
+    torch.set_num_threads(os.cpu_count() or 1)
+    ranks_np, wi_np, scales_np = workload(seed)
+
+    def timed(fn):
+        fn()
+        times, t_end = [], time.perf_counter() + budget_s
+        while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 50):
+            t0 = time.perf_counter()
+            fn()
+            times.append(time.perf_counter() - t0)
+        return statistics.median(times), len(times)
+
+    for dtype, name in ((torch.float32, "fp32"), (torch.bfloat16, "bf16")):
+        g = torch.Generator().manual_seed(seed + 1)
+        A = torch.zeros(SLOTS, K_IN, MAX_RANK)
+        B = torch.zeros(SLOTS, MAX_RANK, N_OUT)
+        for s_ in range(1, SLOTS):
+            r = int(ranks_np[s_])
+            A[s_, :, :r] = (torch.rand(K_IN, r, generator=g) * 2 - 1) / 64
+            B[s_, :r] = torch.randn(r, N_OUT, generator=g) * 0.02
+        cache = types.SimpleNamespace(A={"m": A.to(dtype)}, B={"m": B.to(dtype)},
+                                      ranks={"m": torch.from_numpy(ranks_np)}, scales={"m": torch.from_numpy(scales_np)})
+        layer = types.SimpleNamespace(cache=cache, module_name="m")
+        x = torch.randn(rows, 1, K_IN, generator=g).to(dtype)
+        base = torch.randn(rows, 1, N_OUT, generator=g).to(dtype)
+        seq = torch.ones(rows, dtype=torch.int32)
+        idx = torch.from_numpy(wi_np[:rows])
+        sec, n = timed(lambda: RefLinear._reference_forward(layer, x, base, seq, idx))
+        out[f"reference_forward_{name}"] = {"tokens_per_s": rows / sec, "ms_per_pass": sec * 1e3, "passes": n,
+                                           "sample": f"first {rows} rows of the config-2 batch (T=16384), {name}"}
+
+    # BASELINE config 1 through the reference's model wrapper on the CPU
+    torch.manual_seed(0)
+    enc = _deberta_v3_small().float()
+    targets = ["query_proj", "key_proj", "value_proj", "dense"]
+    shapes = {n: (m.in_features, m.out_features) for n, m in enc.named_modules()
+              if isinstance(m, torch.nn.Linear) and any(n == t or n.endswith("." + t) for t in targets)}
+    model = RefModel(enc, RefConfig(max_gpu_adapters=4, max_rank=16, target_modules=targets, use_triton_kernels=False))
+    rng = np.random.default_rng(0)
+    for i, r in enumerate((4, 8, 8, 16)):
+        layers = {}
+        for mod, (k, n_out) in shapes.items():
+            a = torch.empty(r, k)
+            torch.nn.init.kaiming_uniform_(a, a=5 ** 0.5)
+            layers[mod] = RefWeights(A=a.t().contiguous(), B=torch.randn(r, n_out) * 0.02, rank=r, scale=2.0)
+        model.adapter_store.add_adapter(f"a{i}", layers, {"r": r, "lora_alpha": 2 * r})
+    lens = rng.integers(32, 129, size=8)
+    ids = [["__base__", "a0", "a1", "a2", "a3"][int(j)] for j in rng.integers(0, 5, size=8)]
+    input_ids = torch.from_numpy(rng.integers(0, 128100, size=(8, 128))).long()
+    mask = (torch.arange(128)[None, :] < torch.from_numpy(lens)[:, None]).long()
+    with torch.inference_mode():
+        sec, n = timed(lambda: model(input_ids=input_ids, attention_mask=mask, adapter_ids=ids))
+    out["cfg1_model_forward"] = {"ms_per_forward": sec * 1e3, "non_pad_tokens_per_s": int(lens.sum()) / sec,
+                                 "forwards": n, "workload": "BASELINE config 1: DeBERTa-v3-small-shaped encoder "
+                                 "(6 layers, hidden 768), fp32 CPU, 36 wrapped Linears, 4 adapters ranks {4,8,8,16}, "
+                                 "batch 8 x 128 right-padded, lengths U[32,128]; reference PolyLoraModel, "
+                                 "use_triton_kernels=False"}
+    return out
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -182,6 +292,7 @@ def run_reference(args):
                    "path": "reference CPU algorithm (layers.py:112-134), oracle port, host cores"},
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_own": reference_own_cpu(seed=0),
     }
     print(json.dumps(line), flush=True)
 
@@ -310,6 +421,7 @@ def run_ours(args):
     expand_ms = time_kernel(lambda: sgmv_expand(tmp, Bw, y, table, ranks, scales), reps)
     pair_ms = time_kernel(lambda: sgmv_shrink_expand(x, A, Bw, y, table, ranks, scales, tmp=tmp), reps)
     seg_ms = time_kernel(lambda: build_segments(wi, seq, ranks, 1), reps)
+    seg_launches = 1 if T_TOKENS <= SEG_ONE_LAUNCH_ROWS else 3
     del flush_w, flush_r
     clocks = sampler.stop()
 
@@ -365,10 +477,19 @@ def run_ours(args):
     peak, peak_kind = measured_peaks()
     achieved_expand = b_expand / (expand_ms * 1e-3) / 1e9
     achieved_shrink = b_shrink / (shrink_ms * 1e-3) / 1e9
-    traffic = None
-    tfile = ROOT / "profiles" / "expand_cfg2_traffic.json"
-    if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get("bytes_per_launch")
+    stream = _native.stream_kernels() != 0
+    k_shrink = "sgmv_shrink_stream_kernel<bf16>" if stream else "sgmv_shrink_mma_kernel<16,bf16>"
+    k_expand = "sgmv_expand_stream_kernel<bf16>" if stream else "sgmv_expand_mma_kernel<16,bf16>"
+    traffic, traffic_source = traffic_record(k_expand)
+    traffic_shrink, _ = traffic_record(k_shrink)
+
+    # the reference's own GPU path (its Triton kernels) on this B200, same batch
+    triton_ref = _triton_pair_cfg2(dev, x, A, Bw, seq, wi, ranks, scales, y) if world == 1 else None
+    # BASELINE config 3 at this N: row-parallel model forward with the NCCL all-gather in the step
+    try:
+        cfg3 = _cfg3_row_parallel(world, rank, dev, steps=3, warmup=2)
+    except Exception as exc:  # noqa: BLE001 - reported in the line, not fatal
+        cfg3 = {"unavailable": f"{type(exc).__name__}: {exc}"}
 
     cb = cpu_baseline(seed=0) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     if rank != 0:
@@ -400,7 +521,7 @@ def run_ours(args):
             "active_tokens_per_gpu": t_act,
         },
         "roofline": {
-            "kernel": "sgmv_expand_mma_kernel<16,bf16>",
+            "kernel": k_expand,
             "bound": "hbm",
             "achieved": achieved_expand,
             "peak": peak,
@@ -408,13 +529,16 @@ def run_ours(args):
             "frac": achieved_expand / peak,
             "peak_source": peak_kind,
             "traffic": traffic,
+            "traffic_source": traffic_source,
             "algorithmic_bytes_per_launch": b_expand,
             "avg_launch_ms": expand_ms,
         },
         "kernels": {
-            "shrink": {"avg_launch_ms": shrink_ms, "bytes": b_shrink, "gbs": achieved_shrink, "frac": achieved_shrink / peak},
-            "expand": {"avg_launch_ms": expand_ms, "bytes": b_expand, "gbs": achieved_expand, "frac": achieved_expand / peak},
-            "segments": {"avg_ms": seg_ms, "launches": 3},
+            "shrink": {"kernel": k_shrink, "avg_launch_ms": shrink_ms, "bytes": b_shrink, "gbs": achieved_shrink,
+                       "frac": achieved_shrink / peak, "traffic": traffic_shrink},
+            "expand": {"kernel": k_expand, "avg_launch_ms": expand_ms, "bytes": b_expand, "gbs": achieved_expand,
+                       "frac": achieved_expand / peak, "traffic": traffic},
+            "segments": {"avg_ms": seg_ms, "launches": seg_launches},
             "shrink_expand_call": {"avg_ms": pair_ms, "bytes": b_shrink + b_expand,
                                    "gbs": (b_shrink + b_expand) / (pair_ms * 1e-3) / 1e9},
             "step_combined_gbs": b_comb / (ms_per_step * 1e-3) / 1e9,
@@ -428,12 +552,76 @@ def run_ours(args):
                 "serial_ms_per_step": serial_ms,
                 "serial_path": "sgmv_lora_a_fwd + sgmv_lora_b_fwd (C-ABI) on one stream: pinned host x/y/metadata "
                                "in, y out"},
-        "gpu_launches": 5 * args.steps,
+        "gpu_launches": (seg_launches + 2) * args.steps,
         "clocks": clocks,
+        "triton_reference": triton_ref,
+        "model_cfg3": cfg3,
     }
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def _triton_pair_cfg2(dev, x, A, Bw, seq, wi, ranks, scales, y):
+    """The reference's own GPU path on this B200: its unmodified Triton
+    sgmv_lora_a_fwd + sgmv_lora_b_fwd (src/polylora/sgmv.py:141-175, 278-328,
+    from baseline/_ref) against this library's operators of the same
+    signatures, eager calls as layers.py:42-58 makes them, on the benched
+    config-2 batch; L2 flushed before each pair (loop [flush, pair] minus loop
+    [flush]).  None fields and a reason when the reference is not installed."""
+    import torch
+
+    from polylora_b200.sgmv import sgmv_lora_a_fwd, sgmv_lora_b_fwd
+
+    try:
+        sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
+        from polylora.sgmv import sgmv_lora_a_fwd as ref_a, sgmv_lora_b_fwd as ref_b
+    except Exception as exc:  # noqa: BLE001
+        return {"unavailable": f"reference not importable from baseline/_ref: {type(exc).__name__}: {exc}"}
+    flush_w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_r = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    sink = torch.empty((), dtype=torch.float32, device=dev)
+
+    def flush():
+        flush_w.fill_(7)
+        torch.sum(flush_r, dim=0, out=sink)
+
+    def loop_ms(fns, reps=20):
+        for _ in range(3):
+            for f in fns:
+                f()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            for f in fns:
+                f()
+        b.record()
+        b.synchronize()
+        return a.elapsed_time(b) / reps
+
+    out = y.clone()
+    ours = lambda: sgmv_lora_b_fwd(sgmv_lora_a_fwd(x, A, seq, wi, ranks), Bw, seq, wi, ranks, scales, out)  # noqa: E731
+    theirs = lambda: ref_b(ref_a(x, A, seq, wi, ranks), Bw, seq, wi, ranks, scales, out)  # noqa: E731
+    # agreement on a fresh N(0, 1) base output (the benched y has been updated in place many times)
+    y = torch.randn(y.shape, device=dev, generator=torch.Generator(device=dev).manual_seed(7)).to(y.dtype)
+    y_o, y_r = y.clone(), y.clone()
+    sgmv_lora_b_fwd(sgmv_lora_a_fwd(x, A, seq, wi, ranks), Bw, seq, wi, ranks, scales, y_o)
+    ref_b(ref_a(x, A, seq, wi, ranks), Bw, seq, wi, ranks, scales, y_r)
+    torch.cuda.synchronize()
+    delta = (y_r.float() - y.float()).abs().max().item()
+    t_flush = loop_ms([flush])
+    res = {"path": "eager sgmv_lora_a_fwd + sgmv_lora_b_fwd pair, L2 flushed before each pair",
+           "max_abs_diff_over_max_delta": (y_o.float() - y_r.float()).abs().max().item() / max(delta, 1e-30)}
+    for name, fn in (("triton_reference", theirs), ("ours", ours)):
+        ms = loop_ms([flush, fn]) - t_flush
+        res[name] = {"us_per_pair": ms * 1e3, "tokens_per_s": T_TOKENS / (ms * 1e-3)}
+    res["speedup"] = res["triton_reference"]["us_per_pair"] / res["ours"]["us_per_pair"]
+    import triton
+
+    res["triton"] = triton.__version__
+    del flush_w, flush_r
+    return res
 
 
 # ---------------------------------------------------------------- config-2 op sweep
@@ -771,16 +959,14 @@ def _deberta_v3_large():
     return DebertaV2Model(cfg).eval()
 
 
-def run_model_cfg3(args):
+def _cfg3_setup(dev):
+    """BASELINE config 3 on `dev`: the wrapped DeBERTa-v3-large-shaped encoder,
+    its 32 synthetic adapters and the 256 x 512 right-padded batch (seeded)."""
     import torch
-    import torch.distributed as dist
 
     from polylora_b200 import PolyLoraConfig, PolyLoraModel
-    from polylora_b200.rowshard import RowParallel
     from polylora_b200.store import CpuLayerWeights
 
-    world, rank, local = dist_setup(args.gpus)
-    dev = torch.device("cuda", torch.cuda.current_device())
     torch.manual_seed(0)
     torch.set_default_dtype(torch.bfloat16)
     with torch.device(dev):
@@ -808,12 +994,81 @@ def run_model_cfg3(args):
     ids = [("__base__" if rng.random() < 0.25 else f"adapter{int(rng.integers(CFG3_SLOTS))}") for _ in range(CFG3_ROWS)]
     input_ids = torch.randint(0, 128100, (CFG3_ROWS, CFG3_SEQ), generator=g).to(dev)
     mask = (torch.arange(CFG3_SEQ)[None, :] < torch.from_numpy(lens)[:, None]).long().to(dev)
-    tokens = int(lens.sum())
+    return model, base, ids, input_ids, mask, int(lens.sum())
+
+
+def _cfg3_row_parallel(world, rank, dev, steps, warmup):
+    """The config-3 forward under RowParallel (equal rows per rank, NCCL
+    all-gather of the outputs inside the timed step).  Returns tokens/s and
+    the split of the step: each rank's shard forward alone (max and min over
+    ranks: the load imbalance) and the all-gather alone (the collective)."""
+    import torch
+    import torch.distributed as dist
+
+    from polylora_b200.rowshard import RowParallel, partition_rows
+
+    model, _, ids, input_ids, mask, tokens = _cfg3_setup(dev)
+    fn = lambda adapter_ids, **kw: model(adapter_ids=adapter_ids, **kw).last_hidden_state  # noqa: E731
+    lora_fn = RowParallel(fn, row_cost=RowParallel.EQUAL_ROWS)
+    bounds = partition_rows([CFG3_SEQ] * CFG3_ROWS, world, lambda n: 1)
+    s0, s1 = bounds[rank]
+    shard = dict(input_ids=input_ids[s0:s1], attention_mask=mask[s0:s1])
+
+    def max_min(v):
+        if world == 1:
+            return v, v
+        t = torch.tensor([v, -v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0]), -float(t[1])
+
+    def timed(step, n):
+        with torch.inference_mode():
+            for _ in range(max(warmup, 2)):
+                step()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(n):
+                step()
+            e1.record()
+            e1.synchronize()
+            if world > 1:
+                dist.barrier()
+        return e0.elapsed_time(e1) / n
+
+    step_ms = max_min(timed(lambda: lora_fn(ids, input_ids=input_ids, attention_mask=mask), steps))[0]
+    shard_max, shard_min = max_min(timed(lambda: fn(ids[s0:s1], **shard), steps))
+    out = {"ms_per_forward": step_ms, "tokens_per_s": tokens / (step_ms * 1e-3),
+           "padded_tokens_per_s": CFG3_ROWS * CFG3_SEQ / (step_ms * 1e-3), "non_pad_tokens": tokens,
+           "shard_forward_ms_max": shard_max, "shard_forward_ms_min": shard_min, "steps": steps}
+    if world > 1:
+        from polylora_b200.rowshard import all_gather_rows
+
+        local = torch.zeros(s1 - s0, CFG3_SEQ, 1024, device=dev, dtype=torch.bfloat16)
+        gather_ms = max_min(timed(lambda: all_gather_rows(local, bounds), steps))[0]
+        out["all_gather_ms"] = gather_ms
+        out["limiter"] = ("all-gather" if gather_ms > shard_max - shard_min else "row imbalance")
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_model_cfg3(args):
+    import torch
+    import torch.distributed as dist
+
+    from polylora_b200.rowshard import RowParallel
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    model, base, ids, input_ids, mask, tokens = _cfg3_setup(dev)
 
     # the encoder computes every row at the padded length: balance shards by rows
     lora_fn = RowParallel(lambda adapter_ids, **kw: model(adapter_ids=adapter_ids, **kw).last_hidden_state,
-                          row_cost=lambda n: 1)
-    base_fn = RowParallel(lambda adapter_ids, **kw: base(**kw).last_hidden_state, row_cost=lambda n: 1)
+                          row_cost=RowParallel.EQUAL_ROWS)
+    base_fn = RowParallel(lambda adapter_ids, **kw: base(**kw).last_hidden_state, row_cost=RowParallel.EQUAL_ROWS)
 
     def barrier():
         if world > 1:
@@ -1136,7 +1391,7 @@ def run_model_cfg5(args):
             micro_batches[0] += 1
         return out
 
-    lora_fn = RowParallel(lambda adapter_ids, input_ids: serve(adapter_ids, input_ids), row_cost=lambda n: 1)
+    lora_fn = RowParallel(lambda adapter_ids, input_ids: serve(adapter_ids, input_ids), row_cost=RowParallel.EQUAL_ROWS)
 
     def step(ids, x):
         return lora_fn(ids, input_ids=x)

@@ -131,6 +131,23 @@ def lora_err(out, ref, y, dtype: str) -> float:
     return float(np.max(excess)) / scale
 
 
+def lora_err_strict(out, ref, y, dtype: str) -> float:
+    """As :func:`lora_err`, with half an output ulp of allowance instead of
+    one: max over elements of max(0, |out - ref| - ULP[dtype]/2 * |ref|) /
+    max|ref - y|.  Half an ulp is exactly the rounding of ``y + delta`` into
+    ``dtype``, so what remains is the error of the LoRA delta itself (its
+    accumulation and its own rounding).  With ``y = 0`` the output is the
+    delta and this is an element-wise check of it."""
+    out = np.asarray(out, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    y = np.asarray(y, dtype=np.float64)
+    if ref.size == 0:
+        return 0.0
+    scale = max(float(np.max(np.abs(ref - y))), 1e-30)
+    excess = np.maximum(np.abs(out - ref) - 0.5 * ULP[dtype] * np.abs(ref), 0.0)
+    return float(np.max(excess)) / scale
+
+
 def rel_err(out, ref) -> float:
     """Normwise max relative error: max|out - ref| / max|ref|."""
     out = np.asarray(out, dtype=np.float64)

@@ -80,25 +80,41 @@ class RowParallel:
     ``.last_hidden_state`` from it).  Batch tensors are the keyword arguments
     whose first dimension equals the number of rows; they are sliced, other
     arguments are passed through.  Returns the full-batch output (all-gathered).
+
+    The partition needs each row's length on the host.  With
+    ``row_cost=RowParallel.EQUAL_ROWS`` (every row costs the same: models that
+    compute every row at the padded length) it needs none; otherwise it takes
+    ``host_seq_lens`` (a list the caller already holds, e.g. from its
+    tokenizer) or, failing that, reads the attention mask back from the
+    device, which waits for the work queued before it.
     """
 
+    EQUAL_ROWS = object()  # row_cost: balance rows, no lengths needed
+
     def __init__(self, fn: Callable[..., torch.Tensor], group=None,
-                 row_cost: Callable[[int], float] | None = None) -> None:
+                 row_cost: Callable[[int], float] | object | None = None) -> None:
         self.fn = fn
         self.group = group
-        self.row_cost = row_cost  # see partition_rows
+        self.row_cost = row_cost  # see partition_rows, or EQUAL_ROWS
 
-    def __call__(self, adapter_ids: list[str], **batch: Any) -> torch.Tensor:
+    def _seq_lens(self, rows: int, host_seq_lens, batch: dict) -> list[int]:
+        if host_seq_lens is not None:
+            return [int(v) for v in host_seq_lens]
+        mask = batch.get("attention_mask")
+        if mask is not None:
+            return mask.sum(-1).tolist()  # device -> host read
+        ref = batch.get("input_ids", batch.get("inputs_embeds"))
+        return [int(ref.shape[1])] * rows
+
+    def __call__(self, adapter_ids: list[str], host_seq_lens: Sequence[int] | None = None,
+                 **batch: Any) -> torch.Tensor:
         world = dist.get_world_size(self.group) if dist.is_initialized() else 1
         rank = dist.get_rank(self.group) if dist.is_initialized() else 0
         rows = len(adapter_ids)
-        mask = batch.get("attention_mask")
-        if mask is not None:
-            seq_lens = mask.sum(-1).tolist()
+        if self.row_cost is RowParallel.EQUAL_ROWS:
+            bounds = partition_rows([1] * rows, world, lambda n: 1)
         else:
-            ref = batch.get("input_ids", batch.get("inputs_embeds"))
-            seq_lens = [int(ref.shape[1])] * rows
-        bounds = partition_rows(seq_lens, world, self.row_cost)
+            bounds = partition_rows(self._seq_lens(rows, host_seq_lens, batch), world, self.row_cost)
         start, end = bounds[rank]
         if end == start:  # fewer rows than ranks: run a copy of the last row, drop it
             start, end = rows - 1, rows

@@ -182,3 +182,22 @@ def test_cpu_lru_oracle_and_store_match_reference_sequences(golden_dir):
     for seq in sequences:
         _replay_lru(OracleView, seq)
         _replay_lru(StoreView, seq)
+
+
+def test_strict_error_catches_a_delta_lost_on_large_outputs():
+    """A planted mistake (30% of the LoRA delta dropped on the elements whose
+    base output is large) hides under the one-ulp allowance of lora_err but
+    not under the half-ulp allowance of lora_err_strict: the rounding of
+    y + delta into bf16 costs at most half an output ulp."""
+    rng = np.random.default_rng(5)
+    y = sgmv_ref.round_to(rng.normal(0, 1, size=(4096,)).astype(np.float32) * 4, "bfloat16")
+    delta = rng.normal(0, 0.03, size=y.shape)
+    ref = (y.astype(np.float64) + delta).astype(np.float32)
+    big = np.abs(y) > 3.0
+    planted = y.astype(np.float64) + np.where(big, 0.7 * delta, delta)
+    out = sgmv_ref.round_to(planted.astype(np.float32), "bfloat16")
+    good = sgmv_ref.round_to(ref, "bfloat16")
+    assert sgmv_ref.lora_err_strict(good, ref, y, "bfloat16") <= 1e-6  # correct rounding passes exactly
+    assert sgmv_ref.lora_err_strict(out, ref, y, "bfloat16") > 0.05
+    # the loose form lets part of the planted error through
+    assert sgmv_ref.lora_err(out, ref, y, "bfloat16") < sgmv_ref.lora_err_strict(out, ref, y, "bfloat16")
