@@ -36,6 +36,14 @@ CASES = [
     (1024, 17, 65, 0.2, [0, 4, 8, 16]),
     (1025, 1, 65, 0.2, [0, 4, 8, 16]),
     (1024, 1, 257, 0.2, [0, 4, 8, 16]),
+    # larger batches (three kernels): many blocks of rows, all slots in one block, long rows
+    (1025, 3, 9, 0.2, [0, 4, 8, 16]),
+    (2048, 1, 1, 0.0, [0]),
+    (4097, 2, 256, 0.1, [0, 16]),
+    (32768, 1, 65, 0.2, [0, 4, 8, 16]),
+    (32769, 1, 65, 0.2, [0, 4, 8, 16]),
+    (8192, 1, 257, 0.2, [0, 4, 8, 16]),
+    (4096, 1025, 9, 0.0, [16]),
 ]
 
 
