@@ -1487,6 +1487,37 @@ def run_model_cfg5(args):
         dist.destroy_process_group()
 
 
+def run_profile(args):
+    """A small case for ncu: the config-2 inputs (x and y 128 MiB each, larger
+    than L2), two warm-up steps, then one step of segment table + shrink +
+    expand as plain launches.  Prints the kernel-source digest the capture
+    describes."""
+    import torch
+
+    from polylora_b200.sgmv import build_segments, sgmv_shrink_expand
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    ranks_np, wi_np, scales_np = workload(seed=0)
+    g = torch.Generator(device=dev).manual_seed(1000)
+    ranks = torch.from_numpy(ranks_np).to(dev)
+    colmask = (torch.arange(MAX_RANK, device=dev)[None, :] < ranks[:, None]).float()
+    A = ((torch.rand(SLOTS, K_IN, MAX_RANK, device=dev, generator=g) * 2 - 1) / 64 * colmask[:, None, :]).to(torch.bfloat16)
+    Bw = (torch.randn(SLOTS, MAX_RANK, N_OUT, device=dev, generator=g) * 0.02 * colmask[:, :, None]).to(torch.bfloat16)
+    scales = torch.from_numpy(scales_np).to(dev)
+    wi = torch.from_numpy(wi_np).to(dev)
+    seq = torch.ones(T_TOKENS, dtype=torch.int32, device=dev)
+    x = torch.randn(T_TOKENS, 1, K_IN, device=dev, generator=g).to(torch.bfloat16)
+    y = torch.randn(T_TOKENS, 1, N_OUT, device=dev, generator=g).to(torch.bfloat16)
+    tmp = torch.empty(T_TOKENS, 1, MAX_RANK, device=dev, dtype=torch.bfloat16)
+    for _ in range(3):
+        table = build_segments(wi, seq, ranks, 1)
+        sgmv_shrink_expand(x, A, Bw, y, table, ranks, scales, tmp=tmp)
+    torch.cuda.synchronize()
+    print(json.dumps({"workload": "profile", "kernel_source_sha256": kernel_source_digest(),
+                      "active_tokens": int((ranks_np[wi_np] > 0).sum())}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1494,7 +1525,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["cfg2", "cfg2-sweep", "cfg2-triton", "cfg3", "cfg4", "cfg4-decode",
+    ap.add_argument("--workload", choices=["cfg2", "profile", "cfg2-sweep", "cfg2-triton", "cfg3", "cfg4", "cfg4-decode",
                                            "cfg4-ops", "cfg5"],
                     default="cfg2",
                     help="cfg2: the SGMV op step (default, the headline line); cfg3: model forward")
@@ -1504,7 +1535,9 @@ def main():
     ap.add_argument("--split", choices=["token_split", "weight_split"], default=None,
                     help="cfg4-ops: only this work split")
     args = ap.parse_args()
-    if args.workload == "cfg2-sweep" and args.impl != "reference":
+    if args.workload == "profile" and args.impl != "reference":
+        run_profile(args)
+    elif args.workload == "cfg2-sweep" and args.impl != "reference":
         run_sweep(args)
     elif args.workload == "cfg2-triton" and args.impl != "reference":
         run_triton_compare(args)
