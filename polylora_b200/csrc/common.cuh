@@ -134,6 +134,10 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
 __device__ __forceinline__ void named_barrier(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
+// Counts the calling warp in at the named barrier without waiting for it.
+__device__ __forceinline__ void named_barrier_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 
 // Orders this thread's generic-proxy shared-memory accesses before its later
 // async-proxy (TMA) operations on the same memory.

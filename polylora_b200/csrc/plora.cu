@@ -365,7 +365,7 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
       if (plan.nst >= 2) {
         // the kernel reads its inputs only after griddep_wait(): always launched programmatically
         PLORA_CUDA(launch_kernel(bf ? sgmv_shrink_stream_kernel<true> : sgmv_shrink_stream_kernel<false>,
-                                 dim3(di->sm_count), dim3(kStreamThreads), plan.smem_bytes, stream, true, 0,
+                                 dim3(di->sm_count), dim3(kShrinkThreads), plan.smem_bytes, stream, true, 0,
                                  args, plan),
                    "launch sgmv_shrink_stream_kernel");
         return check_launch("sgmv_shrink_stream_kernel");

@@ -8,21 +8,28 @@
 // issued.
 //  * At rank 16 a slot's LoRA-A (K x 16) or LoRA-B (16 x N) is 128 KB for K
 //    or N = 4096.  Split over 16 warps that is 8 KB per warp, 64 registers per
-//    lane in mma fragment layout.  The weights arrive as two "weight stages"
-//    (LoRA-A halves of K/2 rows; LoRA-B rank rows 0-7 and 8-15) by bulk
-//    copies, prefetched like any other stage, and the warps move their slices
-//    into registers with ldmatrix.trans.
+//    lane in mma fragment layout.
 //  * shrink: token rows travel by one non-multicast `cp.async.bulk` per row
 //    (K * 2 bytes) into a ring of shared-memory stages of 8 rows, at a
 //    (K * 2 + 16)-byte pitch so that ldmatrix over eight rows hits eight bank
-//    groups.  Warp w owns K rows [w K/16, (w + 1) K/16): per stage it
+//    groups.  The ring carries token rows only, refilled by a producer warp;
+//    each consumer warp loads its slice of LoRA-A straight into registers
+//    (two 8-byte loads per k16 step, turned into the mma layout by
+//    movmatrix.trans; see shrink_rank_of_row), so the first token rows are
+//    requested at launch, beside the weights, and a change of slot costs one
+//    L2 round trip (the slot's rows are prefetched into L2 when the producer
+//    first meets it) instead of 128 KB of ring stages.  Warp w owns K rows
+//    [w K/16, (w + 1) K/16): per stage it
 //    multiplies its slice of the 8 rows by its A fragments (mma.sync
 //    m16n8k16, D^T = A^T x^T, fp32) and publishes the 16 x 8 partial in
 //    shared memory.  Group i's partials are added, in warp order
 //    (deterministic), by warp i mod 16 two groups later, which rounds and
 //    writes tmp: the reduction is spread over the warps, and by then every
 //    warp has long published group i, so the reducer does not wait.
-//  * expand: warp w owns N columns [w N/16, (w + 1) N/16).  Per group of 8
+//  * expand: the weights arrive as "weight stages" (LoRA-B rank rows 0-7 and
+//    8-15) by bulk copies through a ring of two, and the warps move their
+//    column slices into registers with ldmatrix.trans.
+//    Warp w owns N columns [w N/16, (w + 1) N/16).  Per group of 8
 //    tokens it computes delta = tmp B for its columns (mma.sync with the tmp
 //    rows as A fragments; the share's tmp rows are gathered into shared
 //    memory by cp.async once, at the start), rounds scale * delta to
@@ -32,13 +39,13 @@
 //    reads y, adds and rounds to nearest, so y never passes through the SM
 //    and nothing waits for it; the result is the reference's (round the
 //    scaled delta, then the sum) bit for bit.
-// Stages are refilled by the last of the 16 warps to finish with them;
-// there is no producer role.  Work split: a CTA per SM takes a contiguous
-// share of the slot-ordered token list (its token ids are copied to shared
-// memory once, so no global load sits between a stage landing and its
-// refill), cut into groups of <= 8 tokens of one slot.  At the start the
-// slot table is read first, so that the first weight stages are issued one
-// global round trip after launch, while the token ids are still on their way.
+// The expand's weight stages are refilled by the last of the 16 warps to
+// finish with them.  Work split: a CTA per SM takes a contiguous share of the
+// slot-ordered token list (its token ids are copied to shared memory once, so
+// no global load sits between a stage landing and its refill), cut into
+// groups of <= 8 tokens of one slot.  At the start the slot table is read
+// first, so that the first weights are requested one global round trip after
+// launch.
 // Every wait is bounded; after an expiry or an abort the warps leave their
 // loops, and thread 0 waits (bounded) for the loads already issued before the
 // CTA exits.
@@ -72,14 +79,14 @@ constexpr int kExpandRegroupBytes = kStreamWarps * kStreamGroup * 64;  // per wa
 
 // Shared-memory plan of a stream kernel (host and device alike), offsets from
 // the 128-byte aligned base:
-//   shrink: [nst token/weight stages][3 partial buffers][tmp tiles][group of each buffer][barriers]
+//   shrink: [nst token stages][3 partial buffers][tmp tiles][group of each buffer][barriers]
 //           [token ids][slot table]
 //   expand: [2 weight stages][tmp rows of the share][regroup tiles][barriers][token ids][slot table]
-// Barrier area: per stage / slot an mbarrier (8 B), a release count and the
-// index of the last item loaded (4 B each); then 6 more mbarriers (the
-// shrink's partial hand-off) and the abort flag.
+// Barrier area (expand): per weight stage an mbarrier (8 B), a release count
+// and the index of the last item loaded (4 B each); then 6 unused mbarrier
+// words and the abort flag.  The shrink's is laid out by shrink_bar_bytes.
 struct StreamPlan {
-  int nst;               // shrink: ring stages; expand: weight stages
+  int nst;               // shrink: token stages; expand: weight stages
   uint32_t pitch;        // token / weight row pitch in a stage
   uint32_t stage_bytes;  // 8 rows
   uint32_t aux_off;      // shrink: partial buffers; expand: the share's tmp rows
@@ -89,6 +96,9 @@ struct StreamPlan {
 };
 
 __host__ __device__ inline uint32_t stream_bar_bytes(int slots) { return (uint32_t)slots * 16 + 6 * 8 + 16; }
+// shrink: per stage a full and an empty mbarrier (16 B) and the last item armed
+// (4 B, after the 6 partial barriers), then the abort flag
+__host__ __device__ inline uint32_t shrink_bar_bytes(int stages) { return (uint32_t)stages * 20 + 6 * 8 + 16; }
 
 __host__ __device__ inline StreamPlan shrink_stream_plan(int64_t K, int64_t num_slots) {
   StreamPlan p;
@@ -96,15 +106,15 @@ __host__ __device__ inline StreamPlan shrink_stream_plan(int64_t K, int64_t num_
   p.stage_bytes = p.pitch * kStreamGroup;
   const int64_t tab = slot_tab_bytes(num_slots);
   const int64_t fixed =
-      128 + kShrinkPartBufs * kShrinkPartBytes + kShrinkTmpTileBytes + kShrinkMetaBytes + stream_bar_bytes(0) +
+      128 + kShrinkPartBufs * kShrinkPartBytes + kShrinkTmpTileBytes + kShrinkMetaBytes + shrink_bar_bytes(0) +
       kStreamMaxShare * 4 + tab;
-  int64_t nst = (kStreamSmemLimit - fixed) / ((int64_t)p.stage_bytes + 16);
+  int64_t nst = (kStreamSmemLimit - fixed) / ((int64_t)p.stage_bytes + 24);
   if (nst > kStreamMaxStages) nst = kStreamMaxStages;
   p.nst = (int)nst;
   p.aux_off = (uint32_t)(nst * p.stage_bytes);
   p.rg_off = p.aux_off + kShrinkPartBufs * kShrinkPartBytes;
   p.bar_off = p.rg_off + kShrinkTmpTileBytes + kShrinkMetaBytes;
-  p.tok_off = p.bar_off + stream_bar_bytes(p.nst);
+  p.tok_off = p.bar_off + shrink_bar_bytes(p.nst);
   p.tab_off = p.tok_off + kStreamMaxShare * 4;
   p.smem_bytes = (uint32_t)(128 + p.tab_off + tab);
   return p;
@@ -139,6 +149,27 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
+}
+
+// Asks the L2 to fetch [src, src + bytes) (16-byte aligned, a multiple of 16);
+// nothing waits for it.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// 8-byte load of data that no kernel writes while this one runs, not kept in L1.
+__device__ __forceinline__ uint2 ld_nc_v2(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+
+// Transposes the 8 x 8 16-bit matrix the warp holds in row layout (lane l:
+// row l >> 2, columns 2 (l & 3) and + 1) into the same layout.
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t v) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(v));
+  return d;
 }
 
 __device__ __forceinline__ void cp_async16_cg(uint32_t dst, const void* src) {
@@ -204,9 +235,10 @@ __device__ __forceinline__ uint8_t* align128(uint8_t* p) {
 
 // ---------------------------------------------------------------- items
 // Items of a CTA: for every run of tokens of one slot of rank > 0 inside the
-// CTA's share of the slot-ordered token list, the slot's two weight stages,
-// then its groups of <= 8 tokens (runs of rank-0 slots are skipped).
-// Positions are relative to the share's start `base`.
+// CTA's share of the slot-ordered token list, the slot's two weight stages
+// (unless the sequence is made without them), then its groups of <= 8 tokens
+// (runs of rank-0 slots are skipped).  Positions are relative to the share's
+// start `base`.
 struct RingItem {
   int part;  // weight stage 0 / 1, or -1 for a token group
   int slot, cnt, start;
@@ -215,13 +247,16 @@ struct RingItem {
 struct RingSeq {
   int p, end, slot, wslot, wpart;  // wslot: slot whose weight stages were last emitted
   bool low_half_only;              // slots of rank <= 8 need only weight stage 0 (expand)
-  __device__ void init(const SlotTab& t, int64_t b, int64_t e, bool rank8_one_stage = false) {
+  bool weights;                    // false: token groups only
+  __device__ void init(const SlotTab& t, int64_t b, int64_t e, bool rank8_one_stage = false,
+                       bool with_weights = true) {
     p = 0;
     end = (int)(e - b);
     slot = (b < e) ? slot_of_position(t.ss, t.ns, b) : 0;
     wslot = -1;
     wpart = 0;
     low_half_only = rank8_one_stage;
+    weights = with_weights;
   }
   __device__ __forceinline__ bool next(const SlotTab& t, int64_t base, RingItem& it) {
     while (p < end) {
@@ -233,7 +268,7 @@ struct RingSeq {
       }
       it.slot = slot;
       it.start = p;
-      if (slot != wslot) {
+      if (weights && slot != wslot) {
         it.part = wpart;
         it.cnt = 0;
         if (++wpart == kStreamWeightParts || (low_half_only && t.rk[slot] <= 8)) {
@@ -320,16 +355,57 @@ __device__ __forceinline__ void stream_stage_tokens(const int32_t* token_index, 
                                                     int32_t* dst) {
   for (int64_t i = threadIdx.x; i < end - begin; i += blockDim.x) dst[i] = ld_cg_i32(token_index + begin + i);
 }
+// The same by one warp, 256 ids per round trip.
+__device__ __forceinline__ void stream_stage_tokens_warp(const int32_t* token_index, int64_t begin, int64_t end,
+                                                         int32_t* dst, int lane) {
+  constexpr int kPerLane = 8;
+  const int n = (int)(end - begin);
+  for (int c = 0; c < n; c += 32 * kPerLane) {
+    int32_t v[kPerLane];
+#pragma unroll
+    for (int k = 0; k < kPerLane; ++k)
+      if (c + k * 32 + lane < n) v[k] = ld_cg_i32(token_index + begin + c + k * 32 + lane);
+#pragma unroll
+    for (int k = 0; k < kPerLane; ++k)
+      if (c + k * 32 + lane < n) dst[c + k * 32 + lane] = v[k];
+  }
+}
 
 // ============================================================== shrink
 // tmp[t, :] = x[t, :] @ A[slot(t)] (rank 16) for the active tokens of the
 // table; columns >= min(rank * stack_num, 16) of an active token are written
 // as 0, inactive tokens are not written.  K % 512 == 0, K <= 4096.
 //
-// Weight stage p holds A[slot] rows [p K/2, (p + 1) K/2) (32 bytes each,
-// contiguous); warps 8p .. 8p + 7 take their K slices from it.
+// Roles: warps 0-15 consume token stages; warp 16 stages the share's token
+// ids and refills the ring (it waits for a stage's 16 releases on an mbarrier,
+// then issues the stage's row copies), so a bulk copy that stalls at issue
+// while the copy engine is busy delays no consumer.  Warps 17-19 only make the
+// producer a whole warpgroup: the CTA is launched at kShrinkLaunchRegs
+// registers a thread and setmaxnreg moves the producer warpgroup's share to
+// the consumers (64 fragment registers each).
+//
+// A fragments from global memory: for its k16 step at row k0, lane (g, t)
+// loads ranks 4t .. 4t + 3 of rows k0 + g and k0 + 8 + g (8 bytes each).  The
+// low half of the first load is element (g, 2t) of the 8 x 8 block "rows k0 ..
+// k0 + 7, ranks 4c + {0, 1} for column pair c" in row layout, the high half
+// the same for ranks 4c + {2, 3}; movmatrix.trans turns each into the A^T
+// fragment.  So mma row r (r < 8) holds rank shrink_rank_of_row(r) = 4 (r >> 1)
+// + (r & 1) and row 8 + r holds that rank + 2; the reduction writes tmp in
+// rank order.  A warp's step reads 8 whole 32-byte rows of A (256 contiguous
+// bytes) per load instruction.
+constexpr int kShrinkThreads = kStreamThreads + 128;  // 16 consumer warps + the producer warpgroup
+constexpr int kShrinkLaunchRegs = 96;                 // 5 warps per scheduler partition
+constexpr int kShrinkConsumerRegs = 112;
+constexpr int kShrinkProducerRegs = 32;
+constexpr int kShrinkIdsReady = 1;  // named barrier: the producer has staged the token ids
+// per scheduler partition: 4 consumer warps + 1 producer-group warp within the launch's registers
+static_assert(4 * kShrinkConsumerRegs + kShrinkProducerRegs <= 5 * kShrinkLaunchRegs, "register split");
+static_assert(5 * 32 * kShrinkLaunchRegs <= 16384, "launch registers per partition");
+
+__host__ __device__ constexpr int shrink_rank_of_row(int r) { return 4 * ((r & 7) >> 1) + (r & 1) + 2 * (r >> 3); }
+
 template <bool BF16>
-__global__ void __launch_bounds__(kStreamThreads, 1)
+__global__ void __launch_bounds__(kShrinkThreads, 1)
     sgmv_shrink_stream_kernel(const ShrinkArgs args, const StreamPlan plan) {
   using E = Elem<BF16>;
   extern __shared__ uint8_t smem_raw[];
@@ -337,11 +413,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const int nst = plan.nst;
   const int K = args.K;
   float* part = reinterpret_cast<float*>(smem + plan.aux_off);
-  StreamRing ring;
-  ring.carve(smem + plan.bar_off, nst);
-  uint64_t* pfull = reinterpret_cast<uint64_t*>(ring.loaded + nst);  // [3] all 16 partials of the group written
-  uint64_t* pempty = pfull + kShrinkPartBufs;                          // [3] the group's partials have been read
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(pempty + kShrinkPartBufs);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + plan.bar_off);  // [nst] token rows landed
+  uint64_t* empty = full + nst;                                         // [nst] 16 consumer warps released
+  uint64_t* pfull = empty + nst;              // [3] all 16 partials of the group written
+  uint64_t* pempty = pfull + kShrinkPartBufs;  // [3] the group's partials have been read
+  int32_t* loaded = reinterpret_cast<int32_t*>(pempty + kShrinkPartBufs);  // [nst] last item armed, -1 none
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(loaded + nst);
   int32_t* tok_s = reinterpret_cast<int32_t*>(smem + plan.tok_off);
   int32_t* tab_mem = reinterpret_cast<int32_t*>(smem + plan.tab_off);
 
@@ -351,7 +428,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   griddep_launch();  // the expand may start on SMs this grid releases
   const SlotTab tab = stage_slot_tab(args.seg, args.ranks, nullptr, tab_mem);
   if (threadIdx.x == 0) {
-    ring.init();
+    for (int i = 0; i < nst; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kStreamWarps);
+      loaded[i] = -1;
+    }
     for (int i = 0; i < kShrinkPartBufs; ++i) {
       mbar_init(&pfull[i], kStreamWarps);
       mbar_init(&pempty[i], 1);
@@ -366,110 +447,142 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   if (begin >= end) return;  // uniform across the CTA
   const uint32_t stage0 = smem_u32(smem);
   const uint32_t row_bytes = (uint32_t)K * 2;
-  const uint64_t pol = l2_evict_first_policy();
-  // item ii: a weight stage (8 contiguous K*2-byte pieces of A[slot]) or 8 token rows
-  auto issue = [&](int ii, const RingItem& q) {
-    const int s = ii % nst;
-    const uint32_t dst = stage0 + s * plan.stage_bytes;
-    if (q.part >= 0) {
-      ring_issue_weights(ring, ii, args.a + ((int64_t)q.slot * 2 + q.part) * 8 * row_bytes, dst, row_bytes, row_bytes,
-                         pol, lane);
-      return;
-    }
-    if (lane == 0) ring_arm(ring, s, ii, (uint32_t)q.cnt * row_bytes);
-    __syncwarp();
-    if (lane < q.cnt)
-      bulk_load(dst + lane * plan.pitch, args.x + (int64_t)tok_s[q.start + lane] * row_bytes, row_bytes,
-                &ring.full[s], pol);
-  };
-
-  RingSeq lc;  // load cursor: nst items ahead of consumption; warp 0 issues the first nst
-  lc.init(tab, begin, end);
+  const uint32_t slot_bytes = (uint32_t)K * (kStreamRank * 2);  // A[slot]: K rows of 32 bytes
+  RingSeq it;  // the share's token groups (the producer's and every consumer's own cursor)
+  it.init(tab, begin, end, false, false);
   RingItem q;
-  {
-    // weight stages first (they need only the table), token stages once the ids are staged
-    RingSeq pre = lc;
-    for (int ii = 0; ii < nst && pre.next(tab, begin, q); ++ii)
-      if (warp == 0 && q.part >= 0) issue(ii, q);
-    stream_stage_tokens(args.seg.token_index, begin, end, tok_s);
-    __syncthreads();
-    for (int ii = 0; ii < nst && lc.next(tab, begin, q); ++ii)
-      if (warp == 0 && q.part < 0) issue(ii, q);
-  }
-
-  const int g = lane >> 2;  // fragment row group
-  const int t = lane & 3;   // lane within the quad
-  const int ks = K >> 8;    // k16 steps of this warp's K slice (K / 16 rows)
-  const int kw0 = warp * (K >> 4);
-  const int my_part = warp / (kStreamWarps / kStreamWeightParts);
-  uint32_t a[16][4];  // A^T fragments of the warp's K slice (rank rows g, g + 8)
-  // ldmatrix row of this lane in a token stage: token row lane & 7, k offset kw0 + 8 (lane >> 3)
-  const uint32_t ld_off = (uint32_t)(lane & 7) * plan.pitch + (uint32_t)(kw0 + 8 * (lane >> 3)) * 2;
-  // ldmatrix.trans row of this lane in its weight stage: k = 16 j + 8 (m >> 1) + (lane & 7)
-  // of the warp's slice, rank half m & 1, for matrix m = lane >> 3
-  const uint32_t w_off = (uint32_t)(kw0 - my_part * (K >> 1) + 8 * (lane >> 4) + (lane & 7)) * 32 +
-                         16 * ((lane >> 3) & 1);
-  uint16_t* tmp = reinterpret_cast<uint16_t*>(args.tmp);
-  uint16_t* tile = reinterpret_cast<uint16_t*>(smem + plan.rg_off) + warp * kStreamGroup * kStreamRank;
-  int32_t* pmeta = reinterpret_cast<int32_t*>(smem + plan.rg_off + kShrinkTmpTileBytes);  // [3][slot, cnt, start]
-  // Adds the 16 partials of group gi (warp order), rounds and writes its tmp rows.
-  auto reduce = [&](int gi) -> bool {
-    const int pb = gi % kShrinkPartBufs;
-    if (!mbar_wait_warp(&pfull[pb], (uint32_t)(gi / kShrinkPartBufs) & 1u, abort_flag)) return false;
-    const int g_slot = pmeta[3 * pb], g_cnt = pmeta[3 * pb + 1], g_start = pmeta[3 * pb + 2];
-    const float* pp = part + (size_t)pb * (kShrinkPartBytes / 4);
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int w = 0; w < kStreamWarps; ++w) {
-      const float4 u = *reinterpret_cast<const float4*>(pp + (w * 32 + lane) * 4);
-      v[0] += u.x;
-      v[1] += u.y;
-      v[2] += u.z;
-      v[3] += u.w;
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&pempty[pb]);
-    // rounded values -> the warp's tile [token][rank]; then lane l writes 16 bytes
-    // (ranks 8 (l & 1) ..) of token l >> 1 with one vector store
-    const int n_eff = min(tab.rk[g_slot] * args.stack_num, args.R);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      tile[(2 * t + h) * kStreamRank + g] = E::from_f(g < n_eff ? v[h] : 0.f);
-      tile[(2 * t + h) * kStreamRank + g + 8] = E::from_f(g + 8 < n_eff ? v[2 + h] : 0.f);
-    }
-    __syncwarp();
-    if (lane < 2 * g_cnt) {
-      const int64_t row = (int64_t)tok_s[g_start + (lane >> 1)] * args.R;
-      *reinterpret_cast<uint4*>(tmp + row + 8 * (lane & 1)) = reinterpret_cast<const uint4*>(tile)[lane];
-    }
-    __syncwarp();
-    return true;
-  };
-
-  RingSeq it;
-  it.init(tab, begin, end);
-  int ii = 0, ti = 0;
-  RingItem cq;
   bool ok = true;
-  while (it.next(tab, begin, cq)) {
-    const int s = ii % nst;
-    if (!mbar_wait_warp(&ring.full[s], (uint32_t)(ii / nst) & 1u, abort_flag)) {
-      ok = false;
-      break;
-    }
-    const uint32_t sbase = stage0 + s * plan.stage_bytes;
-    // two accumulators (even / odd k16 steps) halve the dependent mma chain
-    float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
-    if (cq.part >= 0) {  // weight stage: the warps of this half take their A fragments
-      if (cq.part == my_part) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (j < ks) ldsm_x4_t(sbase + w_off + 16 * 32 * j, a[j]);
+
+  if (warp >= kStreamWarps) {
+    // ------------------------------------------------ producer warpgroup
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kShrinkProducerRegs));
+    if (warp == kStreamWarps) {
+      stream_stage_tokens_warp(args.seg.token_index, begin, end, tok_s, lane);
+      __syncwarp();
+      // the consumers request their weights only now: their 128 KB of loads
+      // would otherwise queue ahead of these few bytes
+      named_barrier_arrive(kShrinkIdsReady, kStreamThreads + 32);
+      const uint64_t pol = l2_evict_first_policy();
+      int pf_slot = -1;  // slot of the previous group (its rows are in L2 or on their way)
+      for (int ii = 0; ok && it.next(tab, begin, q); ++ii) {
+        const int s = ii % nst;
+        // stage s is free once the 16 consumers released item ii - nst
+        if (ii >= nst && !mbar_wait_warp(&empty[s], (uint32_t)(ii / nst - 1) & 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          loaded[s] = ii;
+          mbar_arrive_expect_tx(&full[s], (uint32_t)q.cnt * row_bytes);
+          if (pf_slot >= 0 && q.slot != pf_slot)  // the consumers load the first slot themselves
+            prefetch_l2_bulk(args.a + (int64_t)q.slot * slot_bytes, slot_bytes);
+        }
+        pf_slot = q.slot;
+        __syncwarp();
+        if (lane < q.cnt)
+          bulk_load(stage0 + s * plan.stage_bytes + lane * plan.pitch,
+                    args.x + (int64_t)tok_s[q.start + lane] * row_bytes, row_bytes, &full[s], pol);
       }
-    } else {
-      // D^T (rank g / g + 8 x token 2t, 2t + 1); stage rows >= cnt hold stale
-      // data that only reaches the discarded token columns
-      const uint32_t base = sbase + ld_off;
+    }
+  } else {
+    // ------------------------------------------------ consumers
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kShrinkConsumerRegs));
+    const int g = lane >> 2;  // fragment row group
+    const int t = lane & 3;   // lane within the quad
+    const int ks = K >> 8;    // k16 steps of this warp's K slice (K / 16 rows)
+    const int kw0 = warp * (K >> 4);
+    uint32_t a[16][4];  // A^T fragments of the warp's K slice (mma rows g, g + 8; ranks permuted)
+    // issues the loads of the slot's fragments in row layout; to_mma_layout() finishes them
+    auto load_a = [&](int slot) {
+      const uint8_t* src = args.a + (int64_t)slot * slot_bytes + (int64_t)(kw0 + g) * 32 + 8 * t;
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j < ks) {
+          const uint2 lo = ld_nc_v2(src + j * 16 * 32);
+          const uint2 hi = ld_nc_v2(src + j * 16 * 32 + 8 * 32);
+          a[j][0] = lo.x;
+          a[j][1] = lo.y;
+          a[j][2] = hi.x;
+          a[j][3] = hi.y;
+        }
+    };
+    auto to_mma_layout = [&]() {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j < ks) {
+#pragma unroll
+          for (int m = 0; m < 4; ++m) a[j][m] = movmatrix_t(a[j][m]);
+        }
+    };
+    int cur_slot = -1;     // slot whose fragments are in a[] (or on their way)
+    bool convert = false;  // a[] holds raw loads still to be transposed
+    named_barrier(kShrinkIdsReady, kStreamThreads + 32);  // the producer has its token ids
+    {
+      RingSeq first = it;
+      if (first.next(tab, begin, q)) {  // requested while the first token rows are on their way
+        load_a(q.slot);
+        cur_slot = q.slot;
+        convert = true;
+      }
+    }
+    // ldmatrix row of this lane in a token stage: token row lane & 7, k offset kw0 + 8 (lane >> 3)
+    const uint32_t ld_off = (uint32_t)(lane & 7) * plan.pitch + (uint32_t)(kw0 + 8 * (lane >> 3)) * 2;
+    uint16_t* tmp = reinterpret_cast<uint16_t*>(args.tmp);
+    uint16_t* tile = reinterpret_cast<uint16_t*>(smem + plan.rg_off) + warp * kStreamGroup * kStreamRank;
+    int32_t* pmeta = reinterpret_cast<int32_t*>(smem + plan.rg_off + kShrinkTmpTileBytes);  // [3][slot, cnt, start]
+    const int rank_lo = shrink_rank_of_row(g), rank_hi = shrink_rank_of_row(g + 8);
+    // Adds the 16 partials of group gi (warp order), rounds and writes its tmp
+    // rows.  The token ids it reads were staged before stage 0 was armed.
+    auto reduce = [&](int gi) -> bool {
+      const int pb = gi % kShrinkPartBufs;
+      if (!mbar_wait_warp(&pfull[pb], (uint32_t)(gi / kShrinkPartBufs) & 1u, abort_flag)) return false;
+      const int g_slot = pmeta[3 * pb], g_cnt = pmeta[3 * pb + 1], g_start = pmeta[3 * pb + 2];
+      const float* pp = part + (size_t)pb * (kShrinkPartBytes / 4);
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int w = 0; w < kStreamWarps; ++w) {
+        const float4 u = *reinterpret_cast<const float4*>(pp + (w * 32 + lane) * 4);
+        v[0] += u.x;
+        v[1] += u.y;
+        v[2] += u.z;
+        v[3] += u.w;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pempty[pb]);
+      // rounded values -> the warp's tile [token][rank]; then lane l writes 16 bytes
+      // (ranks 8 (l & 1) ..) of token l >> 1 with one vector store
+      const int n_eff = min(tab.rk[g_slot] * args.stack_num, args.R);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        tile[(2 * t + h) * kStreamRank + rank_lo] = E::from_f(rank_lo < n_eff ? v[h] : 0.f);
+        tile[(2 * t + h) * kStreamRank + rank_hi] = E::from_f(rank_hi < n_eff ? v[2 + h] : 0.f);
+      }
+      __syncwarp();
+      if (lane < 2 * g_cnt) {
+        const int64_t row = (int64_t)tok_s[g_start + (lane >> 1)] * args.R;
+        *reinterpret_cast<uint4*>(tmp + row + 8 * (lane & 1)) = reinterpret_cast<const uint4*>(tile)[lane];
+      }
+      __syncwarp();
+      return true;
+    };
+
+    int ii = 0;
+    RingItem cq;
+    while (it.next(tab, begin, cq)) {
+      const int s = ii % nst;
+      if (!mbar_wait_warp(&full[s], (uint32_t)(ii / nst) & 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      if (convert) {
+        to_mma_layout();
+        convert = false;
+      }
+      // D^T (mma rows g / g + 8 x token 2t, 2t + 1); stage rows >= cnt hold stale
+      // data that only reaches the discarded token columns.  Two accumulators
+      // (even / odd k16 steps) halve the dependent mma chain.
+      float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t base = stage0 + s * plan.stage_bytes + ld_off;
 #pragma unroll
       for (int j = 0; j < 16; j += 2)
         if (j < ks) {
@@ -478,47 +591,56 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           mma_16816<BF16>(acc, a[j], b[0], b[1]);
           mma_16816<BF16>(acc2, a[j + 1], b[2], b[3]);
         }
+      // the stage's rows have been read (the mma consumed them): release it
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      // the next group of another slot: its weights are requested now, to land
+      // while this group is published and reduced
+      {
+        RingSeq peek = it;
+        RingItem nx;
+        if (peek.next(tab, begin, nx) && nx.slot != cur_slot) {
+          load_a(nx.slot);
+          cur_slot = nx.slot;
+          convert = true;
+        }
+      }
+      const int ti = ii++;
+      // group ti - 2's reduction falls to warp (ti - 2) mod 16
+      const int rg = ti - kShrinkReduceLag;
+      if (rg >= 0 && (rg & (kStreamWarps - 1)) == warp && !reduce(rg)) {
+        ok = false;
+        break;
+      }
+      // this group's partial -> buffer ti mod 3, once the group 3 earlier has been read
+      const int pb = ti % kShrinkPartBufs;
+      if (ti >= kShrinkPartBufs &&
+          !mbar_wait_warp(&pempty[pb], (uint32_t)(ti / kShrinkPartBufs - 1) & 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
+      float* pp = part + (size_t)pb * (kShrinkPartBytes / 4);
+      *reinterpret_cast<float4*>(pp + (warp * 32 + lane) * 4) =
+          make_float4(acc[0] + acc2[0], acc[1] + acc2[1], acc[2] + acc2[2], acc[3] + acc2[3]);
+      if (warp == 0 && lane == 0) {  // the group this buffer now holds, for its reducer
+        pmeta[3 * pb] = cq.slot;
+        pmeta[3 * pb + 1] = cq.cnt;
+        pmeta[3 * pb + 2] = cq.start;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pfull[pb]);
     }
-    // the 16th warp out of the stage refills it with item ii + nst
-    const bool refill = ring.release(s, lane);
-    RingItem nq;
-    if (lc.next(tab, begin, nq) && refill) issue(ii + nst, nq);
-    ++ii;
-    if (cq.part >= 0) continue;
-
-    // group ti - 2's reduction falls to warp (ti - 2) mod 16
-    const int rg = ti - kShrinkReduceLag;
-    if (rg >= 0 && (rg & (kStreamWarps - 1)) == warp && !reduce(rg)) {
-      ok = false;
-      break;
-    }
-    // this group's partial -> buffer ti mod 3, once the group 3 earlier has been read
-    const int pb = ti % kShrinkPartBufs;
-    if (ti >= kShrinkPartBufs &&
-        !mbar_wait_warp(&pempty[pb], (uint32_t)(ti / kShrinkPartBufs - 1) & 1u, abort_flag)) {
-      ok = false;
-      break;
-    }
-    float* pp = part + (size_t)pb * (kShrinkPartBytes / 4);
-    *reinterpret_cast<float4*>(pp + (warp * 32 + lane) * 4) =
-        make_float4(acc[0] + acc2[0], acc[1] + acc2[1], acc[2] + acc2[2], acc[3] + acc2[3]);
-    if (warp == 0 && lane == 0) {  // the group this buffer now holds, for its reducer
-      pmeta[3 * pb] = cq.slot;
-      pmeta[3 * pb + 1] = cq.cnt;
-      pmeta[3 * pb + 2] = cq.start;
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&pfull[pb]);
-    ++ti;
-  }
-  // the reductions of the last groups
+    // the reductions of the last groups
 #pragma unroll
-  for (int k = 0; k < kShrinkReduceLag; ++k) {
-    const int rg = ti - kShrinkReduceLag + k;
-    if (ok && rg >= 0 && (rg & (kStreamWarps - 1)) == warp) ok = reduce(rg);
+    for (int k = 0; k < kShrinkReduceLag; ++k) {
+      const int rg = ii - kShrinkReduceLag + k;
+      if (ok && rg >= 0 && (rg & (kStreamWarps - 1)) == warp) ok = reduce(rg);
+    }
   }
   __syncthreads();  // every warp is out of its loop
-  if (threadIdx.x == 0) ring.drain();
+  if (threadIdx.x == 0)  // the last copy into each stage has landed (unless the roles gave up early)
+    for (int s = 0; s < nst; ++s)
+      if (loaded[s] >= 0) mbar_drain(&full[s], (uint32_t)(loaded[s] / nst) & 1u);
 }
 
 // ============================================================== expand
