@@ -76,9 +76,12 @@ std::atomic<int32_t> g_stream_kernels{1};
 bool stream_share_ok(int64_t num_tokens, const DeviceInfo* di) {
   return (num_tokens + di->sm_count - 1) / di->sm_count <= kStreamMaxShare;
 }
-bool stream_shrink_ok(int64_t R, int64_t K, int64_t num_tokens, const DeviceInfo* di) {
+// The shrink's shares are cost-balanced (stream_share): a share holds at most
+// ceil((tokens + kShrinkSlotCost * active slots) / SMs) + 1 tokens.
+bool stream_shrink_ok(int64_t R, int64_t K, int64_t num_tokens, int64_t num_slots, const DeviceInfo* di) {
+  const int64_t virt = num_tokens + kShrinkSlotCost * num_slots;
   return g_stream_kernels.load(std::memory_order_relaxed) != 0 && R == kStreamRank && K % 512 == 0 &&
-         K <= kStreamMaxDim && stream_share_ok(num_tokens, di);
+         K <= kStreamMaxDim && (virt + di->sm_count - 1) / di->sm_count + 1 <= kStreamMaxShare;
 }
 bool stream_expand_ok(int64_t R, int64_t N, int64_t num_tokens, const DeviceInfo* di) {
   return g_stream_kernels.load(std::memory_order_relaxed) != 0 && R == kStreamRank && N % 512 == 0 &&
@@ -360,7 +363,7 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
 #undef LAUNCH_SHRINK_GRID
       return check_launch("sgmv_shrink_grid_kernel");
     }
-    if (stream_shrink_ok(R, K, num_tokens, di)) {  // rank 16: rows through a bulk-copy ring, A in registers
+    if (stream_shrink_ok(R, K, num_tokens, seg.num_slots, di)) {  // rank 16: rows through a bulk-copy ring, A in registers
       const StreamPlan plan = shrink_stream_plan(K, seg.num_slots);
       if (plan.nst >= 2) {
         // the kernel reads its inputs only after griddep_wait(): always launched programmatically

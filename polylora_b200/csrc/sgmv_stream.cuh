@@ -292,6 +292,62 @@ struct RingSeq {
   }
 };
 
+// Cost-balanced shares.  A token costs 1 and every run of an active slot
+// (rank > 0, at least one token) costs `slot_cost` more: the slot's weights,
+// which every CTA whose share reaches into the run loads in full.  In the
+// "virtual" coordinate VS_j = slot_start[j] + slot_cost * (active slots before
+// j) a slot's weights come first, then its tokens; CTA b of G takes virtual
+// [V b / G, V (b + 1) / G), V = total + slot_cost * active slots, and
+// stream_cut maps a virtual coordinate to the token position it cuts at (a
+// cut inside a slot's weight units falls at the slot's first token).  So a
+// share that reaches into one more slot holds fewer tokens, and the CTAs
+// finish together.  Monotone in v, cut(0) = 0 and cut(V) = total, so the
+// shares are contiguous and cover the list.  Warp-collective: every lane
+// returns the cut; reads the staged slot table only.
+__device__ __forceinline__ bool slot_active(const SlotTab& t, int j) {
+  return t.rk[j] > 0 && t.ss[j + 1] > t.ss[j];
+}
+
+__device__ int64_t stream_cut(const SlotTab& t, int64_t v, int64_t slot_cost, int lane) {
+  int64_t carry = 0;                         // active slots before this chunk of 32
+  int J = 0;                                 // the last slot j with VS_j <= v ...
+  int64_t vsJ = 0;                           // ... its VS_j
+  bool actJ = t.ns > 0 && slot_active(t, 0);  // ... and whether it is active
+  for (int c = 0; c <= t.ns; c += 32) {
+    const int j = c + lane;
+    const bool valid = j <= t.ns;
+    const bool act = j < t.ns && slot_active(t, j);
+    const uint32_t am = __ballot_sync(0xffffffffu, act);
+    const int64_t vs = valid ? t.ss[j] + slot_cost * (carry + __popc(am & ((1u << lane) - 1u))) : 0;
+    const uint32_t le = __ballot_sync(0xffffffffu, valid && vs <= v);  // a prefix of the lanes
+    if (le != 0u) {
+      const int last = 31 - __clz(le);
+      J = c + last;
+      vsJ = __shfl_sync(0xffffffffu, vs, last);
+      actJ = (am >> last) & 1u;
+    }
+    if (le != 0xffffffffu) break;  // VS is non-decreasing: no later slot qualifies
+    carry += __popc(am);
+  }
+  if (J >= t.ns) return t.ss[t.ns];
+  const int64_t off = v - vsJ, s0 = t.ss[J], s1 = t.ss[J + 1];
+  if (actJ) return off <= slot_cost ? s0 : min(s0 + off - slot_cost, s1);
+  return min(s0 + off, s1);
+}
+
+// [begin, end) of CTA b of G (warp-collective, see stream_cut).
+__device__ __forceinline__ void stream_share(const SlotTab& t, int b, int G, int64_t slot_cost, int lane,
+                                             int64_t& begin, int64_t& end) {
+  int nact = 0;
+  for (int c = 0; c < t.ns; c += 32) {
+    const int j = c + lane;
+    nact += __popc(__ballot_sync(0xffffffffu, j < t.ns && slot_active(t, j)));
+  }
+  const int64_t V = (int64_t)t.ss[t.ns] + slot_cost * nact;
+  begin = stream_cut(t, V * b / G, slot_cost, lane);
+  end = stream_cut(t, V * (b + 1) / G, slot_cost, lane);
+}
+
 // A ring of `n` stages in shared memory: full barriers, release counts and
 // the last item index loaded into each stage.
 struct StreamRing {
@@ -398,6 +454,9 @@ constexpr int kShrinkLaunchRegs = 96;                 // 5 warps per scheduler p
 constexpr int kShrinkConsumerRegs = 112;
 constexpr int kShrinkProducerRegs = 32;
 constexpr int kShrinkIdsReady = 1;  // named barrier: the producer has staged the token ids
+// Extra cost of a slot's run in a share, in tokens: loading the slot's 128 KB
+// of LoRA-A (16 rows' worth of x bytes) and the stall around it.
+constexpr int64_t kShrinkSlotCost = 20;
 // per scheduler partition: 4 consumer warps + 1 producer-group warp within the launch's registers
 static_assert(4 * kShrinkConsumerRegs + kShrinkProducerRegs <= 5 * kShrinkLaunchRegs, "register split");
 static_assert(5 * 32 * kShrinkLaunchRegs <= 16384, "launch registers per partition");
@@ -441,9 +500,8 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
     fence_barrier_init();
   }
   __syncthreads();  // slot table staged, barriers initialised
-  const int64_t total = tab.ss[tab.ns];
-  const int64_t begin = total * blockIdx.x / gridDim.x;
-  const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
+  int64_t begin, end;  // this CTA's share, the same in every warp
+  stream_share(tab, blockIdx.x, gridDim.x, kShrinkSlotCost, lane, begin, end);
   if (begin >= end) return;  // uniform across the CTA
   const uint32_t stage0 = smem_u32(smem);
   const uint32_t row_bytes = (uint32_t)K * 2;
