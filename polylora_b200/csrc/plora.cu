@@ -71,21 +71,20 @@ std::atomic<int64_t> g_wsplit_tokens_per_sm{16};
 // this is non-zero (the default); 0 keeps them on the windowed mma kernels.
 std::atomic<int32_t> g_stream_kernels{1};
 
-// A CTA's share of the token list (at most ceil(num_tokens / SMs)) must fit
-// the stream kernels' shared-memory copy of its token ids.
-bool stream_share_ok(int64_t num_tokens, const DeviceInfo* di) {
-  return (num_tokens + di->sm_count - 1) / di->sm_count <= kStreamMaxShare;
+// A CTA's share of the token list must fit the stream kernels' shared-memory
+// copy of its token ids.  Shares are cost-balanced (stream_share): one holds at
+// most ceil((tokens + slot_cost * active slots) / SMs) + 1 tokens.
+bool stream_share_ok(int64_t num_tokens, int64_t num_slots, int64_t slot_cost, const DeviceInfo* di) {
+  const int64_t virt = num_tokens + slot_cost * num_slots;
+  return (virt + di->sm_count - 1) / di->sm_count + 1 <= kStreamMaxShare;
 }
-// The shrink's shares are cost-balanced (stream_share): a share holds at most
-// ceil((tokens + kShrinkSlotCost * active slots) / SMs) + 1 tokens.
 bool stream_shrink_ok(int64_t R, int64_t K, int64_t num_tokens, int64_t num_slots, const DeviceInfo* di) {
-  const int64_t virt = num_tokens + kShrinkSlotCost * num_slots;
   return g_stream_kernels.load(std::memory_order_relaxed) != 0 && R == kStreamRank && K % 512 == 0 &&
-         K <= kStreamMaxDim && (virt + di->sm_count - 1) / di->sm_count + 1 <= kStreamMaxShare;
+         K <= kStreamMaxDim && stream_share_ok(num_tokens, num_slots, kShrinkSlotCost, di);
 }
-bool stream_expand_ok(int64_t R, int64_t N, int64_t num_tokens, const DeviceInfo* di) {
+bool stream_expand_ok(int64_t R, int64_t N, int64_t num_tokens, int64_t num_slots, const DeviceInfo* di) {
   return g_stream_kernels.load(std::memory_order_relaxed) != 0 && R == kStreamRank && N % 512 == 0 &&
-         N <= kStreamMaxDim && stream_share_ok(num_tokens, di);
+         N <= kStreamMaxDim && stream_share_ok(num_tokens, num_slots, 0, di);  // equal token shares
 }
 
 bool use_weight_split(int64_t num_tokens, const DeviceInfo* di) {
@@ -449,7 +448,7 @@ int expand_impl(const void* tmp, const void* b, void* y, const int32_t* ranks, c
 #undef LAUNCH_EXPAND_GRID
       return check_launch("sgmv_expand_grid_kernel");
     }
-    if (stream_expand_ok(R, N, num_tokens, di)) {  // rank 16: rows through a bulk-copy ring, B in registers
+    if (stream_expand_ok(R, N, num_tokens, seg.num_slots, di)) {  // rank 16: rows through a bulk-copy ring, B in registers
       const StreamPlan plan = expand_stream_plan(N, seg.num_slots);
       if (plan.smem_bytes <= (uint32_t)kStreamSmemLimit) {
         // programmatic only right after this library's shrink (after_shrink): the kernel

@@ -732,6 +732,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     fence_barrier_init();
   }
   __syncthreads();  // slot table staged, barriers initialised
+  // equal token shares: the weight ring prefetches a slot change, so it adds
+  // little to a share's time (charging slot runs as the shrink does measured
+  // slower)
   const int64_t total = tab.ss[tab.ns];
   const int64_t begin = total * blockIdx.x / gridDim.x;
   const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
