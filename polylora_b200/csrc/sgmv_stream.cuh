@@ -297,55 +297,86 @@ struct RingSeq {
 // which every CTA whose share reaches into the run loads in full.  In the
 // "virtual" coordinate VS_j = slot_start[j] + slot_cost * (active slots before
 // j) a slot's weights come first, then its tokens; CTA b of G takes virtual
-// [V b / G, V (b + 1) / G), V = total + slot_cost * active slots, and
-// stream_cut maps a virtual coordinate to the token position it cuts at (a
-// cut inside a slot's weight units falls at the slot's first token).  So a
-// share that reaches into one more slot holds fewer tokens, and the CTAs
-// finish together.  Monotone in v, cut(0) = 0 and cut(V) = total, so the
-// shares are contiguous and cover the list.  Warp-collective: every lane
-// returns the cut; reads the staged slot table only.
-__device__ __forceinline__ bool slot_active(const SlotTab& t, int j) {
-  return t.rk[j] > 0 && t.ss[j + 1] > t.ss[j];
-}
+// [V b / G, V (b + 1) / G), V = total + slot_cost * active slots, and a cut at
+// virtual v falls at token position
+//   s_J                                  v - VS_J <= slot_cost, J active
+//   min(s_J + v - VS_J - slot_cost, s_J+1)  otherwise for an active J
+//   min(s_J + v - VS_J, s_J+1)            J inactive
+// with J the last slot whose VS_J <= v (a cut inside a slot's weight units
+// falls at its first token).  So a share that reaches into one more slot
+// holds fewer tokens, and the CTAs finish together.  The cut is monotone in
+// v, 0 at v = 0 and total at v = V, so the shares are contiguous and cover
+// the list; a share holds at most ceil(V / G) + 1 tokens.
+struct StreamCut {
+  int J = 0;
+  int64_t vs = 0;
+  bool act = false;
+  __device__ __forceinline__ int64_t position(const SlotTab& t, int64_t v, int64_t slot_cost) const {
+    if (J >= t.ns) return t.ss[t.ns];
+    const int64_t off = v - vs, s0 = t.ss[J], s1 = t.ss[J + 1];
+    if (act) return off <= slot_cost ? s0 : min(s0 + off - slot_cost, s1);
+    return min(s0 + off, s1);
+  }
+};
 
-__device__ int64_t stream_cut(const SlotTab& t, int64_t v, int64_t slot_cost, int lane) {
-  int64_t carry = 0;                         // active slots before this chunk of 32
-  int J = 0;                                 // the last slot j with VS_j <= v ...
-  int64_t vsJ = 0;                           // ... its VS_j
-  bool actJ = t.ns > 0 && slot_active(t, 0);  // ... and whether it is active
+// [begin, end) of CTA b of G, both cuts found in one walk over the staged slot
+// table, 32 slots per step.  `nact` is the number of active slots.
+// Warp-collective: every lane returns the share.
+__device__ void stream_share(const SlotTab& t, int nact, int b, int G, int64_t slot_cost, int lane, int64_t& begin,
+                             int64_t& end) {
+  const int64_t V = (int64_t)t.ss[t.ns] + slot_cost * nact;
+  const int64_t v0 = V * b / G, v1 = V * (b + 1) / G;
+  StreamCut c0, c1;
+  int64_t carry = 0;  // active slots before this step's 32
   for (int c = 0; c <= t.ns; c += 32) {
     const int j = c + lane;
     const bool valid = j <= t.ns;
-    const bool act = j < t.ns && slot_active(t, j);
+    const bool act = j < t.ns && t.rk[j] > 0 && t.ss[j + 1] > t.ss[j];
     const uint32_t am = __ballot_sync(0xffffffffu, act);
     const int64_t vs = valid ? t.ss[j] + slot_cost * (carry + __popc(am & ((1u << lane) - 1u))) : 0;
-    const uint32_t le = __ballot_sync(0xffffffffu, valid && vs <= v);  // a prefix of the lanes
-    if (le != 0u) {
-      const int last = 31 - __clz(le);
-      J = c + last;
-      vsJ = __shfl_sync(0xffffffffu, vs, last);
-      actJ = (am >> last) & 1u;
+    // VS is non-decreasing, so the slots with VS_j <= v are a prefix of the lanes
+    const uint32_t le0 = __ballot_sync(0xffffffffu, valid && vs <= v0);
+    const uint32_t le1 = __ballot_sync(0xffffffffu, valid && vs <= v1);
+    if (le0 != 0u) {
+      const int last = 31 - __clz(le0);
+      c0.J = c + last;
+      c0.vs = __shfl_sync(0xffffffffu, vs, last);
+      c0.act = (am >> last) & 1u;
     }
-    if (le != 0xffffffffu) break;  // VS is non-decreasing: no later slot qualifies
+    if (le1 != 0u) {
+      const int last = 31 - __clz(le1);
+      c1.J = c + last;
+      c1.vs = __shfl_sync(0xffffffffu, vs, last);
+      c1.act = (am >> last) & 1u;
+    }
+    if (le1 != 0xffffffffu) break;  // v0 <= v1: both cuts are found
     carry += __popc(am);
   }
-  if (J >= t.ns) return t.ss[t.ns];
-  const int64_t off = v - vsJ, s0 = t.ss[J], s1 = t.ss[J + 1];
-  if (actJ) return off <= slot_cost ? s0 : min(s0 + off - slot_cost, s1);
-  return min(s0 + off, s1);
+  begin = c0.position(t, v0, slot_cost);
+  end = c1.position(t, v1, slot_cost);
 }
 
-// [begin, end) of CTA b of G (warp-collective, see stream_cut).
-__device__ __forceinline__ void stream_share(const SlotTab& t, int b, int G, int64_t slot_cost, int lane,
-                                             int64_t& begin, int64_t& end) {
-  int nact = 0;
-  for (int c = 0; c < t.ns; c += 32) {
-    const int j = c + lane;
-    nact += __popc(__ballot_sync(0xffffffffu, j < t.ns && slot_active(t, j)));
+// stage_slot_tab, also counting how many of the slots this thread staged are
+// active (rank > 0, at least one token); the table's scale column is not
+// written.
+__device__ __forceinline__ SlotTab stage_slot_tab_counted(const SegTable& t, const int32_t* ranks, int32_t* dst,
+                                                          int& active_mine) {
+  const int ns = t.num_slots;
+  int32_t* ss = dst;
+  int32_t* rk = dst + ns + 1;
+  float* sc = reinterpret_cast<float*>(dst + 2 * ns + 1);
+  active_mine = 0;
+  for (int i = threadIdx.x; i <= ns; i += blockDim.x) {
+    const int32_t s0 = ld_cg_i32(t.slot_start + i);
+    ss[i] = s0;
+    if (i < ns) {
+      const int32_t s1 = ld_cg_i32(t.slot_start + i + 1);
+      const int32_t r = __ldg(ranks + i);
+      rk[i] = r;
+      active_mine += (r > 0 && s1 > s0) ? 1 : 0;
+    }
   }
-  const int64_t V = (int64_t)t.ss[t.ns] + slot_cost * nact;
-  begin = stream_cut(t, V * b / G, slot_cost, lane);
-  end = stream_cut(t, V * (b + 1) / G, slot_cost, lane);
+  return SlotTab{ss, rk, sc, ns};
 }
 
 // A ring of `n` stages in shared memory: full barriers, release counts and
@@ -457,6 +488,7 @@ constexpr int kShrinkIdsReady = 1;  // named barrier: the producer has staged th
 // Extra cost of a slot's run in a share, in tokens: loading the slot's 128 KB
 // of LoRA-A (16 rows' worth of x bytes) and the stall around it.
 constexpr int64_t kShrinkSlotCost = 20;
+static_assert(kFastPathMaxSlots <= 2 * kShrinkThreads, "a thread stages at most 2 slots");
 // per scheduler partition: 4 consumer warps + 1 producer-group warp within the launch's registers
 static_assert(4 * kShrinkConsumerRegs + kShrinkProducerRegs <= 5 * kShrinkLaunchRegs, "register split");
 static_assert(5 * 32 * kShrinkLaunchRegs <= 16384, "launch registers per partition");
@@ -485,7 +517,8 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   const int lane = threadIdx.x & 31;
   griddep_wait();    // inputs (segment table, x) come from earlier kernels
   griddep_launch();  // the expand may start on SMs this grid releases
-  const SlotTab tab = stage_slot_tab(args.seg, args.ranks, nullptr, tab_mem);
+  int active_mine;  // active slots among those this thread staged (<= 2)
+  const SlotTab tab = stage_slot_tab_counted(args.seg, args.ranks, tab_mem, active_mine);
   if (threadIdx.x == 0) {
     for (int i = 0; i < nst; ++i) {
       mbar_init(&full[i], 1);
@@ -499,9 +532,10 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  __syncthreads();  // slot table staged, barriers initialised
+  // slot table staged, barriers initialised, active slots counted
+  const int nact = __syncthreads_count(active_mine >= 1) + __syncthreads_count(active_mine >= 2);
   int64_t begin, end;  // this CTA's share, the same in every warp
-  stream_share(tab, blockIdx.x, gridDim.x, kShrinkSlotCost, lane, begin, end);
+  stream_share(tab, nact, blockIdx.x, gridDim.x, kShrinkSlotCost, lane, begin, end);
   if (begin >= end) return;  // uniform across the CTA
   const uint32_t stage0 = smem_u32(smem);
   const uint32_t row_bytes = (uint32_t)K * 2;
