@@ -49,6 +49,7 @@ extern "C" {
 #define PLORA_DEV_SLOT_RANGE 2   /* a weight index outside [0, num_slots) was skipped      */
 #define PLORA_DEV_RANK_RANGE 4   /* a rank outside [0, max_rank] was clamped               */
 #define PLORA_DEV_IMAGE_RANGE 8  /* a slot-image record pointed outside the image: rank 0  */
+#define PLORA_DEV_PADDING 16     /* an attention mask was not right-padded                */
 
 /* Library version string. */
 const char* plora_version(void);
@@ -118,6 +119,19 @@ int plora_build_segments(const int64_t* weight_indices, const int32_t* seq_lens,
                          const int32_t* lora_ranks, int64_t num_rows, int64_t max_seq,
                          int32_t num_slots, int32_t* slot_start, int32_t* token_index,
                          void* workspace, size_t workspace_size, void* stream);
+
+/* Checks on the stream that an attention mask is right-padded, without
+ * reading anything back: mask is (rows, width), contiguous, elements of
+ * mask_elem_bytes (1, 2, 4 or 8) bytes, treated as floats with mask_is_float
+ * (2, 4 or 8 bytes; the sign bit is ignored); seq_lens[r] (int64) is row r's sum
+ * as the caller computed it from the same mask.  A row that is not non-zero
+ * exactly at positions < seq_lens[r] sets PLORA_DEV_PADDING in the device
+ * status word, which plora_device_status() reports later.  Replaces the
+ * host-synchronising comparison of src/polylora/context.py:37-45
+ * (assert_right_padded) for callers that keep the forward free of host
+ * synchronisation. */
+int plora_check_right_padded(const void* mask, int32_t mask_elem_bytes, int32_t mask_is_float,
+                             const int64_t* seq_lens, int64_t rows, int64_t width, void* stream);
 
 /* Reference-compatible flat tile schedule: src/polylora/sgmv.py:29-61
  * (_build_flat_schedule).  cum_tiles (num_rows+1,) and num_n_tiles (num_rows,)

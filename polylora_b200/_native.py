@@ -28,6 +28,7 @@ DEV_WAIT_TIMEOUT = 1
 DEV_SLOT_RANGE = 2
 DEV_RANK_RANGE = 4
 DEV_IMAGE_RANGE = 8
+DEV_PADDING = 16
 
 NOALLOC_SCRATCH_BYTES = 8 << 20  # PLORA_NOALLOC_SCRATCH_BYTES
 
@@ -97,6 +98,10 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "plora_flat_schedule": (
         ctypes.c_int,
         [_c_void_p, _c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p, _c_void_p],
+    ),
+    "plora_check_right_padded": (
+        ctypes.c_int,
+        [_c_void_p, _i32, _i32, _c_void_p, _i64, _i64, _c_void_p],
     ),
     "plora_sgmv_a_fwd": (
         ctypes.c_int,
@@ -221,6 +226,29 @@ def set_wait_limit_ns(limit_ns: int) -> int:
     prev = ctypes.c_uint64(0)
     check("plora_set_wait_limit_ns", load().plora_set_wait_limit_ns(int(limit_ns), ctypes.byref(prev)))
     return int(prev.value)
+
+
+def check_right_padded(mask, seq_lens, stream=None) -> None:
+    """Enqueues the device-side right-padding check of a (rows, width) mask
+    (see plora_check_right_padded); a violation shows up later as
+    DEV_PADDING in device_status().  ``seq_lens`` must be the int64 row sums
+    of the same mask, on the same device.  Nothing is read back."""
+    import torch
+
+    if mask.dim() != 2:
+        raise ValueError("attention_mask must be a 2D batch mask")
+    if mask.dtype == torch.bool:
+        m = mask.view(torch.uint8)
+    else:
+        m = mask
+    m = m.contiguous()
+    lens = seq_lens.to(torch.int64).contiguous()
+    is_float = 1 if m.is_floating_point() else 0
+    if stream is None:
+        stream = torch.cuda.current_stream(m.device).cuda_stream
+    check("plora_check_right_padded",
+          load().plora_check_right_padded(m.data_ptr(), m.element_size(), is_float, lens.data_ptr(),
+                                          m.shape[0], m.shape[1], stream))
 
 
 def workspace_size(num_rows: int, max_seq: int, num_slots: int) -> int:

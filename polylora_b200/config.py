@@ -27,6 +27,11 @@ class PolyLoraConfig:
     # threads of the CPU tier's disk prefetch (PolyLoraModel.prefetch); None: 1.
     # No counterpart in the reference.
     prefetch_workers: int | None = None
+    # where enforce_right_padding checks the mask: "host" compares it at once
+    # (the reference's check, which waits for the device), "device" enqueues a
+    # library kernel that records a violation in the device status word, read
+    # by PolyLoraModel.raise_for_device_status().  No counterpart in the reference.
+    right_padding_check: str = "host"
 
     def __post_init__(self) -> None:
         checks = (
@@ -48,6 +53,7 @@ class PolyLoraConfig:
                 self.target_modules is not None and not self.target_modules,
                 "target_modules must not be empty when provided",
             ),
+            (self.right_padding_check not in ("host", "device"), 'right_padding_check must be "host" or "device"'),
         )
         for failed, message in checks:
             if failed:

@@ -48,11 +48,15 @@ def use_lora_context(ctx: LoraBatchContext | None) -> Iterator[None]:
         _CURRENT.reset(token)
 
 
+RIGHT_PADDING_ERROR = "Custom multi-LoRA runtime currently requires right-padded attention_mask"
+
+
 def assert_right_padded(attention_mask: torch.Tensor, seq_lens: torch.Tensor) -> None:
-    """Raises unless every mask row is ones followed by zeros (context.py:37-45)."""
+    """Raises unless every mask row is ones followed by zeros (context.py:37-45).
+    Compares on the host, so it waits for the device."""
     if attention_mask.dim() != 2:
         raise ValueError("attention_mask must be a 2D batch mask")
     width = attention_mask.shape[1]
     expected = torch.arange(width, device=attention_mask.device)[None, :] < seq_lens[:, None]
     if not torch.equal(attention_mask.bool(), expected):
-        raise ValueError("Custom multi-LoRA runtime currently requires right-padded attention_mask")
+        raise ValueError(RIGHT_PADDING_ERROR)

@@ -121,6 +121,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// Bounded wait that ignores the abort flag: used to let copies already issued
+// land before the CTA exits.  Its limit is the fixed 1 s, not the settable
+// wait limit: a copy in flight takes microseconds, and a shortened limit must
+// not let a CTA exit while one still writes its shared memory.  Returns false
+// on expiry (status raised).
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    if (mbar_try_wait_parked(bar, parity)) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      raise_status(PLORA_DEV_WAIT_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // Warp-uniform variant: every lane polls, and the warp proceeds only if all
 // lanes saw the phase complete (so the .sync.aligned ldmatrix / mma that
 // follow never diverge).

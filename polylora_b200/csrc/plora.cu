@@ -584,6 +584,22 @@ int plora_build_segments(const int64_t* weight_indices, const int32_t* seq_lens,
                         static_cast<cudaStream_t>(stream));
 }
 
+int plora_check_right_padded(const void* mask, int32_t mask_elem_bytes, int32_t mask_is_float,
+                             const int64_t* seq_lens, int64_t rows, int64_t width, void* stream) {
+  g_last_error.clear();
+  const bool size_ok = mask_elem_bytes == 1 || mask_elem_bytes == 2 || mask_elem_bytes == 4 || mask_elem_bytes == 8;
+  if (rows < 0 || width < 0 || !size_ok || (mask_is_float && mask_elem_bytes == 1))
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "mask shape or element type");
+  if (rows > INT32_MAX) return fail(PLORA_ERR_UNSUPPORTED, "more than 2^31-1 mask rows");
+  if (rows == 0 || width == 0) return PLORA_OK;
+  if (!mask || !seq_lens) return fail(PLORA_ERR_INVALID_ARGUMENT, "null pointer");
+  if (reinterpret_cast<uintptr_t>(mask) % mask_elem_bytes)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "mask not aligned to its element size");
+  mask_padding_kernel<<<(unsigned)rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(mask), mask_elem_bytes, mask_is_float ? 1 : 0, seq_lens, width);
+  return check_launch("mask_padding_kernel");
+}
+
 int plora_flat_schedule(const int32_t* seq_lens, const int32_t* n_eff, int64_t num_rows,
                         int32_t block_m, int32_t block_n, int32_t* cum_tiles,
                         int32_t* num_n_tiles, void* stream) {

@@ -345,4 +345,31 @@ __global__ void __launch_bounds__(1024) flat_schedule_kernel(const int32_t* __re
   }
 }
 
+// Right-padding check of an attention mask (rows x width, contiguous, elements
+// of elem_bytes bytes): row r must be non-zero exactly at positions <
+// seq_lens[r], seq_lens being the row sums the caller computed from the same
+// mask.  A float mask (is_float) ignores the sign bit, so -0.0 counts as zero
+// as bool() has it.  A violation ORs PLORA_DEV_PADDING into the device status
+// word; nothing is read back.  One block per row.
+// Reference: src/polylora/context.py:37-45 (assert_right_padded).
+__global__ void mask_padding_kernel(const uint8_t* __restrict__ mask, int elem_bytes, int is_float,
+                                    const int64_t* __restrict__ seq_lens, int64_t width) {
+  const int64_t r = blockIdx.x;
+  const int64_t len = seq_lens[r];
+  const uint8_t* row = mask + r * width * elem_bytes;
+  const uint64_t value_bits = !is_float ? ~0ull : (~0ull >> (65 - 8 * elem_bytes));  // drop the sign bit
+  bool bad = false;
+  for (int64_t p = threadIdx.x; p < width; p += blockDim.x) {
+    uint64_t v;
+    switch (elem_bytes) {
+      case 1: v = row[p]; break;
+      case 2: v = reinterpret_cast<const uint16_t*>(row)[p]; break;
+      case 4: v = reinterpret_cast<const uint32_t*>(row)[p]; break;
+      default: v = reinterpret_cast<const uint64_t*>(row)[p]; break;
+    }
+    bad |= ((v & value_bits) != 0) != (p < len);
+  }
+  if (__syncthreads_or(bad) && threadIdx.x == 0) raise_status(PLORA_DEV_PADDING);
+}
+
 }  // namespace plora

@@ -220,6 +220,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + NB * kWinBytes + Cfg::kPartBytes);
   uint32_t* released = reinterpret_cast<uint32_t*>(full + NB);  // per buffer, monotonic
   volatile int* abort_flag = reinterpret_cast<volatile int*>(released + NB);
+  uint32_t* issued = reinterpret_cast<uint32_t*>(released + NB) + 1;  // per buffer: windows issued into it
   int32_t* tab_mem =
       reinterpret_cast<int32_t*>(smem + NB * kWinBytes + Cfg::kPartBytes + Cfg::kBarrierBytes);
 
@@ -237,6 +238,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   const int nwin = (K + W - 1) / W;
   const int kblocks = K >> 5;  // 32-row blocks per slot
   auto issue = [&](const WinCursor<WorkIt>& wc, int b) {  // one thread
+    atomicAdd(&issued[b], 1u);
     issue_lora_a_window(&tmap_a8, &tmap_a1, &full[b], smem_u32(smem + b * kWinBytes),
                         min(W, K - wc.w * W) >> 5, wc.slot * kblocks + wc.w * (W >> 5), 32 * RP * 2);
   };
@@ -249,6 +251,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     for (int i = 0; i < NB; ++i) {
       mbar_init(&full[i], 1);
       released[i] = 0;
+      issued[i] = 0;
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -338,7 +341,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       __syncwarp();
       if (lane == 0) {
         __threadfence_block();
-        if (atomicAdd(&released[b], 1u) % kMmaWarps == kMmaWarps - 1 && ic.valid) {
+        if (atomicAdd(&released[b], 1u) % kMmaWarps == kMmaWarps - 1 && ic.valid && !*abort_flag) {
           fence_proxy_async_smem();
           issue(ic, b);
         }
@@ -439,6 +442,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     }
     named_barrier(1, kMmaWarps * 32);
   }
+  // the last window issued into each buffer has landed (unless a wait gave up
+  // early; no window is issued after that), so no copy writes this CTA's
+  // shared memory after it exits
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int b = 0; b < NB; ++b)
+      if (issued[b]) mbar_drain(&full[b], (issued[b] - 1u) & 1u);
 }
 
 // ============================================================== expand
@@ -489,6 +499,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + NB * kWinBytes);
   uint32_t* released = reinterpret_cast<uint32_t*>(full + NB);  // per buffer, monotonic
   volatile int* abort_flag = reinterpret_cast<volatile int*>(released + NB);
+  uint32_t* issued = reinterpret_cast<uint32_t*>(released + NB) + 1;  // per buffer: windows issued into it
   uint8_t* regroup = smem + NB * kWinBytes + Cfg::kBarrierBytes;  // per-warp 16 x 64 B delta tile
   int32_t* tab_mem = reinterpret_cast<int32_t*>(regroup + Cfg::kRegroupBytes);
 
@@ -503,6 +514,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   const int N = args.N;
   const int nwin = (N + W - 1) / W;
   auto issue = [&](const WinCursor<WorkIt>& wc, int b) {  // one thread
+    atomicAdd(&issued[b], 1u);
     const int nc = min(W, N - wc.w * W) >> 6;
     mbar_arrive_expect_tx(&full[b], nc * Cfg::kChunkBytes);
     const int ch0 = wc.w * (W >> 6);
@@ -522,6 +534,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     for (int i = 0; i < NB; ++i) {
       mbar_init(&full[i], 1);
       released[i] = 0;
+      issued[i] = 0;
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -608,7 +621,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       __syncwarp();
       if (lane == 0) {
         __threadfence_block();
-        if (atomicAdd(&released[b], 1u) % kMmaWarps == kMmaWarps - 1 && ic.valid) {
+        if (atomicAdd(&released[b], 1u) % kMmaWarps == kMmaWarps - 1 && ic.valid && !*abort_flag) {
           fence_proxy_async_smem();
           issue(ic, b);
         }
@@ -722,6 +735,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     release();
     c_base += whi - wlo + 1;
   }
+  // the last window issued into each buffer has landed (unless a wait gave up
+  // early; no window is issued after that), so no copy writes this CTA's
+  // shared memory after it exits
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int b = 0; b < NB; ++b)
+      if (issued[b]) mbar_drain(&full[b], (issued[b] - 1u) & 1u);
 }
 
 }  // namespace plora

@@ -201,23 +201,6 @@ __device__ __forceinline__ void red_add_v8(void* dst, const uint32_t (&v)[4]) {
                  : "memory");
 }
 
-// Bounded wait that ignores the abort flag: used to let copies already issued
-// land before the CTA exits.  Its limit is the fixed 1 s, not the settable
-// wait limit: a copy in flight takes microseconds, and a shortened limit must
-// not let a CTA exit while one still writes its shared memory.  Returns false
-// on expiry (status raised).
-__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  for (;;) {
-    if (mbar_try_wait_parked(bar, parity)) return true;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
-      raise_status(PLORA_DEV_WAIT_TIMEOUT);
-      return false;
-    }
-  }
-}
-
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])

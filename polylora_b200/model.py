@@ -21,7 +21,8 @@ from torch import nn
 
 from .cache import GpuAdapterCache, ModuleSpec
 from .config import PolyLoraConfig
-from .context import LoraBatchContext, assert_right_padded, use_lora_context
+from . import _native
+from .context import RIGHT_PADDING_ERROR, LoraBatchContext, assert_right_padded, use_lora_context
 from .layers import MultiLoraLinear
 from .store import CpuAdapterStore, DiskAdapterCache
 
@@ -137,12 +138,29 @@ class PolyLoraModel(nn.Module):
             mask = attention_mask.to(device)
             seq_lens = mask.to(torch.int32).sum(dim=-1)  # int64, as torch sums integers
             if self.config.enforce_right_padding:
-                assert_right_padded(mask, seq_lens)
+                if self.config.right_padding_check == "device" and mask.is_cuda:
+                    if mask.dim() != 2:
+                        raise ValueError("attention_mask must be a 2D batch mask")
+                    _native.check_right_padded(mask, seq_lens)  # no wait; see raise_for_device_status
+                else:
+                    assert_right_padded(mask, seq_lens)
         else:
             seq_lens = torch.full((batch_size,), seq_len, dtype=torch.int32, device=device)
         return LoraBatchContext(adapter_ids=list(adapter_ids), weight_indices=weight_indices, seq_lens=seq_lens,
                                 attention_mask=attention_mask, table_ranks=self.adapter_cache.table_ranks,
                                 ready_event=self.adapter_cache.ready_event)
+
+    def raise_for_device_status(self) -> None:
+        """Waits for the device and raises for what the library's kernels
+        recorded since the last read: the reference's right-padding ValueError
+        for a mask checked on the device (``right_padding_check="device"``),
+        a ``PloraError`` for any other status bit.  Reading clears the word.
+        No counterpart in the reference, whose check raises in the forward."""
+        status = _native.device_status(clear=True)
+        if status & _native.DEV_PADDING:
+            raise ValueError(RIGHT_PADDING_ERROR)
+        if status:
+            raise _native.PloraError("device status", _native.ERR_DEVICE, f"status word 0x{status:x}")
 
     # ------------------------------------------------------------------ module surgery
     @staticmethod

@@ -119,6 +119,21 @@ def test_segment_and_slot_fill_limits_rejected_before_cuda(native):
     assert fill(1, 4096, 4095) == native.ERR_WORKSPACE
 
 
+def test_padding_check_arguments_rejected_before_cuda(native):
+    """plora_check_right_padded checks element sizes, shapes and alignment on
+    the host; an empty mask returns at once."""
+    lib = native.load()
+    dummy = 0x1000
+    assert lib.plora_check_right_padded(dummy, 3, 0, dummy, 2, 2, None) == native.ERR_INVALID_ARGUMENT
+    assert lib.plora_check_right_padded(dummy, 1, 1, dummy, 2, 2, None) == native.ERR_INVALID_ARGUMENT
+    assert lib.plora_check_right_padded(dummy, 8, 0, dummy, -1, 2, None) == native.ERR_INVALID_ARGUMENT
+    assert lib.plora_check_right_padded(dummy + 2, 4, 0, dummy, 2, 2, None) == native.ERR_INVALID_ARGUMENT
+    assert "aligned" in native.last_error()
+    assert lib.plora_check_right_padded(None, 8, 0, None, 2, 2, None) == native.ERR_INVALID_ARGUMENT
+    assert lib.plora_check_right_padded(None, 8, 0, None, 0, 7, None) == native.OK
+    assert lib.plora_check_right_padded(None, 2, 1, None, 5, 0, None) == native.OK
+
+
 def test_header_is_plain_c_and_links(tmp_path, native):
     """A C11 program that includes the header (pedantic, warnings as errors),
     takes the address of every declared entry point and links against the

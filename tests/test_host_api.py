@@ -26,6 +26,7 @@ ROOT = Path(__file__).resolve().parents[1]
     (dict(max_gpu_adapters=1, max_rank=4, max_disk_adapters=2), "disk_cache_dir must be set"),
     (dict(max_gpu_adapters=1, max_rank=0), "max_rank must be at least 1"),
     (dict(max_gpu_adapters=1, max_rank=4, target_modules=[]), "target_modules must not be empty"),
+    (dict(max_gpu_adapters=1, max_rank=4, right_padding_check="gpu"), 'right_padding_check must be "host" or "device"'),
 ])
 def test_config_validation_messages(kwargs, msg):
     with pytest.raises(ValueError, match=msg):
