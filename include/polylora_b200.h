@@ -77,12 +77,16 @@ int64_t plora_weight_split_tokens_per_sm(int64_t value);
 
 /* Kernel family of rank-16 calls of many tokens (max_rank 16, 16-bit types,
  * K % 512 == 0 and K <= 4096 for the shrink, N % 512 == 0 and N <= 4096 for
- * the expand): with value 1 (the default) they stream token rows through
- * shared memory by bulk copies and keep the slot's weights in registers; with
- * 0 they use the windowed tensor-core kernels that serve every other rank.
- * value < 0 only reads.  Returns the previous setting.  Process-wide; the two
- * families agree within the documented tolerance (fp32 summation order).  No
- * counterpart in the reference. */
+ * the expand).  2 (the default): they stream token rows through shared memory
+ * by bulk copies and keep the slot's weights in registers, and
+ * plora_sgmv_shrink_expand runs as one fused kernel in which each CTA expands
+ * the share it has just shrunk (where the expand phase fits the shrink's
+ * shared memory); 1: the same kernels, the combined call as two launches; 0:
+ * the windowed tensor-core kernels that serve every other rank.  Values above
+ * 2 mean 2; value < 0 only reads.  Returns the previous setting.
+ * Process-wide.  The stream settings give bit-identical results; the windowed
+ * kernels agree with them within the documented tolerance (fp32 summation
+ * order).  No counterpart in the reference. */
 int32_t plora_stream_kernels(int32_t value);
 
 /* Sets the limit of every bounded pipeline wait on the current device to

@@ -215,8 +215,9 @@ def weight_split_tokens_per_sm(value: int = -1) -> int:
 
 
 def stream_kernels(value: int = -1) -> int:
-    """Enables (1) or disables (0) the rank-16 stream kernels and returns the
-    previous setting; -1 only reads (see plora_stream_kernels)."""
+    """Selects the rank-16 kernel family (2: stream kernels with the combined
+    call fused, the default; 1: stream kernels, two launches; 0: windowed) and
+    returns the previous setting; -1 only reads (see plora_stream_kernels)."""
     return int(load().plora_stream_kernels(value))
 
 

@@ -68,8 +68,9 @@ std::mutex g_dev_mu;
 std::atomic<int64_t> g_wsplit_tokens_per_sm{16};
 
 // Rank-16 calls of many tokens run the stream kernels (sgmv_stream.cuh) when
-// this is non-zero (the default); 0 keeps them on the windowed mma kernels.
-std::atomic<int32_t> g_stream_kernels{1};
+// this is non-zero; 0 keeps them on the windowed mma kernels.  2 (the default)
+// also runs plora_sgmv_shrink_expand as the fused stream kernel, 1 as the two.
+std::atomic<int32_t> g_stream_kernels{2};
 
 // A CTA's share of the token list must fit the stream kernels' shared-memory
 // copy of its token ids.  Shares are cost-balanced (stream_share): one holds at
@@ -138,8 +139,10 @@ int device_info(DeviceInfo** out) {
     SET_GRID_ALL(32)
     SET_GRID_ALL(64)
 #undef SET_GRID_ALL
-    SET_GRID((sgmv_shrink_stream_kernel<true>), kStreamSmemLimit)
-    SET_GRID((sgmv_shrink_stream_kernel<false>), kStreamSmemLimit)
+    SET_GRID((sgmv_shrink_stream_kernel<true, false>), kStreamSmemLimit)
+    SET_GRID((sgmv_shrink_stream_kernel<false, false>), kStreamSmemLimit)
+    SET_GRID((sgmv_shrink_stream_kernel<true, true>), kStreamSmemLimit)
+    SET_GRID((sgmv_shrink_stream_kernel<false, true>), kStreamSmemLimit)
     SET_GRID((sgmv_expand_stream_kernel<true>), kStreamSmemLimit)
     SET_GRID((sgmv_expand_stream_kernel<false>), kStreamSmemLimit)
 #undef SET_GRID
@@ -366,9 +369,9 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
       const StreamPlan plan = shrink_stream_plan(K, seg.num_slots);
       if (plan.nst >= 2) {
         // the kernel reads its inputs only after griddep_wait(): always launched programmatically
-        PLORA_CUDA(launch_kernel(bf ? sgmv_shrink_stream_kernel<true> : sgmv_shrink_stream_kernel<false>,
+        PLORA_CUDA(launch_kernel(bf ? sgmv_shrink_stream_kernel<true, false> : sgmv_shrink_stream_kernel<false, false>,
                                  dim3(di->sm_count), dim3(kShrinkThreads), plan.smem_bytes, stream, true, 0,
-                                 args, plan),
+                                 args, plan, ExpandArgs{}, FusedPlan{}),
                    "launch sgmv_shrink_stream_kernel");
         return check_launch("sgmv_shrink_stream_kernel");
       }
@@ -544,7 +547,7 @@ int64_t plora_weight_split_tokens_per_sm(int64_t value) {
 }
 
 int32_t plora_stream_kernels(int32_t value) {
-  return value >= 0 ? g_stream_kernels.exchange(value ? 1 : 0) : g_stream_kernels.load();
+  return value >= 0 ? g_stream_kernels.exchange(value > 2 ? 2 : value) : g_stream_kernels.load();
 }
 
 int plora_set_wait_limit_ns(uint64_t limit_ns, uint64_t* previous) {
@@ -649,6 +652,53 @@ int plora_sgmv_expand(const void* tmp, const void* lora_b, void* y, const int32_
                      dtype, static_cast<cudaStream_t>(stream));
 }
 
+// The fused stream kernel for plora_sgmv_shrink_expand: rank 16, 16-bit types,
+// K and N multiples of 512 up to 4096, many tokens, and an expand phase that
+// fits the shrink's shared memory.  *launched = false leaves the call to the
+// two kernels.
+int fused_impl(const void* x, const void* a, void* tmp, const void* b, void* y, const int32_t* ranks,
+               const float* scales, SegTable seg, int64_t num_tokens, int64_t K, int64_t R, int64_t N, int32_t dtype,
+               cudaStream_t stream, bool* launched) {
+  *launched = false;
+  if (g_stream_kernels.load(std::memory_order_relaxed) != 2 || dtype == PLORA_DTYPE_F32 || R != kStreamRank ||
+      seg.num_slots > kFastPathMaxSlots || !aligned16(x) || !aligned16(a) || !aligned16(tmp) || !aligned16(b) ||
+      !aligned16(y) || N % 512 != 0 || N > kStreamMaxDim)
+    return PLORA_OK;
+  DeviceInfo* di = nullptr;
+  int st = device_info(&di);
+  if (st) return st;
+  if (use_weight_split(num_tokens, di) || !stream_shrink_ok(R, K, num_tokens, seg.num_slots, di)) return PLORA_OK;
+  StreamPlan plan;
+  FusedPlan fp;
+  if (!fused_stream_plan(K, N, seg.num_slots, plan, fp)) return PLORA_OK;
+  ShrinkArgs sa;
+  sa.x = static_cast<const uint8_t*>(x);
+  sa.a = static_cast<const uint8_t*>(a);
+  sa.tmp = static_cast<uint8_t*>(tmp);
+  sa.ranks = ranks;
+  sa.seg = seg;
+  sa.K = (int32_t)K;
+  sa.R = (int32_t)R;
+  sa.stack_num = 1;
+  ExpandArgs ea;
+  ea.tmp = static_cast<const uint8_t*>(tmp);
+  ea.b = static_cast<const uint8_t*>(b);
+  ea.y = static_cast<uint8_t*>(y);
+  ea.ranks = ranks;
+  ea.scales = scales;
+  ea.seg = seg;
+  ea.R = (int32_t)R;
+  ea.N = (int32_t)N;
+  const bool bf = dtype == PLORA_DTYPE_BF16;
+  // programmatic like the shrink: it reads its inputs only after griddep_wait()
+  PLORA_CUDA(launch_kernel(bf ? sgmv_shrink_stream_kernel<true, true> : sgmv_shrink_stream_kernel<false, true>,
+                           dim3(di->sm_count), dim3(kShrinkThreads), plan.smem_bytes, stream, true, 0, sa, plan,
+                           ea, fp),
+             "launch fused sgmv_shrink_stream_kernel");
+  *launched = true;
+  return check_launch("fused sgmv_shrink_stream_kernel");
+}
+
 int plora_sgmv_shrink_expand(const void* x, const void* lora_a, void* tmp, const void* lora_b,
                              void* y, const int32_t* lora_ranks, const float* scalings,
                              const int32_t* slot_start, const int32_t* token_index,
@@ -668,6 +718,10 @@ int plora_sgmv_shrink_expand(const void* x, const void* lora_a, void* tmp, const
     return fail(PLORA_ERR_UNSUPPORTED, "num_tokens exceeds int32 token ids");
   SegTable seg{slot_start, token_index, num_slots};
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  bool fused = false;
+  if ((st = fused_impl(x, lora_a, tmp, lora_b, y, lora_ranks, scalings, seg, num_tokens, in_features, max_rank,
+                       out_features, dtype, s, &fused)) || fused)
+    return st;
   if ((st = shrink_impl(x, lora_a, tmp, lora_ranks, seg, num_tokens, in_features, max_rank, 1,
                         dtype, s)))
     return st;

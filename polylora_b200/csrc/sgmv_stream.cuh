@@ -100,24 +100,49 @@ __host__ __device__ inline uint32_t stream_bar_bytes(int slots) { return (uint32
 // (4 B, after the 6 partial barriers), then the abort flag
 __host__ __device__ inline uint32_t shrink_bar_bytes(int stages) { return (uint32_t)stages * 20 + 6 * 8 + 16; }
 
-__host__ __device__ inline StreamPlan shrink_stream_plan(int64_t K, int64_t num_slots) {
+__host__ __device__ inline StreamPlan shrink_stream_plan(int64_t K, int64_t num_slots, int64_t extra_bar_bytes = 0) {
   StreamPlan p;
   p.pitch = (uint32_t)(K * 2 + 16);
   p.stage_bytes = p.pitch * kStreamGroup;
   const int64_t tab = slot_tab_bytes(num_slots);
   const int64_t fixed =
       128 + kShrinkPartBufs * kShrinkPartBytes + kShrinkTmpTileBytes + kShrinkMetaBytes + shrink_bar_bytes(0) +
-      kStreamMaxShare * 4 + tab;
+      extra_bar_bytes + kStreamMaxShare * 4 + tab;
   int64_t nst = (kStreamSmemLimit - fixed) / ((int64_t)p.stage_bytes + 24);
   if (nst > kStreamMaxStages) nst = kStreamMaxStages;
   p.nst = (int)nst;
   p.aux_off = (uint32_t)(nst * p.stage_bytes);
   p.rg_off = p.aux_off + kShrinkPartBufs * kShrinkPartBytes;
   p.bar_off = p.rg_off + kShrinkTmpTileBytes + kShrinkMetaBytes;
-  p.tok_off = p.bar_off + shrink_bar_bytes(p.nst);
+  p.tok_off = p.bar_off + shrink_bar_bytes(p.nst) + (uint32_t)extra_bar_bytes;
   p.tab_off = p.tok_off + kStreamMaxShare * 4;
   p.smem_bytes = (uint32_t)(128 + p.tab_off + tab);
   return p;
+}
+
+// The fused shrink + expand kernel's expand phase reuses the shrink's shared
+// memory once the token ring is idle: two LoRA-B weight stages and the share's
+// tmp rows in the ring area, the regroup tiles in the partial buffers, and 2
+// full + 2 empty mbarriers and 2 last-armed indices after the shrink's barriers.
+struct FusedPlan {
+  uint32_t w_pitch = 0, w_stage_bytes = 0;  // weight stage: 8 rows of N values
+  uint32_t tmp_off = 0, rg_off = 0, wbar_off = 0;
+};
+constexpr int kFusedBarBytes = 8 + 2 * 8 + 2 * 8 + 2 * 4;  // alignment pad + barriers + indices
+
+// Plans of the fused kernel for K x N; false when the expand phase does not
+// fit the shrink's ring area (then the two kernels run one after the other).
+__host__ __device__ inline bool fused_stream_plan(int64_t K, int64_t N, int64_t num_slots, StreamPlan& sp,
+                                                  FusedPlan& fp) {
+  sp = shrink_stream_plan(K, num_slots, kFusedBarBytes);
+  fp.w_pitch = (uint32_t)(N * 2 + 16);
+  fp.w_stage_bytes = fp.w_pitch * kStreamGroup;
+  fp.tmp_off = 2 * fp.w_stage_bytes;
+  fp.rg_off = sp.aux_off;
+  fp.wbar_off = (sp.bar_off + shrink_bar_bytes(sp.nst) + 7u) & ~7u;
+  return sp.nst >= 2 && (int64_t)fp.tmp_off + kStreamMaxShare * kExpandTmpRowBytes <= (int64_t)sp.nst * sp.stage_bytes &&
+         kExpandRegroupBytes <= kShrinkPartBufs * kShrinkPartBytes && fp.wbar_off + 40u <= sp.tok_off &&
+         sp.smem_bytes <= (uint32_t)kStreamSmemLimit;
 }
 
 __host__ __device__ inline StreamPlan expand_stream_plan(int64_t N, int64_t num_slots) {
@@ -340,10 +365,10 @@ __device__ void stream_share(const SlotTab& t, int nact, int b, int G, int64_t s
 }
 
 // stage_slot_tab, also counting how many of the slots this thread staged are
-// active (rank > 0, at least one token); the table's scale column is not
-// written.
-__device__ __forceinline__ SlotTab stage_slot_tab_counted(const SegTable& t, const int32_t* ranks, int32_t* dst,
-                                                          int& active_mine) {
+// active (rank > 0, at least one token); without scales the table's scale
+// column is not written.
+__device__ __forceinline__ SlotTab stage_slot_tab_counted(const SegTable& t, const int32_t* ranks, const float* scales,
+                                                          int32_t* dst, int& active_mine) {
   const int ns = t.num_slots;
   int32_t* ss = dst;
   int32_t* rk = dst + ns + 1;
@@ -356,6 +381,7 @@ __device__ __forceinline__ SlotTab stage_slot_tab_counted(const SegTable& t, con
       const int32_t s1 = ld_cg_i32(t.slot_start + i + 1);
       const int32_t r = __ldg(ranks + i);
       rk[i] = r;
+      if (scales) sc[i] = __ldg(scales + i);
       active_mine += (r > 0 && s1 > s0) ? 1 : 0;
     }
   }
@@ -478,9 +504,133 @@ static_assert(5 * 32 * kShrinkLaunchRegs <= 16384, "launch registers per partiti
 
 __host__ __device__ constexpr int shrink_rank_of_row(int r) { return 4 * ((r & 7) >> 1) + (r & 1) + 2 * (r >> 3); }
 
+// 16-byte load through L2: for data that other threads of this CTA wrote
+// before a barrier.
+__device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+constexpr int kFusedTmpWritten = 2;  // named barrier of the 16 consumer warps (fused kernel)
+
+// The fused kernel's expand phase (consumer warps 0-15): y[t, :] +=
+// round(scale * tmp[t, :] @ B[slot(t)]) for the CTA's share, as
+// sgmv_expand_stream_kernel computes it, with the weight stages streamed by
+// the producer warp (wfull / wempty) and the share's tmp rows gathered from
+// global memory, where this CTA's reducers wrote them.  Every consumer warp
+// passes both barriers, also after an abort.
 template <bool BF16>
+__device__ __forceinline__ void fused_expand_phase(const ExpandArgs& args, const FusedPlan& fp, const SlotTab& tab,
+                                                   const int32_t* tok_s, int64_t begin, int64_t end, uint32_t stage0,
+                                                   volatile int* abort_flag, uint64_t* wfull, uint64_t* wempty,
+                                                   uint8_t* smem, int warp, int lane) {
+  const int N = args.N;
+  const int share = (int)(end - begin);
+  uint8_t* tmp_s = smem + fp.tmp_off;
+  named_barrier(kFusedTmpWritten, kStreamThreads);  // every group's tmp rows are in global memory
+  if (!*abort_flag)
+    for (int i = threadIdx.x; i < 2 * share; i += kStreamThreads)
+      *reinterpret_cast<uint4*>(tmp_s + i * 16) =
+          ld_cg_v4(args.tmp + (int64_t)tok_s[i >> 1] * kExpandTmpRowBytes + (i & 1) * 16);
+  named_barrier(kFusedTmpWritten, kStreamThreads);
+
+  const uint32_t row_bytes = (uint32_t)N * 2;
+  const int g = lane >> 2;
+  const int t = lane & 3;
+  const int ncw = N >> 4;   // columns of this warp
+  const int nt = ncw >> 3;  // n8 tiles of this warp: a multiple of 4, <= 32
+  const int c0w = warp * ncw;
+  uint32_t b[32][2];
+  const uint32_t w_off = (uint32_t)(lane & 7) * fp.w_pitch + (uint32_t)(c0w + 8 * (lane >> 3)) * 2;
+  const uint32_t rg_base = stage0 + fp.rg_off + warp * kStreamGroup * 64;
+  const uint32_t rg_st = rg_base + (lane & 7) * 64 + 16 * ((lane >> 3) ^ (((lane & 7) >> 1) & 3));
+  const uint32_t rg_ld = rg_base + g * 64 + 16 * (t ^ ((g >> 1) & 3));
+  float scale = 0.f;
+  int kr = 0;
+  RingSeq it;
+  it.init(tab, begin, end, true, true);
+  int wi = 0;
+  RingItem cq;
+  while (it.next(tab, begin, cq)) {
+    if (cq.part >= 0) {  // weight stage: rank rows 8 part .. of this warp's columns
+      const int w = wi & 1;
+      if (!mbar_wait_warp(&wfull[w], (uint32_t)(wi / 2) & 1u, abort_flag)) break;
+      if (cq.part == 0) {
+        scale = tab.sc[cq.slot];
+        kr = min(tab.rk[cq.slot], args.R);
+      }
+      const uint32_t sbase = stage0 + w * fp.w_stage_bytes;
+      const bool one_stage = kr <= 8;
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        if (i < nt) {
+          uint32_t r[4];
+          ldsm_x4_t(sbase + w_off + 16 * i, r);
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            if (cq.part == 0) {
+              b[i + m][0] = r[m];
+              if (one_stage) b[i + m][1] = 0u;
+            } else {
+              b[i + m][1] = r[m];
+            }
+          }
+        }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&wempty[w]);
+      ++wi;
+      continue;
+    }
+    uint32_t fa[4] = {0u, 0u, 0u, 0u};
+    const bool vrow = g < cq.cnt;
+    int64_t tok = 0;
+    if (vrow) {
+      const uint32_t* trow = reinterpret_cast<const uint32_t*>(tmp_s + (cq.start + g) * kExpandTmpRowBytes);
+      auto ld2 = [&](int k) -> uint32_t {
+        if (k >= kr) return 0u;
+        const uint32_t v = trow[k >> 1];
+        return k + 1 < kr ? v : (v & 0xFFFFu);
+      };
+      fa[0] = ld2(2 * t);
+      fa[2] = ld2(2 * t + 8);
+      tok = tok_s[cq.start + g];
+    }
+    uint8_t* yrow = args.y + tok * row_bytes + (c0w + 8 * t) * 2;
+#pragma unroll
+    for (int i = 0; i < 32; i += 4)
+      if (i < nt) {
+        uint32_t d[4];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+          mma_16816<BF16>(acc, fa, b[i + m][0], b[i + m][1]);
+          d[m] = pack2<BF16>(scale * acc[0], scale * acc[1]);
+        }
+        stsm_x4(rg_st, d);
+        __syncwarp();
+        lds_v4(rg_ld, d);
+        __syncwarp();
+        if (vrow) red_add_v8<BF16>(yrow + 16 * i, d);
+      }
+  }
+}
+
+
+// kFused: the fused shrink + expand kernel.  After its shrink phase a CTA
+// expands its own share: the producer waits until every ring stage has been
+// released for the last time and streams the share's LoRA-B weight stages
+// into the idle ring (prefetched into L2 while the shrink ran); the consumers
+// pass a barrier (every group's tmp rows written by their reducers), gather
+// the share's tmp rows into shared memory (they are still in L2) and run the
+// expand's group loop (sgmv_expand_stream_kernel).  No grid-wide dependency:
+// a CTA's expand phase reads only its own tmp rows, so it starts while other
+// CTAs still shrink, and the expand's launch, slot table and token ids are
+// not paid twice.
+template <bool BF16, bool kFused>
 __global__ void __launch_bounds__(kShrinkThreads, 1)
-    sgmv_shrink_stream_kernel(const ShrinkArgs args, const StreamPlan plan) {
+    sgmv_shrink_stream_kernel(const ShrinkArgs args, const StreamPlan plan, const ExpandArgs eargs,
+                              const FusedPlan fp) {
   using E = Elem<BF16>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align128(smem_raw);
@@ -495,18 +645,30 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(loaded + nst);
   int32_t* tok_s = reinterpret_cast<int32_t*>(smem + plan.tok_off);
   int32_t* tab_mem = reinterpret_cast<int32_t*>(smem + plan.tab_off);
+  // fused expand phase: [2] weight stage landed, [2] released by the 16 consumers, [2] last item armed
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + fp.wbar_off);
+  uint64_t* wempty = wfull + 2;
+  int32_t* wloaded = reinterpret_cast<int32_t*>(wempty + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   griddep_wait();    // inputs (segment table, x) come from earlier kernels
   griddep_launch();  // the expand may start on SMs this grid releases
   int active_mine;  // active slots among those this thread staged (<= 2)
-  const SlotTab tab = stage_slot_tab_counted(args.seg, args.ranks, tab_mem, active_mine);
+  const SlotTab tab = stage_slot_tab_counted(args.seg, args.ranks, kFused ? eargs.scales : nullptr, tab_mem,
+                                             active_mine);
   if (threadIdx.x == 0) {
     for (int i = 0; i < nst; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kStreamWarps);
       loaded[i] = -1;
+    }
+    if constexpr (kFused) {
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&wfull[i], 1);
+        mbar_init(&wempty[i], kStreamWarps);
+        wloaded[i] = -1;
+      }
     }
     for (int i = 0; i < kShrinkPartBufs; ++i) {
       mbar_init(&pfull[i], kStreamWarps);
@@ -538,8 +700,10 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
       // would otherwise queue ahead of these few bytes
       named_barrier_arrive(kShrinkIdsReady, kStreamThreads + 32);
       const uint64_t pol = l2_evict_first_policy();
+      const uint32_t n_row = kFused ? (uint32_t)eargs.N * 2 : 0u;  // one LoRA-B rank row
       int pf_slot = -1;  // slot of the previous group (its rows are in L2 or on their way)
-      for (int ii = 0; ok && it.next(tab, begin, q); ++ii) {
+      int ii = 0;
+      for (; ok && it.next(tab, begin, q); ++ii) {
         const int s = ii % nst;
         // stage s is free once the 16 consumers released item ii - nst
         if (ii >= nst && !mbar_wait_warp(&empty[s], (uint32_t)(ii / nst - 1) & 1u, abort_flag)) {
@@ -551,12 +715,38 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
           mbar_arrive_expect_tx(&full[s], (uint32_t)q.cnt * row_bytes);
           if (pf_slot >= 0 && q.slot != pf_slot)  // the consumers load the first slot themselves
             prefetch_l2_bulk(args.a + (int64_t)q.slot * slot_bytes, slot_bytes);
+          if (kFused && q.slot != pf_slot)  // the slot's LoRA-B rows, for the expand phase
+            prefetch_l2_bulk(eargs.b + (int64_t)q.slot * kStreamRank * n_row,
+                             (tab.rk[q.slot] > 8 ? 16u : 8u) * n_row);
         }
         pf_slot = q.slot;
         __syncwarp();
         if (lane < q.cnt)
           bulk_load(stage0 + s * plan.stage_bytes + lane * plan.pitch,
                     args.x + (int64_t)tok_s[q.start + lane] * row_bytes, row_bytes, &full[s], pol);
+      }
+      if constexpr (kFused) {
+        // the weight stages overwrite the token ring: wait until the consumers
+        // have released every stage for the last time
+        for (int s = 0; ok && s < nst && s < ii; ++s) {
+          const int last = s + nst * ((ii - 1 - s) / nst);
+          ok = mbar_wait_warp(&empty[s], (uint32_t)(last / nst) & 1u, abort_flag);
+        }
+        RingSeq wseq;  // the share's weight stages (slots of rank <= 8: only rank rows 0-7)
+        wseq.init(tab, begin, end, true, true);
+        for (int wi = 0; ok && wseq.next_of(tab, begin, q, true); ++wi) {
+          const int w = wi & 1;
+          if (wi >= 2 && !mbar_wait_warp(&wempty[w], (uint32_t)(wi / 2 - 1) & 1u, abort_flag)) break;
+          if (lane == 0) {
+            wloaded[w] = wi;
+            mbar_arrive_expect_tx(&wfull[w], kStreamGroup * n_row);
+          }
+          __syncwarp();
+          if (lane < kStreamGroup)
+            bulk_load(stage0 + w * fp.w_stage_bytes + lane * fp.w_pitch,
+                      eargs.b + (((int64_t)q.slot * 2 + q.part) * kStreamGroup + lane) * n_row, n_row, &wfull[w],
+                      pol);
+        }
       }
     }
   } else {
@@ -711,11 +901,17 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
       const int rg = ii - kShrinkReduceLag + k;
       if (ok && rg >= 0 && (rg & (kStreamWarps - 1)) == warp) ok = reduce(rg);
     }
+    if constexpr (kFused) fused_expand_phase<BF16>(eargs, fp, tab, tok_s, begin, end, stage0, abort_flag, wfull,
+                                                   wempty, smem, warp, lane);
   }
   __syncthreads();  // every warp is out of its loop
-  if (threadIdx.x == 0)  // the last copy into each stage has landed (unless the roles gave up early)
+  if (threadIdx.x == 0) {  // the last copy into each stage has landed (unless the roles gave up early)
     for (int s = 0; s < nst; ++s)
       if (loaded[s] >= 0) mbar_drain(&full[s], (uint32_t)(loaded[s] / nst) & 1u);
+    if constexpr (kFused)
+      for (int w = 0; w < 2; ++w)
+        if (wloaded[w] >= 0) mbar_drain(&wfull[w], (uint32_t)(wloaded[w] / 2) & 1u);
+  }
 }
 
 // ============================================================== expand

@@ -188,10 +188,11 @@ def test_token_count_overflow_rejected_before_cuda(native, rows, seq):
 def test_stream_kernel_switch_round_trips(native):
     prev = native.stream_kernels()
     try:
-        assert prev in (0, 1)
+        assert prev == 2  # the default: stream kernels, the combined call fused
         assert native.stream_kernels(0) == prev
         assert native.stream_kernels() == 0
-        assert native.stream_kernels(5) == 0  # any non-zero value enables
-        assert native.stream_kernels() == 1
+        assert native.stream_kernels(1) == 0
+        assert native.stream_kernels(5) == 1  # values above 2 mean 2
+        assert native.stream_kernels() == 2
     finally:
         native.stream_kernels(prev)

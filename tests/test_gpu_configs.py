@@ -11,7 +11,9 @@ active token checked against the CPU oracle.
   popularity: prefill rows of 1024 tokens and a 256 x 1 decode batch.
 
 Every case runs under each kernel family (stream, windowed token split, slot
-grid); the oracle is computed once per case.  Checks: tmp against the oracle
+grid) through the two operators, and through the combined call that the
+layers make (sgmv_shrink_expand: the fused stream kernel where it applies);
+the oracle is computed once per case.  Checks: tmp against the oracle
 shrink, the output against the fp32-accumulated forward with the one-ulp
 error measure and, on a second run over a zero base output, the delta itself
 element-wise (half an ulp of allowance: oracle.sgmv_ref.lora_err_strict);
@@ -25,18 +27,18 @@ import torch
 
 from oracle import sgmv_ref
 from polylora_b200 import _native
-from polylora_b200.sgmv import sgmv_lora_a_fwd, sgmv_lora_b_fwd
+from polylora_b200.sgmv import build_segments, sgmv_lora_a_fwd, sgmv_lora_b_fwd, sgmv_shrink_expand
 
 pytestmark = pytest.mark.gpu
 
 TOL = 2e-2  # bf16, north star
-MODES = ("stream", "token_split", "weight_split")
+MODES = ("stream", "token_split", "weight_split", "combined")
 
 
 def _set_mode(mode):
     prev = (_native.weight_split_tokens_per_sm(), _native.stream_kernels())
     _native.weight_split_tokens_per_sm(1 << 40 if mode == "weight_split" else 0)
-    _native.stream_kernels(0 if mode == "token_split" else 1)
+    _native.stream_kernels({"token_split": 0, "combined": 2}.get(mode, 1))
     return prev
 
 
@@ -66,14 +68,21 @@ def _case(seed, rows, seq, K, N, ns, R, rank_choices, base_frac, popularity=None
     return dict(x=x, y=y, A=A, B=Bw, ranks=ranks, scales=scales, wi=wi, seq=sl)
 
 
-def _run(c, y):
+def _run(c, y, combined=False):
     d = torch.device("cuda")
     seq = torch.from_numpy(c["seq"]).to(d)
     wi = torch.from_numpy(c["wi"]).to(d)
     ranks = torch.from_numpy(c["ranks"]).to(d)
-    tmp = sgmv_lora_a_fwd(c["x"], c["A"], seq, wi, ranks)
+    scales = torch.from_numpy(c["scales"]).to(d)
     out = y.clone()
-    sgmv_lora_b_fwd(tmp, c["B"], seq, wi, ranks, torch.from_numpy(c["scales"]).to(d), out)
+    if combined:
+        x = c["x"]
+        table = build_segments(wi, seq, ranks, x.shape[1])
+        tmp = torch.empty(x.shape[0], x.shape[1], c["A"].shape[2], device=d, dtype=x.dtype)
+        sgmv_shrink_expand(x, c["A"], c["B"], out, table, ranks, scales, tmp=tmp)
+    else:
+        tmp = sgmv_lora_a_fwd(c["x"], c["A"], seq, wi, ranks)
+        sgmv_lora_b_fwd(tmp, c["B"], seq, wi, ranks, scales, out)
     torch.cuda.synchronize()
     return tmp, out
 
@@ -108,8 +117,8 @@ def _check_case(c, chunk_rows, modes=MODES):
         prev = _set_mode(mode)
         try:
             _native.device_status(clear=True)
-            tmp, out = _run(c, c["y"])
-            _, out0 = _run(c, torch.zeros_like(c["y"]))
+            tmp, out = _run(c, c["y"], mode == "combined")
+            _, out0 = _run(c, torch.zeros_like(c["y"]), mode == "combined")
             assert _native.device_status(clear=True) == 0, mode
         finally:
             _restore(prev)

@@ -19,16 +19,17 @@ pytestmark = pytest.mark.gpu
 TOL = {"bfloat16": 2e-2, "float16": 2e-2, "float32": 1e-5}
 
 
-@pytest.fixture(params=["stream", "token_split", "weight_split"])
+@pytest.fixture(params=["stream", "stream_separate", "token_split", "weight_split"])
 def split_mode(request):
     """Runs the test under each kernel family of the tensor-core path: every
     CTA a share of the tokens, with rank-16 calls on the stream kernels (rows
-    by bulk copies, weights in registers) or on the windowed kernels; or each
-    slot's weights spread over the grid (slot grid)."""
+    by bulk copies, weights in registers; the combined call as one fused
+    kernel, or with "stream_separate" as the two) or on the windowed kernels;
+    or each slot's weights spread over the grid (slot grid)."""
     from polylora_b200 import _native
 
     prev = _native.weight_split_tokens_per_sm(1 << 40 if request.param == "weight_split" else 0)
-    prev_stream = _native.stream_kernels(0 if request.param == "token_split" else 1)
+    prev_stream = _native.stream_kernels({"token_split": 0, "stream_separate": 1}.get(request.param, 2))
     yield request.param
     _native.weight_split_tokens_per_sm(prev)
     _native.stream_kernels(prev_stream)

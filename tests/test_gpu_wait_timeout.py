@@ -18,7 +18,7 @@ import torch
 
 from oracle import sgmv_ref
 from polylora_b200 import _native
-from polylora_b200.sgmv import build_segments, sgmv_expand, sgmv_shrink
+from polylora_b200.sgmv import build_segments, sgmv_expand, sgmv_shrink, sgmv_shrink_expand
 
 pytestmark = pytest.mark.gpu
 
@@ -37,15 +37,28 @@ def _config2_like(dev, T=8192, K=4096, N=4096, ns=65, R=16, seed=11):
     return x, y, A, Bw, ranks, scales, wi, torch.ones(T, dtype=torch.int32, device=dev)
 
 
-@pytest.fixture()
-def stream_kernels_on():
-    prev = (_native.weight_split_tokens_per_sm(0), _native.stream_kernels(1))
-    yield
+# kernel families whose waits are driven out: the stream shrink and expand as
+# two launches, the fused stream kernel (combined call), the windowed kernels
+FAMILIES = {"stream": 1, "fused": 2, "windowed": 0}
+
+
+@pytest.fixture(params=list(FAMILIES))
+def family(request):
+    prev = (_native.weight_split_tokens_per_sm(0), _native.stream_kernels(FAMILIES[request.param]))
+    yield request.param
     _native.weight_split_tokens_per_sm(prev[0])
     _native.stream_kernels(prev[1])
 
 
-def test_expired_waits_report_and_leave_the_context_usable(stream_kernels_on):
+def _lora(family, x, A, Bw, table, ranks, scales, tmp, out):
+    if family == "fused":
+        sgmv_shrink_expand(x, A, Bw, out, table, ranks, scales, tmp=tmp)
+    else:
+        sgmv_shrink(x, A, table, ranks, out=tmp)
+        sgmv_expand(tmp, Bw, out, table, ranks, scales)
+
+
+def test_expired_waits_report_and_leave_the_context_usable(family):
     dev = torch.device("cuda")
     x, y, A, Bw, ranks, scales, wi, seq = _config2_like(dev)
     table = build_segments(wi, seq, ranks, 1)
@@ -56,8 +69,7 @@ def test_expired_waits_report_and_leave_the_context_usable(stream_kernels_on):
     try:
         raised = 0
         for _ in range(3):
-            sgmv_shrink(x, A, table, ranks, out=tmp)
-            sgmv_expand(tmp, Bw, y.clone(), table, ranks, scales)
+            _lora(family, x, A, Bw, table, ranks, scales, tmp, y.clone())
             status = _native.device_status(clear=True)  # synchronises: every kernel returned
             raised += bool(status & _native.DEV_WAIT_TIMEOUT)
             assert status & ~_native.DEV_WAIT_TIMEOUT == 0, f"unexpected status {status:#x}"
@@ -68,8 +80,7 @@ def test_expired_waits_report_and_leave_the_context_usable(stream_kernels_on):
         assert _native.set_wait_limit_ns(prev) == 0
     # limit restored: the same calls are correct again and raise nothing
     out = y.clone()
-    sgmv_shrink(x, A, table, ranks, out=tmp)
-    sgmv_expand(tmp, Bw, out, table, ranks, scales)
+    _lora(family, x, A, Bw, table, ranks, scales, tmp, out)
     assert _native.device_status(clear=True) == 0
     rows = np.random.default_rng(0).choice(x.shape[0], size=512, replace=False)
     ref = sgmv_ref.lora_forward_fp32(
