@@ -680,6 +680,7 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
   // slot table staged, barriers initialised, active slots counted
   const int nact = __syncthreads_count(active_mine >= 1) + __syncthreads_count(active_mine >= 2);
   int64_t begin, end;  // this CTA's share, the same in every warp
+  // (the fused kernel too: 20-40 tokens measured best for it, 0-10 and 60 slower)
   stream_share(tab, nact, blockIdx.x, gridDim.x, kShrinkSlotCost, lane, begin, end);
   if (begin >= end) return;  // uniform across the CTA
   const uint32_t stage0 = smem_u32(smem);
@@ -726,17 +727,26 @@ __global__ void __launch_bounds__(kShrinkThreads, 1)
                     args.x + (int64_t)tok_s[q.start + lane] * row_bytes, row_bytes, &full[s], pol);
       }
       if constexpr (kFused) {
-        // the weight stages overwrite the token ring: wait until the consumers
-        // have released every stage for the last time
-        for (int s = 0; ok && s < nst && s < ii; ++s) {
-          const int last = s + nst * ((ii - 1 - s) / nst);
-          ok = mbar_wait_warp(&empty[s], (uint32_t)(last / nst) & 1u, abort_flag);
-        }
+        // Weight stage w overwrites the ring stages under it: before its first
+        // copy, wait until the consumers have released each of those for the
+        // last time (ring stages under neither weight stage, where the tmp rows
+        // go, are written only after the consumers' barrier).  The first
+        // weight stages so land while the shrink's last groups are consumed.
+        int ring_free = 0;  // ring stages [0, ring_free) released for good
+        auto free_ring_below = [&](uint32_t bytes) -> bool {
+          const int need = min(ii, (int)((bytes + plan.stage_bytes - 1) / plan.stage_bytes));
+          for (; ring_free < need; ++ring_free) {
+            const int last = ring_free + nst * ((ii - 1 - ring_free) / nst);
+            if (!mbar_wait_warp(&empty[ring_free], (uint32_t)(last / nst) & 1u, abort_flag)) return false;
+          }
+          return true;
+        };
         RingSeq wseq;  // the share's weight stages (slots of rank <= 8: only rank rows 0-7)
         wseq.init(tab, begin, end, true, true);
         for (int wi = 0; ok && wseq.next_of(tab, begin, q, true); ++wi) {
           const int w = wi & 1;
           if (wi >= 2 && !mbar_wait_warp(&wempty[w], (uint32_t)(wi / 2 - 1) & 1u, abort_flag)) break;
+          if (wi < 2 && !free_ring_below((uint32_t)(w + 1) * fp.w_stage_bytes)) break;
           if (lane == 0) {
             wloaded[w] = wi;
             mbar_arrive_expect_tx(&wfull[w], kStreamGroup * n_row);
