@@ -37,6 +37,8 @@ sys.path.insert(0, str(ROOT))
 METRIC = "mixed-adapter tokens/s at 1/2/4/8 B200; SGMV achieved HBM GB/s vs peak"
 T_TOKENS, K_IN, N_OUT, SLOTS, MAX_RANK = 16384, 4096, 4096, 65, 16
 SEG_ONE_LAUNCH_ROWS = 1024  # rows the one-launch segment builder takes (csrc/segments.cuh)
+SEG_SCAN_PLACE_INTS = 12288  # count-matrix size up to which scan and placement are one launch
+SEG_ROWS_PER_BLOCK = 256     # rows per count block of the segment builder
 E2E_CHUNKS = 8  # row chunks of the host-buffer pipeline (e2e leg)
 ELEM = 2  # bf16
 
@@ -421,7 +423,8 @@ def run_ours(args):
     expand_ms = time_kernel(lambda: sgmv_expand(tmp, Bw, y, table, ranks, scales), reps)
     pair_ms = time_kernel(lambda: sgmv_shrink_expand(x, A, Bw, y, table, ranks, scales, tmp=tmp), reps)
     seg_ms = time_kernel(lambda: build_segments(wi, seq, ranks, 1), reps)
-    seg_launches = 1 if T_TOKENS <= SEG_ONE_LAUNCH_ROWS else 3
+    count_blocks = (T_TOKENS + SEG_ROWS_PER_BLOCK - 1) // SEG_ROWS_PER_BLOCK
+    seg_launches = 1 if T_TOKENS <= SEG_ONE_LAUNCH_ROWS else (2 if count_blocks * SLOTS <= SEG_SCAN_PLACE_INTS else 3)
     del flush_w, flush_r
     clocks = sampler.stop()
 
@@ -478,10 +481,25 @@ def run_ours(args):
     achieved_expand = b_expand / (expand_ms * 1e-3) / 1e9
     achieved_shrink = b_shrink / (shrink_ms * 1e-3) / 1e9
     stream = _native.stream_kernels() != 0
+    fused = _native.stream_kernels() == 2  # the combined call is one kernel (K = N = 4096 fits it)
     k_shrink = "sgmv_shrink_stream_kernel<bf16>" if stream else "sgmv_shrink_mma_kernel<16,bf16>"
     k_expand = "sgmv_expand_stream_kernel<bf16>" if stream else "sgmv_expand_mma_kernel<16,bf16>"
+    k_fused = "sgmv_shrink_stream_kernel<bf16, fused>"
     traffic, traffic_source = traffic_record(k_expand)
     traffic_shrink, _ = traffic_record(k_shrink)
+    traffic_fused, traffic_fused_source = traffic_record(k_fused)
+    b_pair = b_shrink + b_expand
+    achieved_pair = b_pair / (pair_ms * 1e-3) / 1e9
+    if fused:  # the step's dominant kernel is the fused one
+        roofline = {"kernel": k_fused, "bound": "hbm", "achieved": achieved_pair, "peak": peak, "unit": "GB/s",
+                    "frac": achieved_pair / peak, "peak_source": peak_kind, "traffic": traffic_fused,
+                    "traffic_source": traffic_fused_source, "algorithmic_bytes_per_launch": b_pair,
+                    "avg_launch_ms": pair_ms}
+    else:
+        roofline = {"kernel": k_expand, "bound": "hbm", "achieved": achieved_expand, "peak": peak, "unit": "GB/s",
+                    "frac": achieved_expand / peak, "peak_source": peak_kind, "traffic": traffic,
+                    "traffic_source": traffic_source, "algorithmic_bytes_per_launch": b_expand,
+                    "avg_launch_ms": expand_ms}
 
     # the reference's own GPU path (its Triton kernels) on this B200, same batch
     triton_ref = _triton_pair_cfg2(dev, x, A, Bw, seq, wi, ranks, scales, y) if world == 1 else None
@@ -513,34 +531,24 @@ def run_ours(args):
         "config": {
             "workload": "BASELINE config 2 SGMV op: T=16384 token rows per GPU, K=N=4096, 64 slots + __base__, "
                         "max_rank 16, ranks U{0,4,8,16}, 20% base rows",
-            "step": "device segment table + sgmv shrink + sgmv expand (fused scale/add-back) issued as one "
-                    "call, the expand overlapping the shrink's end; CUDA graph",
+            "step": ("device segment table + sgmv shrink + sgmv expand (fused scale/add-back) issued as one call: "
+                     + ("one fused kernel, each CTA expanding the share it has just shrunk" if fused
+                        else "two kernels, the expand overlapping the shrink's end") + "; CUDA graph"),
             "l2": "step: inputs larger than L2 (x 128 MiB + y 128 MiB per GPU); per-kernel times: L2 flushed "
                   "(256 MiB write + 256 MiB read) before every launch, outside the timed difference",
             "parallelism": f"row data-parallel x{world}, independent slot caches, no collective in the step",
             "active_tokens_per_gpu": t_act,
         },
-        "roofline": {
-            "kernel": k_expand,
-            "bound": "hbm",
-            "achieved": achieved_expand,
-            "peak": peak,
-            "unit": "GB/s",
-            "frac": achieved_expand / peak,
-            "peak_source": peak_kind,
-            "traffic": traffic,
-            "traffic_source": traffic_source,
-            "algorithmic_bytes_per_launch": b_expand,
-            "avg_launch_ms": expand_ms,
-        },
+        "roofline": roofline,
         "kernels": {
             "shrink": {"kernel": k_shrink, "avg_launch_ms": shrink_ms, "bytes": b_shrink, "gbs": achieved_shrink,
                        "frac": achieved_shrink / peak, "traffic": traffic_shrink},
             "expand": {"kernel": k_expand, "avg_launch_ms": expand_ms, "bytes": b_expand, "gbs": achieved_expand,
                        "frac": achieved_expand / peak, "traffic": traffic},
             "segments": {"avg_ms": seg_ms, "launches": seg_launches},
-            "shrink_expand_call": {"avg_ms": pair_ms, "bytes": b_shrink + b_expand,
-                                   "gbs": (b_shrink + b_expand) / (pair_ms * 1e-3) / 1e9},
+            "shrink_expand_call": {"kernel": k_fused if fused else f"{k_shrink} + {k_expand}", "avg_ms": pair_ms,
+                                   "bytes": b_pair, "gbs": achieved_pair, "frac": achieved_pair / peak,
+                                   "traffic": traffic_fused if fused else None},
             "step_combined_gbs": b_comb / (ms_per_step * 1e-3) / 1e9,
         },
         "cpu_baseline": cb,
@@ -552,7 +560,7 @@ def run_ours(args):
                 "serial_ms_per_step": serial_ms,
                 "serial_path": "sgmv_lora_a_fwd + sgmv_lora_b_fwd (C-ABI) on one stream: pinned host x/y/metadata "
                                "in, y out"},
-        "gpu_launches": (seg_launches + 2) * args.steps,
+        "gpu_launches": (seg_launches + (1 if fused else 2)) * args.steps,
         "clocks": clocks,
         "triton_reference": triton_ref,
         "model_cfg3": cfg3,

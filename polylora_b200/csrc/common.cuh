@@ -186,6 +186,11 @@ __device__ __forceinline__ uint32_t ld_cg_u32(const void* p) {
   return v;
 }
 __device__ __forceinline__ int32_t ld_cg_i32(const int32_t* p) { return (int32_t)ld_cg_u32(p); }
+__device__ __forceinline__ int64_t ld_cg_i64(const int64_t* p) {
+  int64_t v;
+  asm volatile("ld.global.cg.s64 %0, [%1];" : "=l"(v) : "l"(p));
+  return v;
+}
 // The same ordering, cached in L1 as well: for data read by several warps of
 // the CTA after griddep_wait() (the previous grid has completed by then).
 __device__ __forceinline__ uint32_t ld_ca_u32(const void* p) {

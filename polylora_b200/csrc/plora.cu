@@ -145,6 +145,7 @@ int device_info(DeviceInfo** out) {
     SET_GRID((sgmv_shrink_stream_kernel<false, true>), kStreamSmemLimit)
     SET_GRID((sgmv_expand_stream_kernel<true>), kStreamSmemLimit)
     SET_GRID((sgmv_expand_stream_kernel<false>), kStreamSmemLimit)
+    SET_GRID(seg_scan_place_kernel, (kSegScanPlaceMaxInts + kSegMaxSlots + 1) * 4)
 #undef SET_GRID
     d.attrs_set = true;
   }
@@ -242,48 +243,6 @@ size_t fwd_workspace_bytes(int64_t num_rows, int64_t max_seq, int32_t num_slots)
          align256((size_t)(num_rows * max_seq) * 4);
 }
 
-int build_segments(const int64_t* wi, const int32_t* seq_lens, const int32_t* ranks,
-                   int64_t num_rows, int64_t max_seq, int32_t num_slots, int32_t* slot_start,
-                   int32_t* token_index, void* ws, size_t ws_bytes, cudaStream_t stream) {
-  if (num_slots < 1 || num_slots > kSegMaxSlots)
-    return fail(PLORA_ERR_UNSUPPORTED, "num_slots %d outside [1, %d]", num_slots, kSegMaxSlots);
-  if (num_rows < 0 || max_seq < 0)
-    return fail(PLORA_ERR_INVALID_ARGUMENT, "negative num_rows/max_seq");
-  if (!token_count_ok(num_rows, max_seq))
-    return fail(PLORA_ERR_UNSUPPORTED, "num_rows*max_seq exceeds int32 token ids");
-  if (!slot_start) return fail(PLORA_ERR_INVALID_ARGUMENT, "slot_start is null");
-  if (num_rows == 0 || max_seq == 0) {
-    PLORA_CUDA(cudaMemsetAsync(slot_start, 0, (size_t)(num_slots + 1) * 4, stream), "memset");
-    return PLORA_OK;
-  }
-  if (!wi || !seq_lens || !ranks || !token_index)
-    return fail(PLORA_ERR_INVALID_ARGUMENT, "null segment input");
-  const size_t need = seg_workspace_bytes(num_rows, num_slots);
-  if (!ws || ws_bytes < need)
-    return fail(PLORA_ERR_WORKSPACE, "segment workspace %zu < %zu bytes", ws_bytes, need);
-  if (num_rows <= kSegSmallRows && num_slots <= kSegSmallSlots && num_rows * max_seq <= kSegSmallTokens) {
-    seg_small_kernel<<<1, 1024, 0, stream>>>(wi, seq_lens, ranks, (int32_t)num_rows, max_seq, num_slots,
-                                             slot_start, token_index);
-    return check_launch("seg_small_kernel");
-  }
-  SegWorkspace w = seg_workspace_carve(ws, num_rows, num_slots);
-  const int64_t blocks = (num_rows + kSegRowsPerBlock - 1) / kSegRowsPerBlock;
-  if (blocks > INT32_MAX) return fail(PLORA_ERR_UNSUPPORTED, "too many rows");
-  seg_count_kernel<<<(unsigned)blocks, kSegRowsPerBlock, (size_t)num_slots * 4, stream>>>(
-      wi, seq_lens, ranks, num_rows, max_seq, num_slots, w);
-  int st = check_launch("seg_count_kernel");
-  if (st) return st;
-  seg_scan_kernel<<<1, 1024, (size_t)num_slots * 4, stream>>>((int32_t)blocks, num_slots, w,
-                                                               slot_start);
-  if ((st = check_launch("seg_scan_kernel"))) return st;
-  seg_place_kernel<<<(unsigned)((num_rows + 7) / 8), 256, 0, stream>>>(
-      num_rows, max_seq, seq_lens, (int32_t)blocks, w, slot_start, token_index);
-  return check_launch("seg_place_kernel");
-}
-
-// Tensor-core path eligibility (16-bit types, rank tile 16/32/64, 16-byte rows).
-bool tc_rank_ok(int64_t R) { return R == 16 || R == 32 || R == 64; }
-
 // Launches `kernel` with programmatic stream serialisation when `pdl` is set:
 // the kernel may then start while its predecessor in the stream finishes and
 // must call griddep_wait() before reading anything that predecessor writes.
@@ -314,6 +273,64 @@ cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
   cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
+
+int build_segments(const int64_t* wi, const int32_t* seq_lens, const int32_t* ranks,
+                   int64_t num_rows, int64_t max_seq, int32_t num_slots, int32_t* slot_start,
+                   int32_t* token_index, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  if (num_slots < 1 || num_slots > kSegMaxSlots)
+    return fail(PLORA_ERR_UNSUPPORTED, "num_slots %d outside [1, %d]", num_slots, kSegMaxSlots);
+  if (num_rows < 0 || max_seq < 0)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "negative num_rows/max_seq");
+  if (!token_count_ok(num_rows, max_seq))
+    return fail(PLORA_ERR_UNSUPPORTED, "num_rows*max_seq exceeds int32 token ids");
+  if (!slot_start) return fail(PLORA_ERR_INVALID_ARGUMENT, "slot_start is null");
+  if (num_rows == 0 || max_seq == 0) {
+    PLORA_CUDA(cudaMemsetAsync(slot_start, 0, (size_t)(num_slots + 1) * 4, stream), "memset");
+    return PLORA_OK;
+  }
+  if (!wi || !seq_lens || !ranks || !token_index)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "null segment input");
+  const size_t need = seg_workspace_bytes(num_rows, num_slots);
+  if (!ws || ws_bytes < need)
+    return fail(PLORA_ERR_WORKSPACE, "segment workspace %zu < %zu bytes", ws_bytes, need);
+  if (num_rows <= kSegSmallRows && num_slots <= kSegSmallSlots && num_rows * max_seq <= kSegSmallTokens) {
+    PLORA_CUDA(launch_kernel(seg_small_kernel, dim3(1), dim3(1024), 0, stream, true, 0, wi, seq_lens, ranks,
+                             (int32_t)num_rows, max_seq, num_slots, slot_start, token_index),
+               "launch seg_small_kernel");
+    return check_launch("seg_small_kernel");
+  }
+  SegWorkspace w = seg_workspace_carve(ws, num_rows, num_slots);
+  const int64_t blocks = (num_rows + kSegRowsPerBlock - 1) / kSegRowsPerBlock;
+  if (blocks > INT32_MAX) return fail(PLORA_ERR_UNSUPPORTED, "too many rows");
+  // programmatic launches: each kernel waits for its predecessor before touching memory
+  PLORA_CUDA(launch_kernel(seg_count_kernel, dim3((unsigned)blocks), dim3(kSegRowsPerBlock), (size_t)num_slots * 4,
+                           stream, true, 0, wi, seq_lens, ranks, num_rows, max_seq, num_slots, w),
+             "launch seg_count_kernel");
+  int st = check_launch("seg_count_kernel");
+  if (st) return st;
+  if (blocks * num_slots <= kSegScanPlaceMaxInts) {  // scan and placement in one launch
+    DeviceInfo* di = nullptr;
+    if ((st = device_info(&di))) return st;
+    const int64_t grid = std::min<int64_t>(di->sm_count, (num_rows + 31) / 32);
+    PLORA_CUDA(launch_kernel(seg_scan_place_kernel, dim3((unsigned)grid), dim3(1024),
+                             (size_t)(blocks * num_slots + num_slots + 1) * 4, stream, true, 0, num_rows, max_seq,
+                             seq_lens, (int32_t)blocks, num_slots, w, slot_start, token_index),
+               "launch seg_scan_place_kernel");
+    return check_launch("seg_scan_place_kernel");
+  }
+  PLORA_CUDA(launch_kernel(seg_scan_kernel, dim3(1), dim3(1024), (size_t)num_slots * 4, stream, true, 0,
+                           (int32_t)blocks, num_slots, w, slot_start),
+             "launch seg_scan_kernel");
+  if ((st = check_launch("seg_scan_kernel"))) return st;
+  PLORA_CUDA(launch_kernel(seg_place_kernel, dim3((unsigned)((num_rows + 7) / 8)), dim3(256), 0, stream, true, 0,
+                           num_rows, max_seq, seq_lens, (int32_t)blocks, w, slot_start, token_index),
+             "launch seg_place_kernel");
+  return check_launch("seg_place_kernel");
+}
+
+// Tensor-core path eligibility (16-bit types, rank tile 16/32/64, 16-byte rows).
+bool tc_rank_ok(int64_t R) { return R == 16 || R == 32 || R == 64; }
+
 
 // K parts of the grid-split shrink: parts of >= 512 rows (a multiple of 32),
 // at most 16 (the largest cluster).

@@ -3,6 +3,11 @@
 // flat tile schedule.  Integer work only; results are bit-exact and
 // deterministic (no atomics decide an order).
 //
+// The table kernels are launched programmatically: each may start while its
+// predecessor in the stream finishes, waits (griddep_wait) before reading or
+// writing global memory, reads what earlier kernels wrote with volatile L2
+// loads (which stay below the wait), and lets its successor start at once.
+//
 // Replaces the host-synchronising schedule construction of the reference,
 // src/polylora/sgmv.py:29-61 (_build_flat_schedule) and sgmv.py:304-309, and
 // the per-row slot lookups of layers.py:124-130.
@@ -56,17 +61,19 @@ __global__ void __launch_bounds__(kSegRowsPerBlock) seg_count_kernel(
     SegWorkspace ws) {
   extern __shared__ int32_t cnt[];  // [num_slots]
   for (int s = threadIdx.x; s < num_slots; s += blockDim.x) cnt[s] = 0;
+  griddep_wait();
+  griddep_launch();
 
   const int64_t row = (int64_t)blockIdx.x * kSegRowsPerBlock + threadIdx.x;
   int key = -1;
   int len = 0;
   if (row < num_rows) {
-    const int64_t slot = weight_indices[row];
+    const int64_t slot = ld_cg_i64(weight_indices + row);
+    int64_t l = ld_cg_i32(seq_lens + row);  // issued beside the slot's load
     if (slot < 0 || slot >= num_slots) {
       raise_status(PLORA_DEV_SLOT_RANGE);
     } else {
-      const int32_t rank = lora_ranks[slot];
-      int64_t l = seq_lens[row];
+      const int32_t rank = ld_cg_i32(lora_ranks + slot);
       l = l < 0 ? 0 : (l > max_seq ? max_seq : l);
       if (rank > 0 && l > 0) {
         key = (int)slot;
@@ -114,12 +121,14 @@ __global__ void __launch_bounds__(1024) seg_scan_kernel(int32_t num_blocks, int3
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nwarps = blockDim.x >> 5;
+  griddep_wait();
+  griddep_launch();
   for (int s = warp; s < num_slots; s += nwarps) {
     int32_t* row = ws.partial + (int64_t)s * num_blocks;
     int run = 0;
     for (int b0 = 0; b0 < num_blocks; b0 += 32) {
       const int b = b0 + lane;
-      const int v = b < num_blocks ? row[b] : 0;
+      const int v = b < num_blocks ? ld_cg_i32(row + b) : 0;
       int incl = v;
 #pragma unroll
       for (int d = 1; d < 32; d <<= 1) {
@@ -170,18 +179,126 @@ __global__ void __launch_bounds__(256) seg_place_kernel(int64_t num_rows, int64_
                                                          int32_t num_blocks, SegWorkspace ws,
                                                          const int32_t* __restrict__ slot_start,
                                                          int32_t* __restrict__ token_index) {
+  griddep_wait();
+  griddep_launch();
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= num_rows) return;
-  const int key = ws.row_info[row];
+  const int key = ld_cg_i32(ws.row_info + row);
   if (key < 0) return;
-  int64_t l = seq_lens[row];
+  int64_t l = ld_cg_i32(seq_lens + row);
   l = l < 0 ? 0 : (l > max_seq ? max_seq : l);
   const int64_t blk = row / kSegRowsPerBlock;
-  const int64_t dst = (int64_t)slot_start[key] + ws.partial[(int64_t)key * num_blocks + blk] +
-                      ws.row_off[row];
+  const int64_t dst = (int64_t)ld_cg_i32(slot_start + key) + ld_cg_i32(ws.partial + (int64_t)key * num_blocks + blk) +
+                      ld_cg_i32(ws.row_off + row);
   const int64_t tok0 = row * max_seq;
   for (int64_t m = lane; m < l; m += 32) token_index[dst + m] = (int32_t)(tok0 + m);
+}
+
+// Passes 2 and 3 in one launch, for tables whose count matrix (num_slots x
+// count blocks) fits shared memory: every block loads the whole matrix (it is
+// in L2), turns each slot's counts into the prefix over count blocks and the
+// slot totals into slot_start (block 0 writes it out), then places its own
+// contiguous range of rows, one warp per row.  The scan is repeated in every
+// block; it costs a few microseconds of SM time and saves a launch and a
+// round trip through global memory.  1024 threads.
+constexpr int kSegScanPlaceMaxInts = 12288;  // count-matrix limit: 48 KB of shared memory
+
+__global__ void __launch_bounds__(1024) seg_scan_place_kernel(
+    int64_t num_rows, int64_t max_seq, const int32_t* __restrict__ seq_lens, int32_t num_blocks,
+    int32_t num_slots, SegWorkspace ws, int32_t* __restrict__ slot_start, int32_t* __restrict__ token_index) {
+  extern __shared__ int32_t sm[];
+  int32_t* part = sm;                                        // [num_slots][num_blocks]
+  int32_t* base = sm + (int64_t)num_slots * num_blocks;      // [num_slots + 1] slot starts
+  __shared__ int32_t warp_sums[32];
+  __shared__ int32_t carry;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  griddep_wait();
+  griddep_launch();
+  const int n = num_slots * num_blocks;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) part[i] = ld_cg_i32(ws.partial + i);
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  // per slot (a warp each): counts -> prefix over count blocks; the total into base[s]
+  for (int s = warp; s < num_slots; s += nwarps) {
+    int32_t* row = part + (int64_t)s * num_blocks;
+    int run = 0;
+    for (int b0 = 0; b0 < num_blocks; b0 += 32) {
+      const int b = b0 + lane;
+      const int v = b < num_blocks ? row[b] : 0;
+      int incl = v;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += u;
+      }
+      if (b < num_blocks) row[b] = run + incl - v;
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) base[s] = run;
+  }
+  __syncthreads();
+  // exclusive scan of the totals over slots, in place
+  for (int s0 = 0; s0 < num_slots; s0 += blockDim.x) {
+    const int s = s0 + threadIdx.x;
+    const int total = s < num_slots ? base[s] : 0;
+    int incl = total;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += v;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int v = (lane < nwarps) ? warp_sums[lane] : 0;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v += u;
+      }
+      warp_sums[lane] = v;
+    }
+    __syncthreads();
+    const int excl = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + incl - total;
+    __syncthreads();  // every thread has read base[] of this chunk and carry
+    if (s < num_slots) base[s] = excl;
+    if (threadIdx.x == blockDim.x - 1) carry = excl + total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) base[num_slots] = carry;
+  __syncthreads();
+  if (blockIdx.x == 0)
+    for (int s = threadIdx.x; s <= num_slots; s += blockDim.x) slot_start[s] = base[s];
+  // this block's rows, 1024 at a time: a thread loads one row's metadata (all
+  // rows' loads in flight together), then one warp per row writes its ids
+  __shared__ int32_t row_dst[1024], row_len[1024];
+  const int64_t r0 = num_rows * blockIdx.x / gridDim.x, r1 = num_rows * (blockIdx.x + 1) / gridDim.x;
+  for (int64_t c = r0; c < r1; c += blockDim.x) {
+    const int64_t row = c + threadIdx.x;
+    int32_t dst = -1, len = 0;
+    if (row < r1) {
+      const int key = ld_cg_i32(ws.row_info + row);
+      const int32_t off = ld_cg_i32(ws.row_off + row);
+      int64_t l = ld_cg_i32(seq_lens + row);
+      if (key >= 0) {
+        dst = base[key] + part[(int64_t)key * num_blocks + row / kSegRowsPerBlock] + off;
+        len = (int32_t)(l < 0 ? 0 : (l > max_seq ? max_seq : l));
+      }
+    }
+    row_dst[threadIdx.x] = dst;
+    row_len[threadIdx.x] = len;
+    __syncthreads();
+    const int n = (int)(r1 - c < (int64_t)blockDim.x ? r1 - c : (int64_t)blockDim.x);
+    for (int i = warp; i < n; i += nwarps) {
+      if (row_dst[i] < 0) continue;
+      const int64_t tok0 = (c + i) * max_seq;
+      for (int m = lane; m < row_len[i]; m += 32) token_index[row_dst[i] + m] = (int32_t)(tok0 + m);
+    }
+    __syncthreads();
+  }
 }
 
 // One-launch builder for small batches (decode steps): one block of 1024
@@ -213,16 +330,18 @@ __global__ void __launch_bounds__(1024) seg_small_kernel(
   const int lane = t & 31;
   const int warp = t >> 5;
   for (int i = t; i < 32 * kSegSmallSlots; i += blockDim.x) (&cnt[0][0])[i] = 0;
+  griddep_wait();
+  griddep_launch();
 
   int key = -1;
   int len = 0;
   if (t < num_rows) {
-    const int64_t slot = weight_indices[t];
+    const int64_t slot = ld_cg_i64(weight_indices + t);
     if (slot < 0 || slot >= num_slots) {
       raise_status(PLORA_DEV_SLOT_RANGE);
     } else {
-      const int32_t rank = lora_ranks[slot];
-      int64_t l = seq_lens[t];
+      const int32_t rank = ld_cg_i32(lora_ranks + slot);
+      int64_t l = ld_cg_i32(seq_lens + t);
       l = l < 0 ? 0 : (l > max_seq ? max_seq : l);
       if (rank > 0 && l > 0) {
         key = (int)slot;
@@ -282,7 +401,7 @@ __global__ void __launch_bounds__(1024) seg_small_kernel(
   for (int r = warp; r < num_rows; r += 32) {
     const int dst = row_dst[r];
     if (dst < 0) continue;
-    int64_t l = seq_lens[r];
+    int64_t l = ld_cg_i32(seq_lens + r);
     l = l < 0 ? 0 : (l > max_seq ? max_seq : l);
     const int64_t tok0 = (int64_t)r * max_seq;
     for (int64_t m = lane; m < l; m += 32) token_index[dst + m] = (int32_t)(tok0 + m);
