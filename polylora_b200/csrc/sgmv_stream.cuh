@@ -9,7 +9,7 @@
 //  * At rank 16 a slot's LoRA-A (K x 16) or LoRA-B (16 x N) is 128 KB for K
 //    or N = 4096.  Split over 16 warps that is 8 KB per warp, 64 registers per
 //    lane in mma fragment layout.
-//  * shrink: token rows travel by one non-multicast `cp.async.bulk` per row
+//  * shrink: token rows travel by one plain `cp.async.bulk` per row
 //    (K * 2 bytes) into a ring of shared-memory stages of 8 rows, at a
 //    (K * 2 + 16)-byte pitch so that ldmatrix over eight rows hits eight bank
 //    groups.  The ring carries token rows only, refilled by a producer warp;
