@@ -39,7 +39,7 @@ T_TOKENS, K_IN, N_OUT, SLOTS, MAX_RANK = 16384, 4096, 4096, 65, 16
 SEG_ONE_LAUNCH_ROWS = 1024  # rows the one-launch segment builder takes (csrc/segments.cuh)
 SEG_SCAN_PLACE_INTS = 12288  # count-matrix size up to which scan and placement are one launch
 SEG_ROWS_PER_BLOCK = 256     # rows per count block of the segment builder
-E2E_CHUNKS = 8  # row chunks of the host-buffer pipeline (e2e leg)
+E2E_CHUNKS = 4  # row chunks of the host-buffer pipeline (e2e leg; 4: 5.40 ms, 8: 5.62, 16: 6.04 per step)
 ELEM = 2  # bf16
 
 
