@@ -1497,12 +1497,12 @@ def run_model_cfg5(args):
 
 def run_profile(args):
     """A small case for ncu: the config-2 inputs (x and y 128 MiB each, larger
-    than L2), two warm-up steps, then one step of segment table + shrink +
-    expand as plain launches.  Prints the kernel-source digest the capture
-    describes."""
+    than L2), three steps of segment table + combined shrink/expand call as
+    plain launches, then the shrink and the expand operators once each.
+    Prints the kernel-source digest the capture describes."""
     import torch
 
-    from polylora_b200.sgmv import build_segments, sgmv_shrink_expand
+    from polylora_b200.sgmv import build_segments, sgmv_expand, sgmv_shrink, sgmv_shrink_expand
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(0)
@@ -1521,6 +1521,9 @@ def run_profile(args):
     for _ in range(3):
         table = build_segments(wi, seq, ranks, 1)
         sgmv_shrink_expand(x, A, Bw, y, table, ranks, scales, tmp=tmp)
+    # then the two operators apart (the standalone stream shrink and expand), once each
+    sgmv_shrink(x, A, table, ranks, out=tmp)
+    sgmv_expand(tmp, Bw, y, table, ranks, scales)
     torch.cuda.synchronize()
     print(json.dumps({"workload": "profile", "kernel_source_sha256": kernel_source_digest(),
                       "active_tokens": int((ranks_np[wi_np] > 0).sum())}), flush=True)
