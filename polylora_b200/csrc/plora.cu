@@ -365,12 +365,15 @@ int shrink_impl(const void* x, const void* a, void* tmp, const int32_t* ranks, S
     if (use_weight_split(num_tokens, di)) {  // few tokens per slot: grid split
       int kp = 0, kp_rows = 0;
       grid_k_parts(K, &kp, &kp_rows);
-      const dim3 grid((unsigned)kp, (unsigned)seg.num_slots);
+      // rows: slots plus later 16-token tiles (few K parts, rows within a grid dimension), else slots
+      const int64_t tile_rows = grid_tile_rows(num_tokens, seg.num_slots);
+      const bool by_tile = kp <= kTileMaxKParts && tile_rows <= 65535;
+      const dim3 grid((unsigned)kp, (unsigned)(by_tile ? tile_rows : seg.num_slots));
       // the kernel reads its inputs only after griddep_wait(): always launched programmatically
 #define LAUNCH_SHRINK_GRID(RPV)                                                                    \
   PLORA_CUDA(launch_kernel(bf ? sgmv_shrink_grid_kernel<RPV, true> : sgmv_shrink_grid_kernel<RPV, false>, \
                            grid, dim3(kGridThreads), ShrinkGridCfg<RPV>::kSmemBytes, stream, true, kp, \
-                           args, kp_rows),                                                         \
+                           args, kp_rows, by_tile, (int)grid_later_rows(num_tokens)),              \
              "launch sgmv_shrink_grid_kernel");
       if (R == 16) {
         LAUNCH_SHRINK_GRID(16)
@@ -451,12 +454,16 @@ int expand_impl(const void* tmp, const void* b, void* y, const int32_t* ranks, c
   if (tc) {
     const bool bf = dtype == PLORA_DTYPE_BF16;
     if (use_weight_split(num_tokens, di)) {  // few tokens per slot: grid split
-      const dim3 grid((unsigned)((N + kGridCols - 1) / kGridCols), (unsigned)seg.num_slots);
+      // rows: slots plus later 16-token tiles (few column chunks, rows within a grid dimension), else slots
+      const int64_t chunks = (N + kGridCols - 1) / kGridCols;
+      const int64_t tile_rows = grid_tile_rows(num_tokens, seg.num_slots);
+      const bool by_tile = chunks <= kTileMaxColChunks && tile_rows <= 65535;
+      const dim3 grid((unsigned)chunks, (unsigned)(by_tile ? tile_rows : seg.num_slots));
       // programmatic only right after this library's shrink: tmp is read after griddep_wait()
 #define LAUNCH_EXPAND_GRID(RPV)                                                                    \
   PLORA_CUDA(launch_kernel(bf ? sgmv_expand_grid_kernel<RPV, true> : sgmv_expand_grid_kernel<RPV, false>, \
                            grid, dim3(kGridThreads), ExpandGridCfg<RPV>::kSmemBytes, stream,       \
-                           after_shrink, 0, args),                                                 \
+                           after_shrink, 0, args, by_tile, (int)grid_later_rows(num_tokens)),       \
              "launch sgmv_expand_grid_kernel");
       if (R == 16) {
         LAUNCH_EXPAND_GRID(16)

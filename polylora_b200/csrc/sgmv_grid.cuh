@@ -16,7 +16,8 @@
 //    CTA (q, s) accumulates x A[s] over the K rows of part q for each 16-token
 //    tile of the slot; CTA 0 of the cluster adds the parts' fp32 partials in
 //    part order through distributed shared memory, rounds and writes tmp.
-// CTAs of empty slots (or of rank 0) exit after three loads.  Results are
+// Grid rows are slots, plus rows for the later 16-token tiles of slots with
+// more than 16 tokens (grid_row), while the rows fit a grid dimension.  Results are
 // deterministic (fixed summation order).  The mma operands and shared-memory
 // layouts are those of the token-split kernels (sgmv_mma.cuh).
 //
@@ -78,18 +79,120 @@ __device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
   return v;
 }
 
+// Grid rows by 16-token tile (by_tile): the first num_tokens / 16 rows take the
+// later tiles (tile >= 1) of slots of rank > 0, the e-th in slot order for row
+// e, found by a warp scan of the slots' later-tile counts; row E + s (E =
+// num_tokens / 16) takes the first tile of slot s, as one load round trip
+// shows (slot_start, rank).  So a popular slot's tiles run in parallel in CTAs
+// of their own, launched first, while a row of an empty slot still costs one
+// round trip; only the few later-tile rows scan, and those past the last
+// later tile leave after one warp reduction.  Warp-collective; false when the
+// row has no tile.
+struct GridTile {
+  int slot, rank;
+  int64_t begin, end;  // this row's tokens in the segment table
+};
+
+__device__ __forceinline__ bool grid_later_tile(const SegTable& seg, const int32_t* ranks, int e, int lane,
+                                                GridTile& out) {
+  int carry = 0;        // later tiles of the slots before this round
+  bool found = false;   // warp-uniform
+  for (int c0 = 0; c0 < seg.num_slots; c0 += 256) {
+    int st[8], cnt[8], rk[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int sl = c0 + 32 * k + lane;
+      st[k] = cnt[k] = rk[k] = 0;
+      if (sl < seg.num_slots) {
+        st[k] = ld_cg_i32(seg.slot_start + sl);
+        cnt[k] = ld_cg_i32(seg.slot_start + sl + 1) - st[k];
+        rk[k] = __ldg(ranks + sl);
+      }
+    }
+    {  // rows past the last later tile (most of them) leave after one reduction
+      int sum = 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) sum += (rk[k] > 0 && cnt[k] > kGridTile) ? (cnt[k] - 1) / kGridTile : 0;
+      const int total = __reduce_add_sync(0xffffffffu, sum);
+      if (e >= carry + total) {
+        carry += total;
+        continue;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int nt = (rk[k] > 0 && cnt[k] > kGridTile) ? (cnt[k] - 1) / kGridTile : 0;
+      int incl = nt;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += u;
+      }
+      const int lo = carry + incl - nt;  // this lane's slot's first later tile
+      // no exit inside the unrolled loop: st/cnt/rk stay in registers
+      const uint32_t hit = __ballot_sync(0xffffffffu, !found && lo <= e && e < lo + nt);
+      if (hit != 0u) {
+        const int l = __ffs(hit) - 1;
+        const int tile = 1 + e - __shfl_sync(0xffffffffu, lo, l);
+        const int64_t b = __shfl_sync(0xffffffffu, st[k], l);
+        const int64_t n = __shfl_sync(0xffffffffu, cnt[k], l);
+        out.slot = c0 + 32 * k + l;
+        out.rank = __shfl_sync(0xffffffffu, rk[k], l);
+        out.begin = b + (int64_t)kGridTile * tile;
+        out.end = min(b + n, out.begin + kGridTile);
+        found = true;
+      }
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (found) return true;
+  }
+  return false;
+}
+
+// This CTA's row of the grid: a whole slot (!by_tile) or one tile of one.
+__device__ __forceinline__ bool grid_row(const SegTable& seg, const int32_t* ranks, bool by_tile,
+                                         int later_rows, int lane, GridTile& out) {
+  const int j = (int)blockIdx.y - (by_tile ? later_rows : 0);
+  if (j >= 0) {
+    out.slot = j;
+    out.begin = ld_cg_i32(seg.slot_start + j);
+    out.end = ld_cg_i32(seg.slot_start + j + 1);
+    out.rank = __ldg(ranks + j);
+    if (by_tile) out.end = min(out.end, out.begin + kGridTile);
+    return true;
+  }
+  return grid_later_tile(seg, ranks, (int)blockIdx.y, lane, out);
+}
+
+// Grid rows of the by-tile mapping for num_tokens tokens over num_slots slots:
+// at most num_tokens / 16 later tiles, then one row per slot.  Which kernels
+// take it (config-4 decode, 256 tokens over 128 slots, on B200): the shrink
+// while its clusters have at most 8 K parts (q_proj 34.7 -> 26.8 us; at 16
+// parts the extra 16-CTA cluster rows cost more than the split saves, 65.6
+// -> 68.8 us at K = 14336), the expand while it has at most 16 column chunks
+// (q_proj 24.7 -> 18.3 us; at N = 14336 the grid is 13 waves deep and
+// splitting costs, 37.0 -> 42.9 us).
+constexpr int kTileMaxKParts = 8;
+constexpr int kTileMaxColChunks = 16;
+__host__ __device__ inline int64_t grid_later_rows(int64_t num_tokens) { return num_tokens / kGridTile; }
+__host__ __device__ inline int64_t grid_tile_rows(int64_t num_tokens, int64_t num_slots) {
+  return grid_later_rows(num_tokens) + num_slots;
+}
+
 // ------------------------------------------------------------------- expand
 template <int RP, bool BF16>
-__global__ void __launch_bounds__(kGridThreads, 2) sgmv_expand_grid_kernel(const ExpandArgs args) {
+__global__ void __launch_bounds__(kGridThreads, 2) sgmv_expand_grid_kernel(const ExpandArgs args, bool by_tile, int later_rows) {
   using Cfg = ExpandGridCfg<RP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int s = blockIdx.y;
-  const int64_t t_begin = ld_cg_i32(args.seg.slot_start + s);
-  const int64_t t_end = ld_cg_i32(args.seg.slot_start + s + 1);
-  const int rank = __ldg(args.ranks + s);
+  // this CTA's tokens: one 16-token tile (by_tile) or all of slot blockIdx.y
+  GridTile gt;
+  if (!grid_row(args.seg, args.ranks, by_tile, later_rows, lane, gt)) return;
+  const int s = gt.slot;
+  const int64_t t_begin = gt.begin, t_end = gt.end;
+  const int rank = gt.rank;
   const int N = args.N, R = args.R;
   const int col0 = blockIdx.x * kGridCols + warp * 64;
   if (t_end <= t_begin || rank <= 0 || col0 >= N) return;  // no barrier follows
@@ -206,7 +309,7 @@ __global__ void __launch_bounds__(kGridThreads, 2) sgmv_expand_grid_kernel(const
 // [q * kp_rows, (q + 1) * kp_rows) (kp_rows a multiple of 32).
 template <int RP, bool BF16>
 __global__ void __launch_bounds__(kGridThreads, 2)
-    sgmv_shrink_grid_kernel(const ShrinkArgs args, int kp_rows) {
+    sgmv_shrink_grid_kernel(const ShrinkArgs args, int kp_rows, bool by_tile, int later_rows) {
   using Cfg = ShrinkGridCfg<RP>;
   using E = Elem<BF16>;
   extern __shared__ uint8_t smem_raw[];
@@ -215,10 +318,12 @@ __global__ void __launch_bounds__(kGridThreads, 2)
   const int lane = threadIdx.x & 31;
   griddep_wait();    // inputs (segment table, x) come from earlier kernels
   griddep_launch();  // the expand may start on SMs this grid releases
-  const int s = blockIdx.y;
-  const int64_t t_begin = ld_cg_i32(args.seg.slot_start + s);
-  const int64_t t_end = ld_cg_i32(args.seg.slot_start + s + 1);
-  const int rank = __ldg(args.ranks + s);
+  // this cluster's tokens: one 16-token tile (by_tile) or all of slot blockIdx.y
+  GridTile gt;
+  if (!grid_row(args.seg, args.ranks, by_tile, later_rows, lane, gt)) return;  // uniform (one grid row)
+  const int s = gt.slot;
+  const int64_t t_begin = gt.begin, t_end = gt.end;
+  const int rank = gt.rank;
   if (t_end <= t_begin || rank <= 0) return;  // uniform across the cluster (one slot)
   const int K = args.K, R = args.R;
   const int n_eff = min(rank * args.stack_num, R);

@@ -162,3 +162,14 @@ def test_config4_layer_shapes(K, N, step, cuda_status_clean):
     rows, seq = (16, 1024) if step == "prefill" else (256, 1)
     c = _case(300 + K + N, rows, seq, K, N, 129, 64, [8, 16, 32, 64], 0.0, popularity=_zipf(128, 1.1))
     _check_case(c, chunk_rows=4 if step == "prefill" else 256)
+
+
+@pytest.mark.parametrize("ns,rows", [(601, 2048), (4096, 1500)], ids=["601_slots", "4096_slots"])
+def test_slot_grid_later_tiles_many_slots(ns, rows, cuda_status_clean):
+    """The slot grid's later-tile rows (slots holding more than 16 tokens get
+    one grid row per further 16-token tile) when the slot table spans several
+    256-slot rounds of the row search: Zipf popularity puts hundreds of tokens
+    on the first slots and one or none on the rest."""
+    c = _case(400 + ns, rows, 1, 1024, 1024, ns, 16, [4, 8, 16], 0.1, popularity=_zipf(ns - 1, 1.1))
+    _check_case(c, chunk_rows=rows, modes=("weight_split", "combined"))
+
