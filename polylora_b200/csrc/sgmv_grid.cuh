@@ -167,11 +167,11 @@ __device__ __forceinline__ bool grid_row(const SegTable& seg, const int32_t* ran
 // Grid rows of the by-tile mapping for num_tokens tokens over num_slots slots:
 // at most num_tokens / 16 later tiles, then one row per slot.  Which kernels
 // take it (config-4 decode, 256 tokens over 128 slots, on B200): the shrink
-// while its clusters have at most 8 K parts (q_proj 34.7 -> 26.8 us; at 16
-// parts the extra 16-CTA cluster rows cost more than the split saves, 65.6
-// -> 68.8 us at K = 14336), the expand while it has at most 16 column chunks
-// (q_proj 24.7 -> 18.3 us; at N = 14336 the grid is 13 waves deep and
-// splitting costs, 37.0 -> 42.9 us).
+// while its clusters have at most 8 K parts (q_proj 34.7 -> 26.8 us; with 16
+// parts the extra 16-CTA cluster rows cost more than the split saved, 65.6 ->
+// 68.8 us at K = 14336), the expand while it has at most 16 column chunks
+// (q_proj 24.7 -> 18.3 us; at N = 14336 the grid is many waves deep and
+// splitting cost 37.0 -> 42.9 us).
 constexpr int kTileMaxKParts = 8;
 constexpr int kTileMaxColChunks = 16;
 __host__ __device__ inline int64_t grid_later_rows(int64_t num_tokens) { return num_tokens / kGridTile; }
@@ -181,7 +181,10 @@ __host__ __device__ inline int64_t grid_tile_rows(int64_t num_tokens, int64_t nu
 
 // ------------------------------------------------------------------- expand
 template <int RP, bool BF16>
-__global__ void __launch_bounds__(kGridThreads, 2) sgmv_expand_grid_kernel(const ExpandArgs args, bool by_tile, int later_rows) {
+// 3 CTAs per SM (<= 85 registers, 75 KB of shared memory each at rank 64): at
+// config-4 decode the gate_proj expand took 30.0 us against 36.9 with 2.
+__global__ void __launch_bounds__(kGridThreads, 3)
+    sgmv_expand_grid_kernel(const ExpandArgs args, bool by_tile, int later_rows) {
   using Cfg = ExpandGridCfg<RP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -409,6 +412,10 @@ __global__ void __launch_bounds__(kGridThreads, 2)
           p[(tk + 1) * RP + r + 8] = acc[rt][nt][3];
         }
     }
+    // the token of the tmp row this thread writes below (one piece per thread:
+    // cnt * RP / 8 <= kGridThreads), loaded before the barriers hide its latency
+    static_assert(kGridTile * (RP / 8) <= kGridThreads, "one tmp piece per thread");
+    const int64_t tok_w = threadIdx.x < cnt * (RP / 8) ? ld_cg_i32(args.seg.token_index + a + threadIdx.x / (RP / 8)) : 0;
     __syncthreads();
     for (int i = threadIdx.x; i < kGridTile * RP; i += kGridThreads) {
       float v = 0.f;
@@ -419,8 +426,8 @@ __global__ void __launch_bounds__(kGridThreads, 2)
     cluster_sync();
     if (cluster_ctarank() == 0) {
       const int kp = (int)gridDim.x;  // the cluster spans the K parts
-      for (int i = threadIdx.x; i < cnt * (RP / 8); i += kGridThreads) {
-        const int row = i / (RP / 8), cg = i - row * (RP / 8);
+      if (threadIdx.x < cnt * (RP / 8)) {
+        const int row = threadIdx.x / (RP / 8), cg = threadIdx.x - row * (RP / 8);
         float v[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] = 0.f;
@@ -438,8 +445,7 @@ __global__ void __launch_bounds__(kGridThreads, 2)
           out[e] = (uint32_t)E::from_f(c0 < n_eff ? v[2 * e] : 0.f) |
                    ((uint32_t)E::from_f(c0 + 1 < n_eff ? v[2 * e + 1] : 0.f) << 16);
         }
-        const int64_t tok = ld_cg_i32(args.seg.token_index + a + row);
-        *reinterpret_cast<uint4*>(args.tmp + (tok * R + cg * 8) * 2) = make_uint4(out[0], out[1], out[2], out[3]);
+        *reinterpret_cast<uint4*>(args.tmp + (tok_w * R + cg * 8) * 2) = make_uint4(out[0], out[1], out[2], out[3]);
       }
     }
     cluster_sync();  // the parts' partials and stages are reused by the next tile
