@@ -1219,7 +1219,7 @@ def run_model_cfg4(args):
     def time_graphed_decode(model, base, ids, input_ids, steps):
         """Decode forward replayed as one CUDA graph per call (GraphedForward;
         unpadded rows, so no mask), beside the base model captured the same way."""
-        from polylora_b200.graphed import GraphedForward
+        from polylora_b200.graphed import GraphedForward, eager_mask_decisions
 
         with torch.inference_mode():
             graphed = GraphedForward(model, ids, input_ids=input_ids)
@@ -1231,7 +1231,7 @@ def run_model_cfg4(args):
                     base(input_ids=static_ids)
             torch.cuda.current_stream().wait_stream(side)
             base_graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(base_graph):
+            with eager_mask_decisions(), torch.cuda.graph(base_graph):  # as GraphedForward captures
                 base(input_ids=static_ids)
             ref = model(input_ids=input_ids, adapter_ids=ids).last_hidden_state
             match = bool(torch.equal(graphed(ids, input_ids=input_ids), ref))

@@ -13,15 +13,74 @@ included); the shapes, the input tensors' shapes and the model may not.
 
 The reference has no counterpart (its forward syncs with the host in every
 layer, src/polylora/sgmv.py:51,59).
+
+Attention masks under capture: transformers' mask helpers treat CUDA stream
+capture like tracing and then build an explicit causal mask even for an
+unpadded batch whose causal mask eager mode skips (one query token, or as
+many queries as keys).  SDPA cannot use its flash kernel with an explicit
+mask, so a captured Llama-shaped decode step ran the memory-efficient kernel
+at ~230 us per layer instead of ~40.  A graph is replayed only with the
+shapes it was captured with, so the eager decision holds for it when the
+positions are the model's own; captures given neither ``attention_mask`` nor
+``position_ids`` therefore take it (``eager_mask_decisions``).
 """
 
 from __future__ import annotations
 
+import contextlib
 from typing import Any
 
 import torch
 
 from .context import LoraBatchContext, use_lora_context
+
+
+@contextlib.contextmanager
+def eager_mask_decisions():
+    """Within the block, while a CUDA stream captures, transformers' mask
+    helpers decide as in eager mode for a batch given neither a padding mask
+    nor position ids: the positions are the model's own aranges (no packed
+    sequences), and the causal mask is skipped for one query token or as many
+    queries as keys, so that SDPA applies ``is_causal`` itself.  Eager mode
+    reaches the same decisions by reading tensor values, which a capture cannot
+    do.  Outside a capture, under other tracing, with a padding mask, or on
+    XPU devices the helpers run unchanged.  A no-op without transformers or
+    when its helpers have other names."""
+    try:
+        from transformers import masking_utils
+        from transformers.utils import import_utils
+    except ImportError:
+        yield
+        return
+    packed = getattr(masking_utils, "find_packed_sequence_indices", None)
+    skip = getattr(masking_utils, "_ignore_causal_mask_sdpa", None)
+    compiling = getattr(import_utils, "is_torchdynamo_compiling", None)
+    jit_tracing = getattr(import_utils, "is_jit_tracing", None)
+    capturing = getattr(import_utils, "is_cuda_stream_capturing", None)  # False where CUDA is absent
+    if None in (packed, skip, compiling, jit_tracing, capturing) or getattr(masking_utils, "_is_torch_xpu_available",
+                                                                           True):
+        yield
+        return
+
+    def capturing_only() -> bool:
+        return capturing() and not compiling() and not jit_tracing()
+
+    def packed_eager(position_ids):
+        return None if capturing_only() else packed(position_ids)
+
+    def skip_eager(padding_mask, query_length, kv_length, kv_offset, local_attention_size=None):
+        if padding_mask is None and capturing_only():
+            return (query_length == 1 or kv_length == query_length) and (
+                local_attention_size is None or kv_length < local_attention_size)
+        return skip(padding_mask, query_length, kv_length, kv_offset, local_attention_size)
+
+    masking_utils.find_packed_sequence_indices = packed_eager
+    masking_utils._ignore_causal_mask_sdpa = skip_eager
+    try:
+        yield
+    finally:
+        masking_utils.find_packed_sequence_indices = packed
+        masking_utils._ignore_causal_mask_sdpa = skip
 
 
 class GraphedForward:
@@ -31,7 +90,9 @@ class GraphedForward:
     every call must keep; ``output`` picks the tensor to return from the base
     model's output (default: ``last_hidden_state`` when present).  Pass no
     ``attention_mask`` for unpadded batches: mask helpers of some models sync
-    with the host, which a capture cannot contain.
+    with the host, which a capture cannot contain.  Given neither a mask nor
+    position ids, the capture takes the eager mode's attention-mask decisions
+    (``eager_mask_decisions``).
     """
 
     def __init__(self, model: Any, adapter_ids: list[str], warmup: int = 2, output=None, **inputs: torch.Tensor):
@@ -63,7 +124,9 @@ class GraphedForward:
         torch.cuda.current_stream(device).wait_stream(side)
         torch.cuda.synchronize(device)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.inference_mode(), torch.cuda.graph(self.graph):
+        own_positions = "attention_mask" not in self.static and "position_ids" not in self.static
+        with torch.inference_mode(), (eager_mask_decisions() if own_positions else contextlib.nullcontext()), \
+                torch.cuda.graph(self.graph):
             self.out = device_part()
         torch.cuda.synchronize(device)
 

@@ -63,3 +63,20 @@ def test_graphed_decode_matches_eager_across_refills(cuda_status_clean):
         base2 = model.base_model(input_ids=x2).last_hidden_state
     torch.testing.assert_close(got2, ref2, rtol=0, atol=0)
     assert not torch.equal(got2, base2)  # the adapters did act
+
+
+def test_graphed_unpadded_prefill_matches_eager(cuda_status_clean):
+    """Several tokens per row, no attention mask: the capture skips the causal
+    mask as eager mode does (SDPA's own causal path, not an explicit mask), so
+    replay and eager agree bit for bit."""
+    dev = torch.device("cuda")
+    model = _model(dev)
+    g = torch.Generator(device=dev).manual_seed(3)
+    ids = ["a0", "__base__", "a1", "a2"]
+    x = torch.randint(0, 1000, (4, 16), device=dev, generator=g)
+    with torch.inference_mode():
+        graphed = GraphedForward(model, ids, input_ids=x)
+        ref = model(input_ids=x, adapter_ids=ids).last_hidden_state
+        for _ in range(2):
+            got = graphed(ids, input_ids=x).clone()
+            torch.testing.assert_close(got, ref, rtol=0, atol=0)
