@@ -1385,14 +1385,46 @@ def run_model_cfg5(args):
         return ids, input_ids
 
     micro_batches = [0]
+    # attribution of a batch's time (timed pass with prefetch, this rank): host
+    # seconds in the slot policy (CPU-tier gets, disk loads left on the critical
+    # path, refill issue) and device time of each micro-batch forward (events
+    # around the base model call, after the policy; includes waits for refills)
+    attrib = {"on": False, "host_s": 0.0, "fwd": []}
+    prepare = model.prepare_lora_context
+
+    def timed_prepare(*a, **k):
+        t = time.perf_counter()
+        try:
+            return prepare(*a, **k)
+        finally:
+            if attrib["on"]:
+                attrib["host_s"] += time.perf_counter() - t
+
+    model.prepare_lora_context = timed_prepare
+    inner_forward = base.forward
+
+    def timed_forward(*a, **k):
+        if not attrib["on"]:
+            return inner_forward(*a, **k)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = inner_forward(*a, **k)
+        e1.record()
+        attrib["fwd"].append((e0, e1))
+        return out
+
+    base.forward = timed_forward
+
+    def groups_of(adapter_ids):
+        order = list(dict.fromkeys(adapter_ids))
+        for i in range(0, len(order), CFG5_SLOTS):
+            group = set(order[i:i + CFG5_SLOTS])
+            yield [j for j, a in enumerate(adapter_ids) if a in group]
 
     def serve(adapter_ids, input_ids):
         """This rank's rows as micro-batches of <= 32 distinct adapters (in order of first use)."""
         out = torch.empty(input_ids.shape + (768,), device=dev, dtype=torch.bfloat16)
-        order = list(dict.fromkeys(adapter_ids))
-        for i in range(0, len(order), CFG5_SLOTS):
-            group = set(order[i:i + CFG5_SLOTS])
-            rows = [j for j, a in enumerate(adapter_ids) if a in group]
+        for rows in groups_of(adapter_ids):
             idx = torch.tensor(rows, device=dev)
             res = model(input_ids=input_ids.index_select(0, idx), adapter_ids=[adapter_ids[j] for j in rows])
             out.index_copy_(0, idx, res.last_hidden_state)
@@ -1414,9 +1446,10 @@ def run_model_cfg5(args):
     visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
     gpu_ids = [v for v in visible.split(",") if v.strip().isdigit()]
     sampler = ClockSampler(int(gpu_ids[local]) if local < len(gpu_ids) else local)
-    def run_pass(seq, prefetch):
+    def run_pass(seq, prefetch, attribute=False):
         """Warm-up then timed batches; with `prefetch`, each step first queues the
-        next batch's adapters for the CPU tier's prefetch thread (this rank's rows)."""
+        next batch's adapters for the CPU tier's prefetch thread (this rank's rows).
+        With `attribute`, the timed batches feed `attrib`."""
         def my_ids(ids):
             lo, hi = len(ids) * rank // world, len(ids) * (rank + 1) // world
             return ids[lo:hi]
@@ -1430,10 +1463,12 @@ def run_model_cfg5(args):
         st0, ld0, mbs0 = dict(cache.stats), disk_loads[0], micro_batches[0]
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
+        attrib["on"] = attribute
         for i, (ids, x) in enumerate(seq[nw:], start=nw):
             if prefetch and i + 1 < len(seq):
                 model.prefetch(my_ids(seq[i + 1][0]))
             step(ids, x)
+        attrib["on"] = False
         e1.record()
         e1.synchronize()
         store.wait_prefetches()
@@ -1443,8 +1478,26 @@ def run_model_cfg5(args):
     with torch.inference_mode():
         ms_nopf, _, _, _ = run_pass(batches[: nw + args.steps], prefetch=False)
         sampler.start()
-        ms, stats0, loads0, mb0 = run_pass(batches[nw + args.steps:], prefetch=True)
+        ms, stats0, loads0, mb0 = run_pass(batches[nw + args.steps:], prefetch=True, attribute=True)
         clocks = sampler.stop()
+        fwd_ms = sum(a.elapsed_time(b) for a, b in attrib["fwd"]) / args.steps
+        # the last batch's micro-batches again, each right after a first run that made
+        # its adapters resident: the forwards without refills or policy misses
+        ids, x = batches[-1]
+        n = x.shape[0]
+        lo, hi = n * rank // world, n * (rank + 1) // world
+        my_ids_, my_x = ids[lo:hi], x[lo:hi]
+        resident_ms = 0.0
+        for rows in groups_of(my_ids_):
+            sub_ids = [my_ids_[j] for j in rows]
+            sub_x = my_x.index_select(0, torch.tensor(rows, device=dev))
+            model(input_ids=sub_x, adapter_ids=sub_ids)
+            torch.cuda.synchronize()
+            attrib["on"], attrib["fwd"] = True, []
+            model(input_ids=sub_x, adapter_ids=sub_ids)
+            attrib["on"] = False
+            torch.cuda.synchronize()
+            resident_ms += sum(a.elapsed_time(b) for a, b in attrib["fwd"])
         # the same batches through the base model alone
         torch.cuda.synchronize()
         b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1485,6 +1538,17 @@ def run_model_cfg5(args):
                 "evictions": delta["evictions"] / args.steps,
                 "refill_h2d_MB": delta["h2d_bytes"] / args.steps / 1e6,
                 "disk_loads": (disk_loads[0] - loads0) / args.steps,
+            },
+            "attribution_rank0_ms_per_step": {
+                "slot_policy_host": attrib["host_s"] * 1e3 / args.steps,
+                "micro_batch_forwards_device": fwd_ms,
+                "micro_batch_forwards_device_resident": resident_ms,
+                "device_idle_or_between_forwards": ms - fwd_ms,
+                "note": "slot_policy_host: host time in the slot policy (CPU-tier gets, disk loads on the "
+                        "critical path, refill issue); micro_batch_forwards_device: events around each "
+                        "micro-batch's base-model call (LoRA kernels included, and waits for its refills); "
+                        "_resident: the last batch's micro-batches re-run with their adapters resident; "
+                        "device_idle_or_between_forwards: the step minus the forwards",
             },
             "catalog_setup_s": t_setup,
             "base_model_ms_per_step": ms_base, "lora_overhead_frac": ms / ms_base - 1.0,
