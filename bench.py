@@ -451,8 +451,13 @@ def run_ours(args):
     ranks_d.copy_(meta_h[2])
     scales_d.copy_(meta_h[3])
 
-    def pipelined_step():  # the package's host-buffer entry: row chunks over two copy streams
-        pipe(x_h, A_b, Bw, meta_h[0], meta_h[1], ranks_d, scales_d, y_h, out_h)
+    def pipelined_step():  # the package's host-buffer entry, in place: only the table's rows cross the bus
+        pipe(x_h, A_b, Bw, meta_h[0], meta_h[1], ranks_d, scales_d, y_h, y_h)
+
+    pipe_all = HostLoraPipeline(dev, chunks=E2E_CHUNKS, active_rows=False)
+
+    def all_rows_step():  # the same call moving every row by copies
+        pipe_all(x_h, A_b, Bw, meta_h[0], meta_h[1], ranks_d, scales_d, y_h, out_h)
 
     def time_e2e(fn):
         with torch.cuda.stream(stream):
@@ -470,9 +475,11 @@ def run_ours(args):
         return max_over_ranks(e0.elapsed_time(e1)) / e_steps
 
     serial_ms = time_e2e(serial_step)
-    e2e_ms = time_e2e(pipelined_step)
-    h2d = x_h.numel() * 2 + y_h.numel() * 2 + sum(t.numel() * t.element_size() for t in meta_h[:2])
-    d2h = out_h.numel() * 2
+    all_rows_ms = time_e2e(all_rows_step)
+    e2e_ms = time_e2e(pipelined_step)  # last: it adds each step's delta into y_h
+    meta_bytes = sum(t.numel() * t.element_size() for t in meta_h[:2])
+    h2d = t_act * (K_IN + N_OUT) * ELEM + meta_bytes  # x and base-output rows of the active tokens
+    d2h = t_act * N_OUT * ELEM
     status = _native.device_status(clear=True)
     if status:
         raise RuntimeError(f"device status {status:#x} during the bench")
@@ -554,9 +561,15 @@ def run_ours(args):
         "cpu_baseline": cb,
         "e2e": {"value": world * T_TOKENS / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                "path": f"HostLoraPipeline ({E2E_CHUNKS} row chunks; per chunk: pinned host x, base output, "
-                        "seq_lens, weight_indices in on one copy stream, segment table + shrink + expand (C-ABI), "
-                        "output out on a second copy stream); slot weights, ranks, scalings resident",
+                "path": f"HostLoraPipeline in place ({E2E_CHUNKS} row chunks; per chunk: seq_lens, "
+                        "weight_indices in by copy, segment table, the table's x and base-output rows read "
+                        "from pinned host memory by plora_gather_token_rows, shrink + expand, the table's "
+                        "output rows written back by plora_scatter_token_rows on a second stream; rows of "
+                        "__base__ / rank-0 tokens stay in host memory, unchanged); slot weights, ranks, "
+                        "scalings resident",
+                "all_rows_ms_per_step": all_rows_ms,
+                "all_rows_path": "the same pipeline copying every row in and out (x, base output in on one copy "
+                                 "stream, output out on another)",
                 "serial_ms_per_step": serial_ms,
                 "serial_path": "sgmv_lora_a_fwd + sgmv_lora_b_fwd (C-ABI) on one stream: pinned host x/y/metadata "
                                "in, y out"},

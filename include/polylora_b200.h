@@ -50,6 +50,7 @@ extern "C" {
 #define PLORA_DEV_RANK_RANGE 4   /* a rank outside [0, max_rank] was clamped               */
 #define PLORA_DEV_IMAGE_RANGE 8  /* a slot-image record pointed outside the image: rank 0  */
 #define PLORA_DEV_PADDING 16     /* an attention mask was not right-padded                */
+#define PLORA_DEV_TOKEN_RANGE 32 /* a segment-table token id outside [0, num_tokens) skipped */
 
 /* Library version string. */
 const char* plora_version(void);
@@ -221,6 +222,33 @@ int plora_sgmv_shrink_expand(const void* x, const void* lora_a, void* tmp, const
                              const int32_t* slot_start, const int32_t* token_index,
                              int64_t num_tokens, int64_t in_features, int64_t max_rank,
                              int64_t out_features, int32_t num_slots, int32_t dtype,
+                             void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Token rows between host memory and the device, for the tokens of a segment
+ * table only.  No reference counterpart: the reference operators take device
+ * tensors (src/polylora/sgmv.py:141-175, 278-328), so a caller holding host
+ * buffers copies every row in and out.  The LoRA op reads x and the base
+ * output only at the tokens the table lists and updates the base output in
+ * place (the reference's expand adds into y, sgmv.py:278-328), so an in-place
+ * host caller needs just those rows on the bus.
+ *
+ * plora_gather_token_rows copies row t (row_bytes bytes) of host_rows to row t
+ * of device_rows, and plora_scatter_token_rows row t of device_rows to row t of
+ * host_rows, for every token t in token_index[0 : slot_start[num_slots]].
+ * The kernel itself reads or writes the host rows over PCIe, so host_rows must
+ * be page-locked and mapped (cudaHostAlloc, or cudaHostRegister with
+ * cudaHostRegisterMapped; both ends of its num_tokens * row_bytes bytes are
+ * checked with cudaPointerGetAttributes, and pageable memory is refused with
+ * PLORA_ERR_INVALID_ARGUMENT before any launch).  row_bytes: a positive
+ * multiple of 16; both buffers 16-byte aligned.  The table is read on the
+ * device after the preceding work in `stream`; a token id outside [0,
+ * num_tokens) is skipped and sets PLORA_DEV_TOKEN_RANGE. */
+int plora_gather_token_rows(const void* host_rows, void* device_rows, int64_t row_bytes, int64_t num_tokens,
+                            const int32_t* slot_start, const int32_t* token_index, int32_t num_slots,
+                            void* stream);
+int plora_scatter_token_rows(const void* device_rows, void* host_rows, int64_t row_bytes, int64_t num_tokens,
+                             const int32_t* slot_start, const int32_t* token_index, int32_t num_slots,
                              void* stream);
 
 /* ---------------------------------------------------------------------------

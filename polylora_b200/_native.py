@@ -29,6 +29,7 @@ DEV_SLOT_RANGE = 2
 DEV_RANK_RANGE = 4
 DEV_IMAGE_RANGE = 8
 DEV_PADDING = 16
+DEV_TOKEN_RANGE = 32
 
 NOALLOC_SCRATCH_BYTES = 8 << 20  # PLORA_NOALLOC_SCRATCH_BYTES
 
@@ -102,6 +103,14 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "plora_check_right_padded": (
         ctypes.c_int,
         [_c_void_p, _i32, _i32, _c_void_p, _i64, _i64, _c_void_p],
+    ),
+    "plora_gather_token_rows": (
+        ctypes.c_int,
+        [_c_void_p, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i32, _c_void_p],
+    ),
+    "plora_scatter_token_rows": (
+        ctypes.c_int,
+        [_c_void_p, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i32, _c_void_p],
     ),
     "plora_sgmv_a_fwd": (
         ctypes.c_int,
@@ -250,6 +259,33 @@ def check_right_padded(mask, seq_lens, stream=None) -> None:
     check("plora_check_right_padded",
           load().plora_check_right_padded(m.data_ptr(), m.element_size(), is_float, lens.data_ptr(),
                                           m.shape[0], m.shape[1], stream))
+
+
+def token_rows(host, device, table, to_host: bool, stream=None) -> None:
+    """Copies the rows of the table's tokens between a pinned host tensor and
+    a device tensor of the same shape (tokens x row elements; see
+    plora_gather_token_rows / plora_scatter_token_rows): host -> device, or
+    device -> host with ``to_host``.  Other rows are not touched."""
+    import torch
+
+    if host.device.type != "cpu" or device.device.type != "cuda":
+        raise ValueError("token_rows takes a host tensor and a CUDA tensor")
+    if host.shape != device.shape or host.dtype != device.dtype:
+        raise ValueError(f"host {tuple(host.shape)} {host.dtype} and device {tuple(device.shape)} {device.dtype} differ")
+    if not (host.is_contiguous() and device.is_contiguous()):
+        raise ValueError("token_rows needs contiguous tensors")
+    if not host.is_pinned():
+        raise ValueError("the host tensor must be pinned (page-locked) memory")
+    if host.dim() not in (2, 3):
+        raise ValueError("token_rows takes (tokens, row) or (rows, seq, row) tensors")
+    tokens = host.shape[0] * host.shape[1] if host.dim() == 3 else host.shape[0]
+    row_bytes = host.numel() * host.element_size() // max(tokens, 1)
+    if stream is None:
+        stream = torch.cuda.current_stream(device.device).cuda_stream
+    fn = "plora_scatter_token_rows" if to_host else "plora_gather_token_rows"
+    args = (device.data_ptr(), host.data_ptr()) if to_host else (host.data_ptr(), device.data_ptr())
+    check(fn, getattr(load(), fn)(*args, row_bytes, tokens, table.slot_start.data_ptr(),
+                                  table.token_index.data_ptr(), table.num_slots, stream))
 
 
 def workspace_size(num_rows: int, max_seq: int, num_slots: int) -> int:

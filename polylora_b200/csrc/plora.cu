@@ -14,6 +14,7 @@
 #include "segments.cuh"
 #include "sgmv_simt.cuh"
 #include "sgmv_grid.cuh"
+#include "host_rows.cuh"
 #include "sgmv_stream.cuh"
 #include "peft_pack.h"
 
@@ -147,6 +148,12 @@ int device_info(DeviceInfo** out) {
     SET_GRID((sgmv_expand_stream_kernel<false>), kStreamSmemLimit)
     SET_GRID(seg_scan_place_kernel, (kSegScanPlaceMaxInts + kSegMaxSlots + 1) * 4)
 #undef SET_GRID
+    // the row copies use no shared memory; an SM running them keeps its largest
+    // shared-memory carveout, so the segment-table kernels of the next rows of
+    // a host pipeline fit beside them instead of waiting for the SM to drain
+    PLORA_CUDA(cudaFuncSetAttribute(token_rows_copy_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    (int)cudaSharedmemCarveoutMaxShared),
+               "cudaFuncSetAttribute(carveout)");
     d.attrs_set = true;
   }
   *out = &d;
@@ -549,6 +556,73 @@ FwdWorkspace carve_fwd(void* ws, int64_t num_rows, int64_t max_seq, int32_t num_
   return f;
 }
 
+// Device address of `bytes` (> 0) bytes of host memory that a kernel may read
+// and write over PCIe: page-locked and mapped at both ends, as one range.
+int mapped_host_range(const void* p, int64_t bytes, const char* what, const uint8_t** dev) {
+  cudaPointerAttributes a = {}, b = {};
+  const void* last = static_cast<const uint8_t*>(p) + (bytes - 1);
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess || cudaPointerGetAttributes(&b, last) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "%s: pointer attributes unavailable", what);
+  }
+  if (a.type != cudaMemoryTypeHost || b.type != cudaMemoryTypeHost || !a.devicePointer || !b.devicePointer)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "%s must be page-locked, mapped host memory", what);
+  const uint8_t* d0 = static_cast<const uint8_t*>(a.devicePointer);
+  if (static_cast<const uint8_t*>(b.devicePointer) - d0 != bytes - 1)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "%s is not one mapped range", what);
+  *dev = d0;
+  return PLORA_OK;
+}
+
+int device_range(const void* p, int64_t bytes, const char* what) {
+  cudaPointerAttributes a = {}, b = {};
+  const void* last = static_cast<const uint8_t*>(p) + (bytes - 1);
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess || cudaPointerGetAttributes(&b, last) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "%s: pointer attributes unavailable", what);
+  }
+  const bool ok = (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) && a.type == b.type;
+  if (!ok) return fail(PLORA_ERR_INVALID_ARGUMENT, "%s must be device memory", what);
+  return PLORA_OK;
+}
+
+// Both directions of the token-row copy: arguments checked on the host, then
+// one programmatic launch of token_rows_copy_kernel.
+int token_rows_impl(const void* host_rows, void* device_rows, bool to_host, int64_t row_bytes, int64_t num_tokens,
+                    const int32_t* slot_start, const int32_t* token_index, int32_t num_slots, void* stream) {
+  g_last_error.clear();
+  if (row_bytes < 16 || row_bytes % 16 || num_tokens < 0)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "row_bytes must be a positive multiple of 16, num_tokens >= 0");
+  if (num_slots < 1 || num_slots > kSegMaxSlots)
+    return fail(PLORA_ERR_UNSUPPORTED, "num_slots %d outside [1, %d]", num_slots, kSegMaxSlots);
+  if (num_tokens > (int64_t)INT32_MAX) return fail(PLORA_ERR_UNSUPPORTED, "num_tokens exceeds int32 token ids");
+  if (row_bytes > INT64_MAX / std::max<int64_t>(num_tokens, 1))
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "num_tokens * row_bytes overflows");
+  if (num_tokens == 0) return PLORA_OK;
+  if (!host_rows || !device_rows || !slot_start || !token_index)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "null pointer");
+  if (reinterpret_cast<uintptr_t>(host_rows) % 16 || reinterpret_cast<uintptr_t>(device_rows) % 16)
+    return fail(PLORA_ERR_INVALID_ARGUMENT, "row buffers must be 16-byte aligned");
+  const int64_t bytes = num_tokens * row_bytes;
+  const uint8_t* host_dev = nullptr;
+  int st = mapped_host_range(host_rows, bytes, "host_rows", &host_dev);
+  if (st) return st;
+  st = device_range(device_rows, bytes, "device_rows");
+  if (st) return st;
+  DeviceInfo* di = nullptr;
+  st = device_info(&di);
+  if (st) return st;
+  const uint8_t* dev_rows = static_cast<const uint8_t*>(device_rows);
+  const uint8_t* src = to_host ? dev_rows : host_dev;
+  uint8_t* dst = const_cast<uint8_t*>(to_host ? host_dev : dev_rows);
+  // a plain launch: the rows' producers typically finish on another stream (events)
+  PLORA_CUDA(launch_kernel(token_rows_copy_kernel, dim3((unsigned)(2 * di->sm_count)), dim3(kRowsThreads), 0,
+                           static_cast<cudaStream_t>(stream), false, 0, src, dst, row_bytes, num_tokens, slot_start,
+                           token_index, num_slots),
+             "launch token_rows_copy_kernel");
+  return PLORA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -612,6 +686,20 @@ int plora_build_segments(const int64_t* weight_indices, const int32_t* seq_lens,
   return build_segments(weight_indices, seq_lens, lora_ranks, num_rows, max_seq, num_slots,
                         slot_start, token_index, workspace, workspace_size,
                         static_cast<cudaStream_t>(stream));
+}
+
+int plora_gather_token_rows(const void* host_rows, void* device_rows, int64_t row_bytes, int64_t num_tokens,
+                            const int32_t* slot_start, const int32_t* token_index, int32_t num_slots,
+                            void* stream) {
+  return token_rows_impl(host_rows, device_rows, false, row_bytes, num_tokens, slot_start, token_index, num_slots,
+                         stream);
+}
+
+int plora_scatter_token_rows(const void* device_rows, void* host_rows, int64_t row_bytes, int64_t num_tokens,
+                             const int32_t* slot_start, const int32_t* token_index, int32_t num_slots,
+                             void* stream) {
+  return token_rows_impl(host_rows, const_cast<void*>(device_rows), true, row_bytes, num_tokens, slot_start,
+                         token_index, num_slots, stream);
 }
 
 int plora_check_right_padded(const void* mask, int32_t mask_elem_bytes, int32_t mask_is_float,

@@ -14,12 +14,22 @@ result does not depend on the chunking.
 Adapter slot state (weights, ranks, scalings) stays on the device, as in the
 GPU cache; per-row metadata (``seq_lens``, ``weight_indices``) travels with
 the rows.
+
+In place (``out_host`` is ``base_output_host``) with pinned host buffers, only
+the rows the op reads and writes cross the bus: after a chunk's segment table
+is built, a kernel reads x and the base output of the table's tokens from the
+mapped host memory (``plora_gather_token_rows``), and after the op another
+writes those output rows back (``plora_scatter_token_rows``).  Rows of
+``__base__`` or rank-0 tokens, and padding, stay in host memory untouched,
+which is their result (the op leaves them unchanged, as the reference's
+in-place expand does).
 """
 
 from __future__ import annotations
 
 import torch
 
+from . import _native
 from .sgmv import _require_cuda, build_segments, sgmv_shrink_expand
 
 
@@ -33,7 +43,7 @@ class HostLoraPipeline:
     point after the call (e.g. ``torch.cuda.current_stream().synchronize()``).
     """
 
-    def __init__(self, device: torch.device | int | str, chunks: int = 4) -> None:
+    def __init__(self, device: torch.device | int | str, chunks: int = 4, active_rows: bool = True) -> None:
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise RuntimeError("HostLoraPipeline needs a CUDA device; there is no CPU fallback")
@@ -42,6 +52,7 @@ class HostLoraPipeline:
         if chunks < 1:
             raise ValueError(f"chunks must be >= 1, got {chunks}")
         self.chunks = int(chunks)
+        self.active_rows = bool(active_rows)  # in-place pinned calls move the table's rows only
         self.h2d = torch.cuda.Stream(self.device)
         self.d2h = torch.cuda.Stream(self.device)
         self._key = None
@@ -49,6 +60,7 @@ class HostLoraPipeline:
         self._out_free: list[torch.cuda.Event] = []
         self._in_ready: list[torch.cuda.Event] = []
         self._done: list[torch.cuda.Event] = []
+        self._tables_built: list[torch.cuda.Event] = []
 
     def _buffers(self, x_host, base_host, weights_a, seq_host, wi_host):
         B, M, K = x_host.shape
@@ -70,6 +82,7 @@ class HostLoraPipeline:
             self._out_free = [torch.cuda.Event() for _ in range(self.chunks)]
             self._in_ready = [torch.cuda.Event() for _ in range(self.chunks)]
             self._done = [torch.cuda.Event() for _ in range(self.chunks)]
+            self._tables_built = [torch.cuda.Event() for _ in range(self.chunks)]
             self._key = key
         return self._bufs
 
@@ -117,6 +130,10 @@ class HostLoraPipeline:
             return out_host
         bufs = self._buffers(x_host, base_output_host, weights_a, seq_lens_host, weight_indices_host)
         compute = torch.cuda.current_stream(self.device)
+        in_place = out_host.data_ptr() == base_output_host.data_ptr()
+        if self.active_rows and in_place and x_host.is_pinned() and base_output_host.is_pinned():
+            return self._active_rows(x_host, weights_a, weights_b, seq_lens_host, weight_indices_host, lora_ranks,
+                                     scalings, out_host, bufs, compute)
         n = min(self.chunks, B)
         bounds = [B * c // n for c in range(n + 1)]
         for c in range(n):
@@ -134,6 +151,7 @@ class HostLoraPipeline:
             self._in_ready[c].record(self.h2d)
             compute.wait_event(self._in_ready[c])
             table = build_segments(ws, ss, lora_ranks, M)
+            self._tables_built[c].record(compute)  # the metadata buffers are free again
             sgmv_shrink_expand(xs, weights_a, weights_b, ys, table, lora_ranks, scalings, tmp=ts)
             self._done[c].record(compute)
             with torch.cuda.stream(self.d2h):
@@ -142,3 +160,42 @@ class HostLoraPipeline:
                 self._out_free[c].record(self.d2h)
         compute.wait_stream(self.d2h)
         return out_host
+
+    def _active_rows(self, x_host, weights_a, weights_b, seq_host, wi_host, lora_ranks, scalings, y_host, bufs,
+                     compute):
+        """The in-place call moving only the segment table's rows.  Per chunk:
+        on the copy stream the metadata and the chunk's segment table (so that
+        it is built while the previous chunk's rows move); on the compute
+        stream the gather of the table's x and y rows from mapped host memory
+        (after the previous call's scatter of those rows) and the op; on the
+        second stream the scatter of its y rows back."""
+        B, M, _ = x_host.shape
+        n = min(self.chunks, B)
+        bounds = [B * c // n for c in range(n + 1)]
+        for c in range(n):
+            r0, r1 = bounds[c], bounds[c + 1]
+            if r1 == r0:
+                continue
+            xs, ys, ts = bufs["x"][r0:r1], bufs["y"][r0:r1], bufs["tmp"][r0:r1]
+            ss, ws = bufs["seq"][r0:r1], bufs["wi"][r0:r1]
+            with torch.cuda.stream(self.h2d):
+                self.h2d.wait_event(self._tables_built[c])  # the previous call's table read these
+                ss.copy_(seq_host[r0:r1], non_blocking=True)
+                ws.copy_(wi_host[r0:r1], non_blocking=True)
+                table = build_segments(ws, ss, lora_ranks, M)
+                self._tables_built[c].record(self.h2d)
+            compute.wait_event(self._tables_built[c])
+            compute.wait_event(self._out_free[c])  # the previous call's scatter out of these rows
+            for t in (table.slot_start, table.token_index):
+                t.record_stream(compute)
+                t.record_stream(self.d2h)
+            _native.token_rows(x_host[r0:r1], xs, table, to_host=False)
+            _native.token_rows(y_host[r0:r1], ys, table, to_host=False)
+            sgmv_shrink_expand(xs, weights_a, weights_b, ys, table, lora_ranks, scalings, tmp=ts)
+            self._done[c].record(compute)
+            with torch.cuda.stream(self.d2h):
+                self.d2h.wait_event(self._done[c])
+                _native.token_rows(y_host[r0:r1], ys, table, to_host=True, stream=self.d2h.cuda_stream)
+                self._out_free[c].record(self.d2h)
+        compute.wait_stream(self.d2h)
+        return y_host

@@ -196,3 +196,22 @@ def test_stream_kernel_switch_round_trips(native):
         assert native.stream_kernels() == 2
     finally:
         native.stream_kernels(prev)
+
+
+def test_token_rows_arguments_rejected_before_cuda(native):
+    """plora_gather_token_rows / plora_scatter_token_rows check row sizes,
+    counts, slots, nulls and alignment on the host; no tokens returns at once."""
+    lib = native.load()
+    dummy = 0x1000
+    for fn in (lib.plora_gather_token_rows, lib.plora_scatter_token_rows):
+        assert fn(dummy, dummy, 24, 4, dummy, dummy, 1, None) == native.ERR_INVALID_ARGUMENT  # not a multiple of 16
+        assert "multiple of 16" in native.last_error()
+        assert fn(dummy, dummy, 0, 4, dummy, dummy, 1, None) == native.ERR_INVALID_ARGUMENT
+        assert fn(dummy, dummy, 32, -1, dummy, dummy, 1, None) == native.ERR_INVALID_ARGUMENT
+        assert fn(dummy, dummy, 32, 4, dummy, dummy, 0, None) == native.ERR_UNSUPPORTED
+        assert fn(dummy, dummy, 32, 1 << 32, dummy, dummy, 1, None) == native.ERR_UNSUPPORTED
+        assert fn(dummy, dummy, 1 << 40, 1 << 30, dummy, dummy, 1, None) == native.ERR_INVALID_ARGUMENT  # overflow
+        assert fn(None, dummy, 32, 4, dummy, dummy, 1, None) == native.ERR_INVALID_ARGUMENT
+        assert fn(dummy + 8, dummy, 32, 4, dummy, dummy, 1, None) == native.ERR_INVALID_ARGUMENT
+        assert "aligned" in native.last_error()
+        assert fn(None, None, 32, 0, None, None, 1, None) == native.OK
