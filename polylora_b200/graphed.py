@@ -44,8 +44,10 @@ def eager_mask_decisions():
     queries as keys, so that SDPA applies ``is_causal`` itself.  Eager mode
     reaches the same decisions by reading tensor values, which a capture cannot
     do.  Outside a capture, under other tracing, with a padding mask, or on
-    XPU devices the helpers run unchanged.  A no-op without transformers or
-    when its helpers have other names."""
+    XPU devices the helpers run unchanged.  The two helpers are replaced in
+    transformers' module for the duration of the block, so a capture on
+    another thread at the same time gets the same decisions.  A no-op without
+    transformers or when its helpers have other names."""
     try:
         from transformers import masking_utils
         from transformers.utils import import_utils

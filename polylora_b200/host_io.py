@@ -172,6 +172,8 @@ class HostLoraPipeline:
         B, M, _ = x_host.shape
         n = min(self.chunks, B)
         bounds = [B * c // n for c in range(n + 1)]
+        # the tables read lora_ranks on the copy stream: after the caller's work on it
+        self.h2d.wait_stream(compute)
         for c in range(n):
             r0, r1 = bounds[c], bounds[c + 1]
             if r1 == r0:
