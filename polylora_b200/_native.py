@@ -274,6 +274,8 @@ def token_rows(host, device, table, to_host: bool, stream=None) -> None:
         raise ValueError(f"host {tuple(host.shape)} {host.dtype} and device {tuple(device.shape)} {device.dtype} differ")
     if not (host.is_contiguous() and device.is_contiguous()):
         raise ValueError("token_rows needs contiguous tensors")
+    if host.numel() == 0:
+        return
     if not host.is_pinned():
         raise ValueError("the host tensor must be pinned (page-locked) memory")
     if host.dim() not in (2, 3):
